@@ -1,0 +1,362 @@
+#!/usr/bin/env python
+"""Selective-scan fwd+bwd throughput on B200 — the benchmark contract of this repository.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl mamba_b200|reference]
+    torchrun --nproc-per-node N bench.py --gpus N ...          (N > 1, one rank per GPU)
+
+A step is one forward + backward of the selective scan (public operator
+``mamba_b200.selective_scan_fn`` and autograd) over one batch of synthetic inputs at the
+north-star point of BASELINE.json: per GPU batch 8, d_inner 1536, seqlen 2048, d_state 16,
+bf16 u / delta / z / B / C, fp32 A / D / delta_bias, softplus on, SiLU(z) gate.  Inputs per
+step (u, delta, z, dout: 4 x 50 MB) exceed the 126 MB L2, so no flush is needed between
+steps.  N GPUs run N batch shards of a global batch 8N (weak scaling; the scan has no
+exchange, so no collective runs inside the timed region).
+
+Rank 0 prints one JSON line.  ``value`` is tokens/s of the whole job (inputs resident in
+HBM); ``e2e`` is the same metric with pinned-host inputs copied in and all results copied
+out every step; ``roofline`` covers the dominant kernel (the backward scan) with
+algorithmic bytes; ``cpu_baseline`` is the CPU oracle port (oracle/ss_oracle.c, fp32,
+all host threads) on a bounded sample.  ``--impl reference`` times that CPU port alone:
+the reference (nmquan1503/Mamba) has no CPU implementation of its own, and its CUDA
+extension has no bf16 or z support.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, HERE)
+
+METRIC = "selective-scan fwd+bwd tokens/s and HBM GB/s (% of ~8 TB/s peak) at 1/2/4/8 B200"
+PER_GPU = dict(b=8, d=1536, L=2048, n=16)
+
+
+def args_():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="mamba_b200", choices=["mamba_b200", "reference"])
+    ap.add_argument("--e2e-steps", type=int, default=5)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=12.0, help="CPU-baseline sample budget")
+    return ap.parse_args()
+
+
+def algorithmic_bytes(b, d, L, n, es=2):
+    """Bytes the path must move (bf16 I/O, z gate, variable B / C, fp32 dB / dC).
+    fwd: read u, delta, z; write out            -> 4 es per element; B, C -> 2 n es per token
+    bwd: read u, delta, z, dout; write du, ddelta, dz -> 7 es per element;
+         read B, C (2 n es) and write dB, dC fp32 (2 n 4) per token."""
+    elems, tokens = b * d * L, b * L
+    fwd = elems * 4 * es + tokens * 2 * n * es
+    bwd = elems * 7 * es + tokens * (2 * n * es + 2 * n * 4)
+    return fwd, bwd
+
+
+def load_peaks():
+    p = os.path.join(HERE, "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            j = json.load(f)
+        return float(j["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def profile_traffic():
+    """dram bytes per backward launch from the committed ncu summary, if present."""
+    p = os.path.join(HERE, "profiles", "ss_bwd_north_traffic.txt")
+    try:
+        for line in open(p):
+            if line.startswith("bytes_per_launch_full"):
+                return float(line.split("=")[1])
+    except OSError:
+        pass
+    return None
+
+
+# ----------------------------------------------------------------------------- clocks
+class ClockSampler:
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        self.out = ""
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                self.out, _ = self.proc.communicate()
+        return False
+
+    def summary(self):
+        rows = []
+        for line in (self.out or "").strip().splitlines():
+            p = [x.strip() for x in line.split(",")]
+            if len(p) < 8:
+                continue
+            try:
+                rows.append((float(p[0]), float(p[1]), p[4:8]))
+            except ValueError:
+                continue
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for _, _, r in rows for i, v in enumerate(r) if v.lower() == "active"})
+        return {"sm_mhz": statistics.median(r[0] for r in rows), "sm_max_mhz": max(r[1] for r in rows),
+                "reasons": reasons, "samples": len(rows)}
+
+
+# ----------------------------------------------------------------------------- inputs
+def make_inputs(b, d, L, n, seed, device):
+    import torch
+
+    g = torch.Generator().manual_seed(seed)
+    rn = lambda *s: torch.randn(*s, generator=g, dtype=torch.float32)
+    dt = torch.exp(torch.rand(d, generator=g) * (math.log(0.1) - math.log(1e-3)) + math.log(1e-3)).clamp(min=1e-4)
+    host = dict(
+        u=rn(b, d, L).bfloat16(), delta=(0.5 * rn(b, d, L)).bfloat16(), z=rn(b, d, L).bfloat16(),
+        B=rn(b, 1, n, L).bfloat16(), C=rn(b, 1, n, L).bfloat16(), dout=rn(b, d, L).bfloat16(),
+        A=-torch.arange(1, n + 1, dtype=torch.float32).repeat(d, 1), D=torch.ones(d),
+        delta_bias=dt + torch.log(-torch.expm1(-dt)))
+    return host
+
+
+# ----------------------------------------------------------------------------- cpu legs
+def cpu_sample_rate(n_full_elems, tokens_full, budget_s, seed=0):
+    """Time the fp32 CPU oracle port (fwd + bwd, all host threads) on a slice of the
+    workload sized to ~budget_s, and extrapolate to tokens/s of the full workload."""
+    import torch
+    from oracle import oracle as O
+
+    d_full, L, n = PER_GPU["d"], PER_GPU["L"], PER_GPU["n"]
+
+    def run(dsl):
+        h = make_inputs(1, dsl, L, n, seed, "cpu")
+        t = time.perf_counter()
+        O.selective_scan_ref(h["u"], h["delta"], h["A"], h["B"], h["C"], h["D"], h["z"], h["delta_bias"], True,
+                             precision="f32")
+        O.selective_scan_ref_bwd(h["u"], h["delta"], h["A"], h["B"], h["C"], h["D"], h["z"], h["delta_bias"], True,
+                                 h["dout"], precision="f32")
+        return time.perf_counter() - t
+
+    threads = O.max_threads()
+    t_cal = run(8)
+    dsl = int(min(d_full, max(8, 8 * budget_s / max(t_cal, 1e-3))))
+    dsl = max(8, dsl - dsl % 8)
+    t = run(dsl)
+    elems = dsl * L
+    rate_elems = elems / t
+    value = tokens_full / (n_full_elems / rate_elems)
+    return value, threads, f"batch 1 x {dsl} channels x {L} steps (fwd+bwd, fp32 port) in {t:.2f} s", t
+
+
+def reference_arm(a, world, rank):
+    if rank != 0:
+        return 0
+    b, d, L, n = PER_GPU["b"] * world, PER_GPU["d"], PER_GPU["L"], PER_GPU["n"]
+    elems, tokens = b * d * L, b * L
+    per_step_budget = max(1.0, 120.0 / max(1, a.steps + a.warmup))
+    vals = []
+    sample = threads = None
+    for i in range(a.warmup + a.steps):
+        v, threads, sample, _ = cpu_sample_rate(elems, tokens, per_step_budget, seed=i)
+        if i >= a.warmup:
+            vals.append(v)
+    value = statistics.median(vals)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
+        "steps": a.steps, "warmup": a.warmup, "ms_per_step": 1e3 * tokens / value, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": config_dict(world),
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "port",
+                         "sample": f"per step: {sample}; extrapolated to the workload's elements"},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "note": "the reference has no CPU implementation; this is the CPU restatement of its "
+                "algorithm (oracle/ss_oracle.c) with OpenMP over channels",
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def config_dict(world):
+    b = PER_GPU["b"]
+    return {"workload": "selective_scan fwd+bwd, batch 8 per GPU, d_inner 1536, seqlen 2048, d_state 16, "
+                        "bf16 I/O + fp32 state, z gate, softplus (north-star point)",
+            "global_batch": b * world, "per_gpu_batch": b, "d_inner": PER_GPU["d"], "seq_len": PER_GPU["L"],
+            "d_state": PER_GPU["n"], "parallelism": f"batch-sharded x{world}, no collective in the path",
+            "l2": "inputs larger than L2 (200 MB per step of u/delta/z/dout)"}
+
+
+# ----------------------------------------------------------------------------- gpu arm
+def main():
+    a = args_()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if a.impl == "reference":
+        return reference_arm(a, world, rank)
+    if a.warmup < 3:
+        a.warmup = 3
+
+    import torch
+    import torch.distributed as dist
+
+    import mamba_b200
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=180))
+
+    b, d, L, n = PER_GPU["b"], PER_GPU["d"], PER_GPU["L"], PER_GPU["n"]
+    host = make_inputs(b, d, L, n, seed=1000 + rank, device="cpu")
+    x = {k: v.to(dev) for k, v in host.items()}
+    leaves = ["u", "delta", "A", "B", "C", "D", "z", "delta_bias"]
+    for k in leaves:
+        x[k].requires_grad_(True)
+
+    def step(t):
+        out = mamba_b200.selective_scan_fn(t["u"], t["delta"], t["A"], t["B"], t["C"], t["D"], t["z"],
+                                           t["delta_bias"], True)
+        return out
+
+    def clear(t):
+        for k in leaves:
+            t[k].grad = None
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    for _ in range(a.warmup):
+        out = step(x)
+        out.backward(x["dout"])
+        clear(x)
+    torch.cuda.synchronize()
+
+    K = a.steps
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(K)]
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clk:
+        t0.record()
+        for i in range(K):
+            ev[i][0].record()
+            out = step(x)
+            ev[i][1].record()
+            out.backward(x["dout"])
+            ev[i][2].record()
+            clear(x)
+        t1.record()
+        torch.cuda.synchronize()
+        barrier()
+    elapsed = t0.elapsed_time(t1)  # ms
+    fwd_ms = statistics.mean(e[0].elapsed_time(e[1]) for e in ev)
+    bwd_ms = statistics.mean(e[1].elapsed_time(e[2]) for e in ev)
+    if world > 1:
+        tt = torch.tensor([elapsed], device=dev, dtype=torch.float64)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        elapsed = float(tt.item())
+    ms_step = elapsed / K
+    tokens_job = b * L * world
+    value = tokens_job / (ms_step / 1e3)
+
+    # ---- end to end: pinned host inputs in, every result out, through the public operator
+    pin = {k: v.pin_memory() for k, v in host.items()}
+    dbuf = {k: torch.empty_like(v, device=dev) for k, v in host.items()}
+    outs_host = None
+    E = max(1, a.e2e_steps)
+    h2d = sum(v.numel() * v.element_size() for k, v in pin.items() if k in ("u", "delta", "z", "B", "C", "dout"))
+    barrier()
+    torch.cuda.synchronize()
+    s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    d2h = 0
+    for i in range(E + 1):  # first iteration warms the pinned output buffers
+        if i == 1:
+            torch.cuda.synchronize()
+            s0.record()
+        for k in ("u", "delta", "z", "B", "C", "dout", "A", "D", "delta_bias"):
+            dbuf[k].copy_(pin[k], non_blocking=True)
+        t = {k: dbuf[k].detach().requires_grad_(k in leaves) for k in dbuf}
+        out = step(t)
+        out.backward(t["dout"])
+        res = [out.detach()] + [t[k].grad for k in leaves]
+        if outs_host is None:
+            outs_host = [torch.empty(r.shape, dtype=r.dtype, pin_memory=True) for r in res]
+        for hbuf, r in zip(outs_host, res):
+            hbuf.copy_(r, non_blocking=True)
+        d2h = sum(r.numel() * r.element_size() for r in res)
+    s1.record()
+    torch.cuda.synchronize()
+    e2e_ms = s0.elapsed_time(s1) / E
+    if world > 1:
+        tt = torch.tensor([e2e_ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        e2e_ms = float(tt.item())
+    e2e_value = tokens_job / (e2e_ms / 1e3)
+
+    if world > 1:
+        dist.destroy_process_group()
+    if rank != 0:
+        return 0
+
+    fwd_bytes, bwd_bytes = algorithmic_bytes(b, d, L, n)
+    peak, peak_kind = load_peaks()
+    dom_ms, dom_bytes, dom = (bwd_ms, bwd_bytes, "ss_bwd_kernel") if bwd_ms >= fwd_ms else (fwd_ms, fwd_bytes, "ss_fwd_kernel")
+    achieved = dom_bytes / (dom_ms / 1e3) / 1e9
+    step_gbs = (fwd_bytes + bwd_bytes) / (ms_step / 1e3) / 1e9
+    line = {
+        "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": K, "warmup": a.warmup,
+        "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "bf16", "data": "synthetic", "config": config_dict(world),
+        "hbm_gbs_step": step_gbs, "hbm_frac_step": step_gbs / peak, "hbm_frac_step_nominal_8tbs": step_gbs / 8000.0,
+        "kernels_ms": {"fwd": fwd_ms, "bwd": bwd_ms},
+        "roofline": {"kernel": dom, "bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                     "frac": achieved / peak, "peak_source": peak_kind,
+                     "algorithmic_bytes_per_launch": dom_bytes, "traffic": profile_traffic()},
+        "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                "ms_per_step": e2e_ms},
+        "gpu_launches": 2 * K,
+        "clocks": clk.summary(),
+    }
+    if world == 1 and not a.no_cpu_baseline:
+        try:
+            v, thr, sample, _ = cpu_sample_rate(b * d * L, b * L, a.cpu_seconds)
+            line["cpu_baseline"] = {"value": v, "unit": "tokens/s", "cores": thr, "kind": "port", "sample": sample}
+        except Exception as e:  # the baseline is reported, never required
+            line["cpu_baseline"] = {"value": None, "unit": "tokens/s", "cores": None, "kind": "port",
+                                    "sample": f"failed: {e!r}"}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,139 @@
+/*
+ * mamba_b200 selective scan — C ABI of libmamba_b200_ss.so (sm_100a).
+ *
+ * Plain pointers and sizes only.  Every call is asynchronous on the given CUDA stream
+ * (a cudaStream_t passed as void*; NULL = legacy default stream) and returns an
+ * ss_status.  Device pointers must belong to the current device.
+ *
+ * Reference interfaces these entry points replace (nmquan1503/Mamba):
+ *   ss_fwd  <- selective_scan.forward(u, delta, A, B, C, D?, delta_bias?, use_delta_softplus)
+ *              -> [out, x]          csrc/selective_scan/selective_scan.cpp:184-244, :331-334
+ *              (kernel launcher forward_kernel_launch, forward_kernel.cu:313-333)
+ *   ss_bwd  <- selective_scan.backward(u, delta, A, B, C, D?, delta_bias?, dout, x?, flag)
+ *              -> [du, ddelta, dA, dB, dC, dD, ddelta_bias]
+ *                                   csrc/selective_scan/selective_scan.cpp:246-329, :331-334
+ *              (kernel launcher backward_kernel_launch, backward_kernel.cu:588-618)
+ *   ss_step <- no counterpart: the reference has no decode step (models/causal_lm.py:61-62
+ *              is a stub).  It is one step of the same recurrence from a stored state.
+ *
+ * Tensor layouts (element strides; the innermost sequence axis must have stride 1):
+ *   u, delta, z, out, dout, du, ddelta, dz : (batch, dim, seqlen), batch/dim strides given
+ *   A, dA                                  : (dim, dstate) contiguous, fp32
+ *   B, C   variable                        : (batch, ngroups, dstate, seqlen) contiguous
+ *   B, C   constant                        : (dim, dstate) contiguous
+ *   dB, dC                                 : same shape as B, C, always fp32
+ *   D, delta_bias, dD, ddelta_bias         : (dim) fp32
+ *   ckpt                                   : opaque fp32 buffer of ss_ckpt_elems() floats;
+ *                                            written by ss_fwd, read by ss_bwd
+ *   last_state                             : (batch, dim, dstate) fp32
+ * Channel c uses group c / (dim / ngroups), as forward_kernel.cu:144 of the reference.
+ */
+#ifndef MAMBA_B200_SS_H
+#define MAMBA_B200_SS_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define SS_ABI_VERSION 1
+#define SS_MAX_DSTATE 16
+
+#if defined(__GNUC__)
+#define SS_API __attribute__((visibility("default")))
+#else
+#define SS_API
+#endif
+
+typedef enum ss_dtype { SS_F32 = 0, SS_BF16 = 1, SS_F16 = 2 } ss_dtype;
+
+typedef enum ss_status {
+  SS_OK = 0,
+  SS_ERR_INVALID = 1,     /* null pointer, bad size, bad stride, dim % ngroups != 0 */
+  SS_ERR_UNSUPPORTED = 2, /* dtype combination or dstate > SS_MAX_DSTATE */
+  SS_ERR_CUDA = 3         /* a CUDA runtime call or kernel launch failed */
+} ss_status;
+
+typedef struct ss_fwd_args {
+  int batch, dim, seqlen, dstate, ngroups;
+  int var_B, var_C;         /* 1: (batch, ngroups, dstate, seqlen); 0: (dim, dstate)      */
+  int delta_softplus;       /* delta' = softplus(delta + delta_bias), threshold 20        */
+  int io_dtype;             /* ss_dtype of u, delta, z, out                               */
+  int bc_dtype;             /* ss_dtype of B, C: SS_F32 or io_dtype                       */
+  const void* u;     int64_t u_batch_stride, u_dim_stride;
+  const void* delta; int64_t delta_batch_stride, delta_dim_stride;
+  const float* A;
+  const void* B;
+  const void* C;
+  const float* D;           /* nullable: D = 0                                            */
+  const void* z;     int64_t z_batch_stride, z_dim_stride;  /* nullable: no gate          */
+  const float* delta_bias;  /* nullable: bias = 0                                         */
+  void* out;         int64_t out_batch_stride, out_dim_stride; /* y or y * silu(z)        */
+  float* ckpt;              /* nullable: skip the states the backward needs               */
+  float* last_state;        /* nullable                                                   */
+} ss_fwd_args;
+
+typedef struct ss_bwd_args {
+  ss_fwd_args f;            /* the forward's inputs; f.out, f.last_state are ignored;
+                               f.ckpt must hold what ss_fwd wrote for the same inputs     */
+  const void* dout;  int64_t dout_batch_stride, dout_dim_stride;
+  void* du;          int64_t du_batch_stride, du_dim_stride;
+  void* ddelta;      int64_t ddelta_batch_stride, ddelta_dim_stride;
+  void* dz;          int64_t dz_batch_stride, dz_dim_stride;   /* required iff f.z       */
+  float* dA;                /* overwritten (zeroed, then accumulated)                     */
+  float* dB;                /* overwritten                                                */
+  float* dC;                /* overwritten                                                */
+  float* dD;                /* nullable; overwritten                                      */
+  float* ddelta_bias;       /* nullable; overwritten                                      */
+} ss_bwd_args;
+
+typedef struct ss_step_args {
+  int batch, dim, dstate, ngroups;
+  int dt_softplus;
+  int io_dtype;             /* dtype of x, dt, z, out                                     */
+  int bc_dtype;             /* dtype of B, C: SS_F32 or io_dtype                          */
+  float* state;      int64_t state_batch_stride;  /* (batch, dim, dstate) fp32, in/out    */
+  const void* x;     int64_t x_batch_stride;      /* (batch, dim)                         */
+  const void* dt;    int64_t dt_batch_stride;     /* (batch, dim)                         */
+  const float* A;                                 /* (dim, dstate)                        */
+  const void* B;                                  /* (batch, ngroups, dstate) contiguous  */
+  const void* C;
+  const float* D;                                 /* nullable                             */
+  const void* z;     int64_t z_batch_stride;      /* nullable                             */
+  const float* dt_bias;                           /* nullable                             */
+  void* out;         int64_t out_batch_stride;    /* (batch, dim)                         */
+} ss_step_args;
+
+/* Number of fp32 elements of the forward-to-backward state buffer. */
+SS_API size_t ss_ckpt_elems(int batch, int dim, int seqlen, int dstate);
+
+/* Forward scan: out = (D*u + sum_n C*h) [* silu(z)], h_t = exp(delta'*A) h_{t-1} + delta'*u*B. */
+SS_API int ss_fwd(const ss_fwd_args* args, void* stream);
+
+/* Backward scan: all input gradients from dout, using the forward's ckpt. */
+SS_API int ss_bwd(const ss_bwd_args* args, void* stream);
+
+/* One decode step: state <- exp(dt'*A) state + dt'*x*B; out = (C.state + D x) [* silu(z)]. */
+SS_API int ss_step(const ss_step_args* args, void* stream);
+
+/* Static description of a status code. */
+SS_API const char* ss_status_string(int status);
+
+/* The CUDA error (cudaError_t as int) behind the last SS_ERR_CUDA on this thread. */
+SS_API int ss_last_cuda_error(void);
+
+/* SS_ABI_VERSION of the loaded library. */
+SS_API int ss_abi_version(void);
+
+/* sizeof the argument structs as compiled into the library (0: ss_fwd_args,
+ * 1: ss_bwd_args, 2: ss_step_args; 0 for other values) — lets an FFI binding check
+ * its own struct layout against the library's. */
+SS_API size_t ss_struct_size(int which);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MAMBA_B200_SS_H */

@@ -1,0 +1,135 @@
+"""ctypes binding of libmamba_b200_ss.so (declared in include/mamba_b200_ss.h).
+
+The library is the product's only compute path: there is no CPU or PyTorch fallback.
+Loading fails loudly if the library was not built, and every call checks that its
+tensors are CUDA tensors on one device.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+
+import torch
+
+_PKG = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_PKG, "libmamba_b200_ss.so")
+
+SS_F32, SS_BF16, SS_F16 = 0, 1, 2
+SS_OK, SS_ERR_INVALID, SS_ERR_UNSUPPORTED, SS_ERR_CUDA = 0, 1, 2, 3
+SS_MAX_DSTATE = 16
+TILE = 16  # time steps between checkpoints (kTile in csrc/ss_common.cuh)
+
+_DTYPES = {torch.float32: SS_F32, torch.bfloat16: SS_BF16, torch.float16: SS_F16}
+
+c_int, c_i64, c_vp = ctypes.c_int, ctypes.c_int64, ctypes.c_void_p
+
+
+class FwdArgs(ctypes.Structure):
+    _fields_ = [
+        ("batch", c_int), ("dim", c_int), ("seqlen", c_int), ("dstate", c_int), ("ngroups", c_int),
+        ("var_B", c_int), ("var_C", c_int), ("delta_softplus", c_int), ("io_dtype", c_int),
+        ("bc_dtype", c_int),
+        ("u", c_vp), ("u_batch_stride", c_i64), ("u_dim_stride", c_i64),
+        ("delta", c_vp), ("delta_batch_stride", c_i64), ("delta_dim_stride", c_i64),
+        ("A", c_vp), ("B", c_vp), ("C", c_vp), ("D", c_vp),
+        ("z", c_vp), ("z_batch_stride", c_i64), ("z_dim_stride", c_i64),
+        ("delta_bias", c_vp),
+        ("out", c_vp), ("out_batch_stride", c_i64), ("out_dim_stride", c_i64),
+        ("ckpt", c_vp), ("last_state", c_vp),
+    ]
+
+
+class BwdArgs(ctypes.Structure):
+    _fields_ = [
+        ("f", FwdArgs),
+        ("dout", c_vp), ("dout_batch_stride", c_i64), ("dout_dim_stride", c_i64),
+        ("du", c_vp), ("du_batch_stride", c_i64), ("du_dim_stride", c_i64),
+        ("ddelta", c_vp), ("ddelta_batch_stride", c_i64), ("ddelta_dim_stride", c_i64),
+        ("dz", c_vp), ("dz_batch_stride", c_i64), ("dz_dim_stride", c_i64),
+        ("dA", c_vp), ("dB", c_vp), ("dC", c_vp), ("dD", c_vp), ("ddelta_bias", c_vp),
+    ]
+
+
+class StepArgs(ctypes.Structure):
+    _fields_ = [
+        ("batch", c_int), ("dim", c_int), ("dstate", c_int), ("ngroups", c_int),
+        ("dt_softplus", c_int), ("io_dtype", c_int), ("bc_dtype", c_int),
+        ("state", c_vp), ("state_batch_stride", c_i64),
+        ("x", c_vp), ("x_batch_stride", c_i64),
+        ("dt", c_vp), ("dt_batch_stride", c_i64),
+        ("A", c_vp), ("B", c_vp), ("C", c_vp), ("D", c_vp),
+        ("z", c_vp), ("z_batch_stride", c_i64),
+        ("dt_bias", c_vp),
+        ("out", c_vp), ("out_batch_stride", c_i64),
+    ]
+
+
+EXPORTS = ("ss_fwd", "ss_bwd", "ss_step", "ss_ckpt_elems", "ss_status_string",
+           "ss_last_cuda_error", "ss_abi_version", "ss_struct_size")
+
+_lib = None
+_lock = threading.Lock()
+
+
+def lib():
+    """Load the library once.  Raises if it is missing (no fallback exists)."""
+    global _lib
+    if _lib is None:
+        with _lock:
+            if _lib is None:
+                if not os.path.exists(LIB_PATH):
+                    raise RuntimeError(
+                        f"{LIB_PATH} is not built; run `python -m mamba_b200.build` "
+                        "(mamba_b200 has no CPU fallback)")
+                L = ctypes.CDLL(LIB_PATH)
+                L.ss_fwd.argtypes = [ctypes.POINTER(FwdArgs), c_vp]
+                L.ss_bwd.argtypes = [ctypes.POINTER(BwdArgs), c_vp]
+                L.ss_step.argtypes = [ctypes.POINTER(StepArgs), c_vp]
+                for f in ("ss_fwd", "ss_bwd", "ss_step", "ss_last_cuda_error", "ss_abi_version"):
+                    getattr(L, f).restype = c_int
+                L.ss_ckpt_elems.argtypes = [c_int, c_int, c_int, c_int]
+                L.ss_ckpt_elems.restype = ctypes.c_size_t
+                L.ss_status_string.argtypes = [c_int]
+                L.ss_status_string.restype = ctypes.c_char_p
+                L.ss_struct_size.argtypes = [c_int]
+                L.ss_struct_size.restype = ctypes.c_size_t
+                for i, st in enumerate((FwdArgs, BwdArgs, StepArgs)):
+                    if L.ss_struct_size(i) != ctypes.sizeof(st):
+                        raise RuntimeError(f"{LIB_PATH}: struct {st.__name__} layout mismatch "
+                                           f"({L.ss_struct_size(i)} != {ctypes.sizeof(st)} bytes)")
+                _lib = L
+    return _lib
+
+
+def check(rc: int, what: str) -> None:
+    if rc == SS_OK:
+        return
+    L = lib()
+    msg = L.ss_status_string(rc).decode()
+    if rc == SS_ERR_CUDA:
+        msg += f" (cudaError {L.ss_last_cuda_error()})"
+    if rc == SS_ERR_UNSUPPORTED:
+        raise NotImplementedError(f"{what}: {msg}")
+    if rc == SS_ERR_INVALID:
+        raise ValueError(f"{what}: {msg}")
+    raise RuntimeError(f"{what}: {msg}")
+
+
+def dtype_code(t: torch.dtype) -> int:
+    try:
+        return _DTYPES[t]
+    except KeyError:
+        raise NotImplementedError(f"dtype {t} is not supported (float32, bfloat16, float16)") from None
+
+
+def ptr(t):
+    return None if t is None else t.data_ptr()
+
+
+def stream_of(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def ckpt_elems(batch, dim, seqlen, dstate) -> int:
+    return int(lib().ss_ckpt_elems(batch, dim, seqlen, dstate))

@@ -1,0 +1,220 @@
+// Shared device helpers for the sm_100a selective-scan kernels.
+//
+// Work decomposition used by every kernel here:
+//   * one CTA owns one batch row b and a tile of 32 channels of one group (lane = channel);
+//   * warp w owns states 4w .. 4w+3 of those channels, so a CTA has ceil(dstate/4)
+//     warps (1, 2 or 4; dstate <= 16);
+//   * time advances in tiles of kTile = 16 steps; each lane carries its 4 states in
+//     registers across tiles, so the whole sequence is scanned without any cross-thread
+//     scan (the reference runs a CUB block scan per state per 128-token chunk,
+//     forward_kernel.cu:274-286);
+//   * the forward writes the states at every tile boundary (the checkpoint buffer,
+//     the counterpart of the reference's per-chunk carry x, forward_kernel.cu:171-172,
+//     :285) so the backward can restart any tile without a second forward scan.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <stdint.h>
+
+#include "../../include/mamba_b200_ss.h"
+
+namespace ssb {
+
+constexpr int kTile = 16;   // time steps per tile = checkpoint interval
+constexpr int kCh = 32;     // channels per CTA (one per lane)
+constexpr int kSPW = 4;     // states per warp
+constexpr int kPad = 34;    // row stride (floats) of the [t][channel] partial-sum arrays
+constexpr float kLog2e = 1.4426950408889634f;
+
+// ---- scalar conversions -----------------------------------------------------------
+template <typename T> __device__ __forceinline__ float to_f(T x);
+template <> __device__ __forceinline__ float to_f<float>(float x) { return x; }
+template <> __device__ __forceinline__ float to_f<__nv_bfloat16>(__nv_bfloat16 x) { return __bfloat162float(x); }
+template <> __device__ __forceinline__ float to_f<__half>(__half x) { return __half2float(x); }
+
+template <typename T> __device__ __forceinline__ T from_f(float x);
+template <> __device__ __forceinline__ float from_f<float>(float x) { return x; }
+template <> __device__ __forceinline__ __nv_bfloat16 from_f<__nv_bfloat16>(float x) { return __float2bfloat16_rn(x); }
+template <> __device__ __forceinline__ __half from_f<__half>(float x) { return __float2half_rn(x); }
+
+template <typename T> __device__ __forceinline__ T zero_v() { return from_f<T>(0.f); }
+
+// ---- transcendental helpers (hardware approximations, as the reference's fast-math build) --
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+__device__ __forceinline__ float fast_rcp(float x) {
+  float y;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+// e^x via ex2 with a log2(e) prescale
+__device__ __forceinline__ float exp_fast(float x) { return ex2(x * kLog2e); }
+// 1 / (1 + e^-x)
+__device__ __forceinline__ float sigmoid_fast(float x) { return fast_rcp(1.f + exp_fast(-x)); }
+// delta' = softplus(v) with the reference's threshold (forward_kernel.cu:216-221):
+// log1p(exp(v)) for v <= 20, v otherwise.  log1pf keeps full precision for small e^v.
+__device__ __forceinline__ float softplus_thr(float v) { return v <= 20.f ? log1pf(exp_fast(v)) : v; }
+
+// ---- memory helpers -------------------------------------------------------------------
+__device__ __forceinline__ uint4 ld_stream16(const void* p) {
+  uint4 r;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "l"(p));
+  return r;
+}
+__device__ __forceinline__ void red_add_v4(float* p, float a, float b, float c, float d) {
+  asm volatile("red.global.add.v4.f32 [%0], {%1,%2,%3,%4};" ::"l"(p), "f"(a), "f"(b), "f"(c), "f"(d)
+               : "memory");
+}
+__device__ __forceinline__ void red_add_v2(float* p, float a, float b) {
+  asm volatile("red.global.add.v2.f32 [%0], {%1,%2};" ::"l"(p), "f"(a), "f"(b) : "memory");
+}
+__device__ __forceinline__ void red_add(float* p, float a) { atomicAdd(p, a); }
+
+// Copy a (32 channels x kTile steps) tile of a (.., dim, seqlen) tensor into shared memory
+// as dst[channel][t] (row-major, no padding).  Rows >= nrows and steps >= tlen read as 0.
+// vec: the tile's rows start 16-byte aligned (checked on the host), so whole rows move as
+// 16-byte vectors when the tile is full.
+template <typename T, int NT>
+__device__ __forceinline__ void load_tile(T (*dst)[kTile], const T* __restrict__ src, int64_t row_stride,
+                                          int nrows, int tlen, bool vec) {
+  constexpr int EPV = 16 / sizeof(T);  // elements per 16-byte vector
+  constexpr int VPR = kTile / EPV;     // vectors per row
+  if (vec && tlen == kTile) {
+#pragma unroll
+    for (int i = threadIdx.x; i < kCh * VPR; i += NT) {
+      const int r = i / VPR, v = i % VPR;
+      uint4 val = make_uint4(0u, 0u, 0u, 0u);
+      if (r < nrows) val = ld_stream16(src + (int64_t)r * row_stride + v * EPV);
+      *reinterpret_cast<uint4*>(&dst[r][v * EPV]) = val;
+    }
+  } else {
+    for (int i = threadIdx.x; i < kCh * kTile; i += NT) {
+      const int r = i / kTile, t = i % kTile;
+      T val = zero_v<T>();
+      if (r < nrows && t < tlen) val = src[(int64_t)r * row_stride + t];
+      dst[r][t] = val;
+    }
+  }
+}
+
+// Copy the (dstate x kTile) slice of a variable B or C row block (stride seqlen between
+// states) into dst[t][n] as fp32, zero-filled for n >= dstate or t >= tlen.
+template <typename T, int NT, int NS>
+__device__ __forceinline__ void load_bc_tile(float (*dst)[NS], const T* __restrict__ src, int64_t seqlen,
+                                             int dstate, int tlen) {
+  for (int i = threadIdx.x; i < NS * kTile; i += NT) {
+    const int n = i / kTile, t = i % kTile;
+    float v = 0.f;
+    if (n < dstate && t < tlen) v = to_f<T>(src[(int64_t)n * seqlen + t]);
+    dst[t][n] = v;
+  }
+}
+
+// Swizzled [32 rows][4 float4 chunks] layout: chunk q of row r lives at q ^ ((r >> 1) & 3),
+// which makes both "lane r reads its chunk i" and "lanes write consecutive chunks"
+// conflict-free for 16-byte shared-memory accesses.
+__device__ __forceinline__ int swz(int r, int q) { return q ^ ((r >> 1) & 3); }
+
+// Store S consecutive values of one row of a (.., dim, seqlen) tensor (S = 4, 8 or 16),
+// vectorized when aligned and complete.
+template <typename T, int S>
+__device__ __forceinline__ void store_run(T* __restrict__ dst, const float (&v)[S], int nvalid, bool vec) {
+  if (vec && nvalid == S && (S * sizeof(T)) % 8 == 0) {
+    if constexpr (S * sizeof(T) % 16 == 0) {
+#pragma unroll
+      for (int i = 0; i < S; i += 16 / sizeof(T)) {
+        union { uint4 u; T e[16 / sizeof(T)]; } pk;
+#pragma unroll
+        for (int k = 0; k < 16 / (int)sizeof(T); ++k) pk.e[k] = from_f<T>(v[i + k]);
+        *reinterpret_cast<uint4*>(dst + i) = pk.u;
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < S; i += 8 / sizeof(T)) {
+        union { uint2 u; T e[8 / sizeof(T)]; } pk;
+#pragma unroll
+        for (int k = 0; k < 8 / (int)sizeof(T); ++k) pk.e[k] = from_f<T>(v[i + k]);
+        *reinterpret_cast<uint2*>(dst + i) = pk.u;
+      }
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < S; ++i)
+      if (i < nvalid) dst[i] = from_f<T>(v[i]);
+  }
+}
+
+// Warp-wide transpose-reduction of per-step dB / dC contributions (a butterfly over the 32
+// lanes = channels).  Conceptually lane l holds K values v[type*64 + j*16 + t] (type 0 = B,
+// 1 = C; state j of the warp; step t of the tile), and after the five stages lane l holds
+// the sums over all lanes of entries (K/32)*l + i.  The stages whose pairs share a step run
+// inside the step loop (fold_step_*), the last ones once per tile (fold_tile), so at most
+// one partial per step stays live.
+__device__ __forceinline__ float bfly(float keep, float send, int o) {
+  return keep + __shfl_xor_sync(0xffffffffu, send, o);
+}
+// both B and C variable: stages with offsets 16 (B vs C), 8 (j vs j+2), 4 (j vs j+1)
+__device__ __forceinline__ float fold_step_bc(const float (&vB)[4], const float (&vC)[4], int lane) {
+  const bool u16 = lane & 16, u8 = lane & 8, u4 = lane & 4;
+  float x[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) x[j] = bfly(u16 ? vC[j] : vB[j], u16 ? vB[j] : vC[j], 16);
+  float y[2];
+#pragma unroll
+  for (int j = 0; j < 2; ++j) y[j] = bfly(u8 ? x[j + 2] : x[j], u8 ? x[j] : x[j + 2], 8);
+  return bfly(u4 ? y[1] : y[0], u4 ? y[0] : y[1], 4);
+}
+// only one of B, C variable: stages with offsets 16 (j vs j+2), 8 (j vs j+1)
+__device__ __forceinline__ float fold_step_one(const float (&v)[4], int lane) {
+  const bool u16 = lane & 16, u8 = lane & 8;
+  float y[2];
+#pragma unroll
+  for (int j = 0; j < 2; ++j) y[j] = bfly(u16 ? v[j + 2] : v[j], u16 ? v[j] : v[j + 2], 16);
+  return bfly(u8 ? y[1] : y[0], u8 ? y[0] : y[1], 8);
+}
+// remaining stages over the 16 per-step partials W[t]; PER = 4 (offsets 2, 1: lane keeps
+// steps 4*(lane&3) ..) or PER = 2 (offsets 4, 2, 1: lane keeps steps 2*(lane&7) ..)
+template <int PER>
+__device__ __forceinline__ void fold_tile(const float (&W)[16], float (&out)[PER], int lane) {
+  if constexpr (PER == 4) {
+    const bool u2 = lane & 2, u1 = lane & 1;
+    float a[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) a[i] = bfly(u2 ? W[i + 8] : W[i], u2 ? W[i] : W[i + 8], 2);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) out[i] = bfly(u1 ? a[i + 4] : a[i], u1 ? a[i] : a[i + 4], 1);
+  } else {
+    const bool u4 = lane & 4, u2 = lane & 2, u1 = lane & 1;
+    float a[8], b2[4];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) a[i] = bfly(u4 ? W[i + 8] : W[i], u4 ? W[i] : W[i + 8], 4);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) b2[i] = bfly(u2 ? a[i + 4] : a[i], u2 ? a[i] : a[i + 4], 2);
+#pragma unroll
+    for (int i = 0; i < 2; ++i) out[i] = bfly(u1 ? b2[i + 2] : b2[i], u1 ? b2[i] : b2[i + 2], 1);
+  }
+}
+
+// Kernel-side parameter blocks (host fills the derived fields).
+struct FwdK {
+  ss_fwd_args a;
+  int dpg;        // channels per group
+  int tpg;        // 32-channel tiles per group
+  int ntiles;     // ceil(seqlen / kTile)
+  int vec_u, vec_d, vec_z, vec_out;
+};
+
+struct BwdK {
+  ss_bwd_args a;
+  int dpg, tpg, ntiles;
+  int vec_u, vec_d, vec_z, vec_dout, vec_du, vec_dd, vec_dz;
+  int vec_dbc;    // dB/dC rows are 16-byte aligned (seqlen % 4 == 0)
+};
+
+}  // namespace ssb

@@ -1,0 +1,76 @@
+// Single-token decode step (no counterpart in the reference, whose generate() is a stub,
+// models/causal_lm.py:61-62): one step of the forward recurrence from a stored state,
+//   dt'      = softplus(dt + dt_bias)   (threshold 20, as forward_kernel.cu:216-221)
+//   state[n] = exp(dt' A[c,n]) state[n] + dt' x B[n]
+//   out      = (sum_n C[n] state[n] + D x) [* silu(z)]
+// Bandwidth-bound on the fp32 state (read + write 8 B per (b, c, n)).  TPC threads per
+// channel (4 states each, one 16-byte access) keep every state access coalesced; the
+// output sum over states is a shuffle over the TPC adjacent lanes.
+#pragma once
+#include "ss_common.cuh"
+
+namespace ssb {
+
+template <typename IT, int TPC>
+__global__ void __launch_bounds__(128) ss_step_kernel(const __grid_constant__ ss_step_args a) {
+  constexpr int CPB = 128 / TPC;  // channels per block
+  const int tid = threadIdx.x;
+  const int q = tid % TPC;
+  const int c = blockIdx.x * CPB + tid / TPC;
+  const int b = blockIdx.y;
+  const int N = a.dstate;
+  const bool ok = c < a.dim;
+  const int cc = ok ? c : 0;
+  const int g = cc / (a.dim / a.ngroups);
+  const bool bc_f32 = a.bc_dtype == SS_F32;
+
+  float xv = 0.f, dv = 0.f, zv = 0.f;
+  if (ok) {
+    xv = to_f<IT>(((const IT*)a.x)[(int64_t)b * a.x_batch_stride + c]);
+    dv = to_f<IT>(((const IT*)a.dt)[(int64_t)b * a.dt_batch_stride + c]);
+    if (a.dt_bias != nullptr) dv += a.dt_bias[c];
+    if (a.z != nullptr) zv = to_f<IT>(((const IT*)a.z)[(int64_t)b * a.z_batch_stride + c]);
+  }
+  const float dt = a.dt_softplus ? softplus_thr(dv) : dv;
+  float* st = a.state + (int64_t)b * a.state_batch_stride + (int64_t)cc * N;
+  const int64_t bco = ((int64_t)b * a.ngroups + g) * N;
+
+  float y = 0.f;
+  if (ok) {
+    float s[kSPW];
+    const bool vec = (N % 4) == 0 && ((reinterpret_cast<uintptr_t>(st) & 15) == 0);
+    if (vec && 4 * q < N) {
+      const float4 v = *reinterpret_cast<const float4*>(st + 4 * q);
+      s[0] = v.x; s[1] = v.y; s[2] = v.z; s[3] = v.w;
+    } else {
+#pragma unroll
+      for (int j = 0; j < kSPW; ++j) s[j] = (4 * q + j < N) ? st[4 * q + j] : 0.f;
+    }
+#pragma unroll
+    for (int j = 0; j < kSPW; ++j) {
+      const int n = 4 * q + j;
+      if (n < N) {
+        const float Bn = bc_f32 ? ((const float*)a.B)[bco + n] : to_f<IT>(((const IT*)a.B)[bco + n]);
+        const float Cn = bc_f32 ? ((const float*)a.C)[bco + n] : to_f<IT>(((const IT*)a.C)[bco + n]);
+        s[j] = fmaf(exp_fast(dt * a.A[(int64_t)c * N + n]), s[j], dt * xv * Bn);
+        y = fmaf(Cn, s[j], y);
+      }
+    }
+    if (vec && 4 * q < N) {
+      *reinterpret_cast<float4*>(st + 4 * q) = make_float4(s[0], s[1], s[2], s[3]);
+    } else {
+#pragma unroll
+      for (int j = 0; j < kSPW; ++j)
+        if (4 * q + j < N) st[4 * q + j] = s[j];
+    }
+  }
+#pragma unroll
+  for (int o = 1; o < TPC; o <<= 1) y += __shfl_xor_sync(0xffffffffu, y, o);
+  if (ok && q == 0) {
+    if (a.D != nullptr) y = fmaf(a.D[c], xv, y);
+    if (a.z != nullptr) y *= zv * sigmoid_fast(zv);
+    ((IT*)a.out)[(int64_t)b * a.out_batch_stride + c] = from_f<IT>(y);
+  }
+}
+
+}  // namespace ssb

@@ -1,0 +1,252 @@
+"""Selective-scan operators over the sm_100a C-ABI library.
+
+Reference interface mirrored (nmquan1503/Mamba, ops/selective_scan_interface.py:7-49):
+``SelectiveScanFn`` is an autograd Function that makes its inputs contiguous, runs the
+native forward, saves (u, delta, A, B, C, D, delta_bias, x) and runs the native backward.
+This module keeps that contract and widens it to the surface the Mamba ecosystem uses:
+
+* ``selective_scan_fn(u, delta, A, B, C, D=None, z=None, delta_bias=None,
+  delta_softplus=False, return_last_state=False)`` — adds the SiLU(z) gate
+  (the reference applies it outside the op, modules/mamba_simple.py:143-146) and the
+  final state;
+* bf16 / fp16 I/O with fp32 state (the reference hard-codes fp32, forward_kernel.cu:17);
+* B, C as (b, N, L) (one group), (b, G, N, L) or constant (d, N) — the reference
+  classifies B as constant iff ``B.dim() < 3`` (csrc/selective_scan/selective_scan.cpp:194);
+* ``selective_state_update`` — the single-token decode step the reference lacks.
+
+Everything runs on CUDA through ``libmamba_b200_ss.so``; there is no CPU path.
+"""
+from __future__ import annotations
+
+import torch
+
+from . import _lib as L
+
+
+# ----------------------------------------------------------------------------- helpers
+def _cuda_device(*ts):
+    dev = None
+    for t in ts:
+        if t is None:
+            continue
+        if not t.is_cuda:
+            raise RuntimeError("mamba_b200 selective scan needs CUDA tensors (there is no CPU path)")
+        if dev is None:
+            dev = t.device
+        elif t.device != dev:
+            raise RuntimeError(f"tensors on different devices: {dev} and {t.device}")
+    return dev
+
+
+def _rows(t):
+    """(b, d, L) view whose last axis has stride 1 (copy only if it has not)."""
+    if t is None:
+        return None
+    if t.dim() != 3:
+        raise ValueError(f"expected a (batch, dim, seqlen) tensor, got shape {tuple(t.shape)}")
+    return t if t.stride(-1) == 1 or t.shape[-1] <= 1 else t.contiguous()
+
+
+def _f32(t):
+    return None if t is None else t.to(torch.float32).contiguous()
+
+
+def _bc(B, C, io_dtype):
+    """Normalise B, C; returns (B, C, var_B, var_C, ngroups, bc_code)."""
+    var_B, var_C = B.dim() >= 3, C.dim() >= 3
+    if var_B and B.dim() == 3:
+        B = B.unsqueeze(1)
+    if var_C and C.dim() == 3:
+        C = C.unsqueeze(1)
+    ng = B.shape[1] if var_B else (C.shape[1] if var_C else 1)
+    if var_B and var_C and B.shape[1] != C.shape[1]:
+        raise ValueError("B and C must have the same number of groups")
+    if B.dtype == io_dtype and C.dtype == io_dtype:
+        code = L.dtype_code(io_dtype)
+    else:
+        B, C = B.to(torch.float32), C.to(torch.float32)
+        code = L.SS_F32
+    return B.contiguous(), C.contiguous(), int(var_B), int(var_C), int(ng), code
+
+
+class _Prepared:
+    """Validated, normalised operands of one scan call."""
+
+    def __init__(self, u, delta, A, B, C, D, z, delta_bias, delta_softplus):
+        self.device = _cuda_device(u, delta, A, B, C, D, z, delta_bias)
+        self.u_shape = u.shape
+        u = _rows(u)
+        io = u.dtype
+        L.dtype_code(io)
+        self.delta = _rows(delta if delta.dtype == io else delta.to(io))
+        self.z = None if z is None else _rows(z if z.dtype == io else z.to(io))
+        self.u = u
+        b, d, l = u.shape
+        if self.delta.shape != u.shape or (self.z is not None and self.z.shape != u.shape):
+            raise ValueError("u, delta and z must share the shape (batch, dim, seqlen)")
+        if A.dim() != 2 or A.shape[0] != d:
+            raise ValueError(f"A must be (dim, dstate), got {tuple(A.shape)}")
+        self.A = _f32(A)
+        n = A.shape[1]
+        self.B_shape, self.C_shape = B.shape, C.shape
+        self.B, self.C, self.var_B, self.var_C, self.ngroups, self.bc_code = _bc(B, C, io)
+        for M, name, var in ((self.B, "B", self.var_B), (self.C, "C", self.var_C)):
+            want = (b, self.ngroups, n, l) if var else (d, n)
+            if tuple(M.shape) != want:
+                raise ValueError(f"{name} has shape {tuple(M.shape)}, expected {want}")
+        if d % self.ngroups:
+            raise ValueError("dim must be a multiple of the number of groups")
+        self.D = _f32(D)
+        self.delta_bias = _f32(delta_bias)
+        self.softplus = int(bool(delta_softplus))
+        self.b, self.d, self.l, self.n = b, d, l, n
+        self.io = io
+
+    def fwd_args(self, out, ckpt=None, last=None):
+        u, dl, z = self.u, self.delta, self.z
+        return L.FwdArgs(
+            self.b, self.d, self.l, self.n, self.ngroups, self.var_B, self.var_C, self.softplus,
+            L.dtype_code(self.io), self.bc_code,
+            u.data_ptr(), u.stride(0), u.stride(1),
+            dl.data_ptr(), dl.stride(0), dl.stride(1),
+            self.A.data_ptr(), self.B.data_ptr(), self.C.data_ptr(), L.ptr(self.D),
+            L.ptr(z), z.stride(0) if z is not None else 0, z.stride(1) if z is not None else 0,
+            L.ptr(self.delta_bias),
+            out.data_ptr(), out.stride(0), out.stride(1),
+            L.ptr(ckpt), L.ptr(last))
+
+
+def _new_ckpt(p: _Prepared):
+    return torch.empty(max(L.ckpt_elems(p.b, p.d, p.l, p.n), 1), dtype=torch.float32, device=p.device)
+
+
+def scan_forward(p: _Prepared, want_ckpt: bool, want_last: bool):
+    """Run the native forward.  Returns (out, ckpt | None, last_state | None)."""
+    out = torch.empty((p.b, p.d, p.l), dtype=p.io, device=p.device)
+    ckpt = _new_ckpt(p) if want_ckpt else None
+    last = torch.empty((p.b, p.d, p.n), dtype=torch.float32, device=p.device) if want_last else None
+    args = p.fwd_args(out, ckpt, last)
+    with torch.cuda.device(p.device):
+        L.check(L.lib().ss_fwd(args, L.stream_of(p.device)), "ss_fwd")
+    return out, ckpt, last
+
+
+def scan_backward(p: _Prepared, dout, ckpt):
+    """Run the native backward.  Returns (du, ddelta, dA, dB, dC, dD, dz, ddelta_bias) with
+    fp32 dA / dB / dC / dD / ddelta_bias shaped like the normalised operands."""
+    if ckpt is None:  # the forward's states were not kept: recompute them
+        _, ckpt, _ = scan_forward(p, True, False)
+    dout = _rows(dout if dout.dtype == p.io else dout.to(p.io))
+    if dout.shape != p.u.shape:
+        raise ValueError("dout must have the shape of u")
+    dev = p.device
+    du = torch.empty((p.b, p.d, p.l), dtype=p.io, device=dev)
+    ddelta = torch.empty_like(du)
+    dz = torch.empty_like(du) if p.z is not None else None
+    dA = torch.empty((p.d, p.n), dtype=torch.float32, device=dev)
+    dB = torch.empty(p.B.shape, dtype=torch.float32, device=dev)
+    dC = torch.empty(p.C.shape, dtype=torch.float32, device=dev)
+    dD = torch.empty(p.d, dtype=torch.float32, device=dev) if p.D is not None else None
+    dbias = torch.empty(p.d, dtype=torch.float32, device=dev) if p.delta_bias is not None else None
+    placeholder = du  # stands in for the unused output row pointer of the embedded forward args
+    args = L.BwdArgs(
+        p.fwd_args(placeholder, ckpt, None),
+        dout.data_ptr(), dout.stride(0), dout.stride(1),
+        du.data_ptr(), du.stride(0), du.stride(1),
+        ddelta.data_ptr(), ddelta.stride(0), ddelta.stride(1),
+        L.ptr(dz), dz.stride(0) if dz is not None else 0, dz.stride(1) if dz is not None else 0,
+        dA.data_ptr(), dB.data_ptr(), dC.data_ptr(), L.ptr(dD), L.ptr(dbias))
+    with torch.cuda.device(dev):
+        L.check(L.lib().ss_bwd(args, L.stream_of(dev)), "ss_bwd")
+    return du, ddelta, dA, dB, dC, dD, dz, dbias
+
+
+# ----------------------------------------------------------------------------- autograd
+class SelectiveScanFn(torch.autograd.Function):
+    """Autograd op: out = selective_scan(u, delta, A, B, C, D, z, delta_bias).
+
+    Same role as the reference's SelectiveScanFn (ops/selective_scan_interface.py:7-49):
+    the forward keeps the tensors the backward needs plus the opaque state buffer the
+    native forward wrote (the reference keeps its chunk carry ``x`` the same way).
+    """
+
+    @staticmethod
+    def forward(ctx, u, delta, A, B, C, D=None, z=None, delta_bias=None, delta_softplus=False,
+                return_last_state=False):
+        p = _Prepared(u, delta, A, B, C, D, z, delta_bias, delta_softplus)
+        need_grad = any(ctx.needs_input_grad[:8])
+        out, ckpt, last = scan_forward(p, need_grad, return_last_state)
+        ctx.delta_softplus = delta_softplus
+        ctx.shapes = (B.shape, C.shape)
+        ctx.dtypes = (u.dtype, delta.dtype, A.dtype, B.dtype, C.dtype,
+                      None if D is None else D.dtype, None if z is None else z.dtype,
+                      None if delta_bias is None else delta_bias.dtype)
+        ctx.save_for_backward(u, delta, A, B, C, D, z, delta_bias, ckpt)
+        if return_last_state:
+            ctx.mark_non_differentiable(last)
+            return out, last
+        return out
+
+    @staticmethod
+    def backward(ctx, dout, *unused):
+        u, delta, A, B, C, D, z, delta_bias, ckpt = ctx.saved_tensors
+        p = _Prepared(u, delta, A, B, C, D, z, delta_bias, ctx.delta_softplus)
+        du, ddelta, dA, dB, dC, dD, dz, dbias = scan_backward(p, dout, ckpt)
+        tu, tdl, tA, tB, tC, tD, tz, tbias = ctx.dtypes
+        dB = dB.reshape(ctx.shapes[0]).to(tB)
+        dC = dC.reshape(ctx.shapes[1]).to(tC)
+        return (du.to(tu), ddelta.to(tdl), dA.to(tA), dB, dC,
+                None if dD is None else dD.to(tD), None if dz is None else dz.to(tz),
+                None if dbias is None else dbias.to(tbias), None, None)
+
+
+def selective_scan_fn(u, delta, A, B, C, D=None, z=None, delta_bias=None, delta_softplus=False,
+                      return_last_state=False):
+    """Selective scan with optional SiLU(z) gate.
+
+    u, delta, z: (batch, dim, seqlen); A: (dim, dstate); B, C: (batch, dstate, seqlen),
+    (batch, ngroups, dstate, seqlen) or constant (dim, dstate); D, delta_bias: (dim,).
+    Returns out (batch, dim, seqlen) in u's dtype, and last_state (batch, dim, dstate) fp32
+    when return_last_state.
+    """
+    return SelectiveScanFn.apply(u, delta, A, B, C, D, z, delta_bias, delta_softplus,
+                                 return_last_state)
+
+
+# ----------------------------------------------------------------------------- decode
+def selective_state_update(state, x, dt, A, B, C, D=None, z=None, dt_bias=None, dt_softplus=False):
+    """One decode step; updates ``state`` (batch, dim, dstate) fp32 in place.
+
+    x, dt, z: (batch, dim); A: (dim, dstate); B, C: (batch, dstate) or (batch, ngroups, dstate);
+    D, dt_bias: (dim,).  Returns out (batch, dim) in x's dtype:
+    out = (C . state' + D x) [* silu(z)], state' = exp(dt' A) state + dt' x B.
+    """
+    dev = _cuda_device(state, x, dt, A, B, C, D, z, dt_bias)
+    if state.dtype != torch.float32 or state.stride(-1) != 1 or state.stride(-2) != state.shape[-1]:
+        raise ValueError("state must be float32 with contiguous (dim, dstate) rows")
+    b, d, n = state.shape
+    io = x.dtype
+    xs = x if x.stride(-1) == 1 else x.contiguous()
+    dts = (dt if dt.dtype == io else dt.to(io))
+    dts = dts if dts.stride(-1) == 1 else dts.contiguous()
+    zs = None if z is None else (z if z.dtype == io else z.to(io))
+    if zs is not None and zs.stride(-1) != 1:
+        zs = zs.contiguous()
+    if B.dim() == 2:
+        B, C = B.unsqueeze(1), C.unsqueeze(1)
+    ng = B.shape[1]
+    if B.dtype == io and C.dtype == io:
+        bc = L.dtype_code(io)
+    else:
+        B, C, bc = B.float(), C.float(), L.SS_F32
+    B, C = B.contiguous(), C.contiguous()
+    Af, Df, bf = _f32(A), _f32(D), _f32(dt_bias)
+    out = torch.empty((b, d), dtype=io, device=dev)
+    args = L.StepArgs(b, d, n, ng, int(bool(dt_softplus)), L.dtype_code(io), bc,
+                      state.data_ptr(), state.stride(0), xs.data_ptr(), xs.stride(0),
+                      dts.data_ptr(), dts.stride(0), Af.data_ptr(), B.data_ptr(), C.data_ptr(),
+                      L.ptr(Df), L.ptr(zs), zs.stride(0) if zs is not None else 0, L.ptr(bf),
+                      out.data_ptr(), out.stride(0))
+    with torch.cuda.device(dev):
+        L.check(L.lib().ss_step(args, L.stream_of(dev)), "ss_step")
+    return out

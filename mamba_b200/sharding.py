@@ -1,0 +1,104 @@
+"""Partitioning of a selective scan over ranks (one process per GPU).
+
+Every (batch row, channel) recurrence is independent, so the scan shards without any
+exchange inside the path: ranks take disjoint blocks of batch rows first (when the batch
+divides among the ranks) and otherwise disjoint blocks of channels, aligned to whole
+groups' worth of 32-channel CTA tiles where possible.  Collectives appear only around the
+path:
+
+* verification — ``gather_rows`` all-gathers shards of outputs for a check on one rank;
+* parameter gradients — under batch sharding each rank holds partial dA, dD, ddelta_bias
+  (summed over its own rows) and ``reduce_param_grads`` all-reduces them; under channel
+  sharding it is dB / dC (summed over its channels) that are partial.
+
+The helpers take a ``torch.distributed`` process group, so they run unchanged on NCCL
+(GPUs) and gloo (the CPU tests).
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+import torch.distributed as dist
+
+
+@dataclass(frozen=True)
+class Shard:
+    rank: int
+    world: int
+    axis: str            # "batch" or "dim"
+    start: int
+    stop: int
+    gstart: int = 0      # groups owned (channel shards of whole groups); (0, 0): all groups
+    gstop: int = 0
+
+    @property
+    def size(self) -> int:
+        return self.stop - self.start
+
+
+def plan(batch: int, dim: int, world: int, rank: int, ngroups: int = 1) -> Shard:
+    """Split over batch rows when batch % world == 0, else over channels.
+
+    Channel shards keep whole groups together when ngroups % world == 0 (each rank then
+    owns complete groups and its dB / dC need no reduction); otherwise they split the
+    channels into near-equal blocks aligned to 32 channels inside a single group.
+    """
+    if world < 1 or not 0 <= rank < world:
+        raise ValueError(f"bad rank {rank} / world {world}")
+    if batch % world == 0:
+        per = batch // world
+        return Shard(rank, world, "batch", rank * per, (rank + 1) * per)
+    if dim % ngroups:
+        raise ValueError("dim must be a multiple of ngroups")
+    if ngroups > 1 and ngroups % world == 0:
+        gper = ngroups // world
+        per = gper * (dim // ngroups)
+        return Shard(rank, world, "dim", rank * per, (rank + 1) * per, rank * gper, (rank + 1) * gper)
+    if ngroups != 1:
+        raise ValueError("channel sharding needs ngroups == 1 or ngroups % world == 0")
+    tiles = -(-dim // 32)
+    lo = (tiles * rank) // world * 32
+    hi = min(dim, (tiles * (rank + 1)) // world * 32)
+    return Shard(rank, world, "dim", lo, hi)
+
+
+def take(x: torch.Tensor | None, s: Shard, role: str):
+    """Slice an operand for shard s.  role: 'row' (b, d, L), 'bc' (b, G, N, L) or (b, N, L),
+    'chan' (d, ...) per-channel parameter."""
+    if x is None:
+        return None
+    if role == "row":
+        return x[s.start:s.stop] if s.axis == "batch" else x[:, s.start:s.stop]
+    if role == "bc":
+        if s.axis == "batch":
+            return x[s.start:s.stop]
+        if s.gstop > s.gstart and x.dim() == 4:  # whole groups: their B / C rows only
+            return x[:, s.gstart:s.gstop]
+        return x
+    if role == "chan":
+        return x if s.axis == "batch" else x[s.start:s.stop]
+    raise ValueError(role)
+
+
+def gather_rows(local: torch.Tensor, s: Shard, group=None) -> torch.Tensor:
+    """All-gather (b, d, ...) shards into the full tensor (equal shard sizes required,
+    which plan() guarantees for batch shards and for group-aligned channel shards)."""
+    world = s.world
+    parts = [torch.empty_like(local) for _ in range(world)]
+    dist.all_gather(parts, local.contiguous(), group=group)
+    return torch.cat(parts, dim=0 if s.axis == "batch" else 1)
+
+
+def reduce_param_grads(grads: dict, s: Shard, group=None) -> dict:
+    """Sum the gradients that are partial on each rank (see module docstring)."""
+    if s.axis == "batch":
+        keys = ("dA", "dD", "ddelta_bias")
+    elif s.gstop > s.gstart:
+        keys = ()  # each rank owns whole groups: its dB / dC are complete
+    else:
+        keys = ("dB", "dC")
+    for k in keys:
+        if grads.get(k) is not None:
+            dist.all_reduce(grads[k], op=dist.ReduceOp.SUM, group=group)
+    return grads

@@ -1,0 +1,172 @@
+"""Parity of the sm_100a forward / backward scan with the CPU oracle (fp64 state).
+
+Every case runs the product through its public operator (selective_scan_fn, which calls
+the C ABI of libmamba_b200_ss.so) on seeded inputs and compares against the oracle on the
+same values.  Tolerances are the ones stated for this path: fp32 I/O rtol 1e-4 / atol 1e-5,
+bf16 / fp16 I/O (fp32 state) rtol 2e-2 / atol 5e-2, elementwise.  Gradients that are sums
+over many elements (dA, dB, dC, dD, ddelta_bias) are checked elementwise against
+atol + rtol * |ref| with atol scaled by the largest reference magnitude of that tensor
+(a sum of K terms carries ~sqrt(K) ulp of rounding of its largest terms, which a fixed
+atol cannot express); the scale is stated in `_sum_atol`.
+"""
+import zlib
+
+import numpy as np
+import pytest
+import torch
+
+from common import TOL, assert_close, make_inputs, np_, to_dev
+from oracle import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+SUMMED = ("dA", "dB", "dC", "dD", "ddelta_bias")
+
+
+def _sum_atol(ref, rtol):
+    return rtol * float(np.max(np.abs(np_(ref)))) if np_(ref).size else 0.0
+
+
+def run_case(inp, *, last=True, grads=True):
+    import mamba_b200
+
+    dev = to_dev(inp)
+    req = [k for k in ("u", "delta", "A", "B", "C", "D", "z", "delta_bias") if dev[k] is not None]
+    for k in req:
+        dev[k] = dev[k].detach().requires_grad_(grads)
+    res = mamba_b200.selective_scan_fn(dev["u"], dev["delta"], dev["A"], dev["B"], dev["C"], dev["D"],
+                                       dev["z"], dev["delta_bias"], dev["softplus"], return_last_state=last)
+    out, st = res if last else (res, None)
+    got = {"out": out.detach(), "last_state": st}
+    if grads:
+        out.backward(dev["dout"])
+        for k in req:
+            got["d" + k] = dev[k].grad
+    torch.cuda.synchronize()
+    return got
+
+
+def oracle_case(inp, grads=True):
+    args = (inp["u"], inp["delta"], inp["A"], inp["B"], inp["C"], inp["D"], inp["z"], inp["delta_bias"],
+            inp["softplus"])
+    out, last = O.selective_scan_ref(*args, return_last_state=True)
+    want = {"out": out, "last_state": last}
+    if grads:
+        g = O.selective_scan_ref_bwd(*args, inp["dout"])
+        want.update({k: v for k, v in g.items() if v is not None})
+    return want
+
+
+def compare(got, want, dtype, keys=None):
+    rtol, atol = TOL[dtype]
+    for k, w in want.items():
+        if keys is not None and k not in keys:
+            continue
+        if got.get(k) is None:
+            continue
+        g = got[k]
+        if k in ("dB", "dC"):
+            g = g.reshape(w.shape)
+        a = max(atol, _sum_atol(w, rtol)) if k in SUMMED else atol
+        assert_close(k, g, w, rtol, a)
+
+
+CASES = {
+    # name: (b, d, L, n, kwargs)
+    "f32_base": (2, 64, 256, 16, dict()),
+    "f32_z": (2, 64, 200, 16, dict(has_z=True)),
+    "f32_ragged_groups": (2, 96, 301, 16, dict(groups=3, akind="rand")),
+    "f32_n8_partial_tile": (2, 40, 77, 8, dict(has_z=True)),
+    "f32_n4": (1, 32, 64, 4, dict(akind="rand")),
+    "f32_n1": (2, 8, 33, 1, dict()),
+    "f32_n12": (2, 32, 48, 12, dict(has_z=True)),
+    "f32_constB": (2, 32, 96, 16, dict(bc=("const", "var4"))),
+    "f32_constC": (2, 32, 96, 16, dict(bc=("var4", "const"), has_z=True)),
+    "f32_constBC": (2, 32, 50, 8, dict(bc="const")),
+    "f32_var3": (2, 32, 64, 16, dict(bc="var3")),
+    "f32_noD_nobias_nosp": (2, 32, 128, 16, dict(has_D=False, has_bias=False, softplus=False)),
+    "f32_L1": (3, 16, 1, 16, dict(has_z=True)),
+    "f32_L15": (1, 33, 15, 16, dict()),
+    "bf16_base": (2, 64, 512, 16, dict(dtype=torch.bfloat16, has_z=True)),
+    "bf16_bcf32": (2, 64, 130, 16, dict(dtype=torch.bfloat16, bc_f32=True)),
+    "f16_base": (2, 32, 160, 16, dict(dtype=torch.float16, has_z=True)),
+}
+
+
+@pytest.mark.parametrize("name", list(CASES))
+def test_fwd_bwd_parity(name):
+    b, d, L, n, kw = CASES[name]
+    inp = make_inputs(b, d, L, n, seed=zlib.crc32(name.encode()) % 1000, **kw)
+    got = run_case(inp)
+    want = oracle_case(inp)
+    compare(got, want, inp["u"].dtype)
+
+
+def test_forward_only_no_grad_path():
+    """Without autograd the forward runs without the state buffer; results are identical."""
+    import mamba_b200
+
+    inp = make_inputs(2, 64, 100, 16, has_z=True, seed=3)
+    dev = to_dev(inp)
+    with torch.no_grad():
+        out, last = mamba_b200.selective_scan_fn(dev["u"], dev["delta"], dev["A"], dev["B"], dev["C"], dev["D"],
+                                                 dev["z"], dev["delta_bias"], True, return_last_state=True)
+    got = run_case(inp, grads=False)
+    assert torch.equal(out, got["out"]) and torch.equal(last, got["last_state"])
+
+
+def test_strided_inputs_match_contiguous():
+    """u / z as channel halves of one (b, 2d, L) buffer (the xz layout) give the same result."""
+    import mamba_b200
+
+    inp = make_inputs(2, 64, 80, 16, has_z=True, seed=5)
+    dev = to_dev(inp)
+    xz = torch.cat([dev["u"], dev["z"]], dim=1)
+    u_v, z_v = xz[:, :64], xz[:, 64:]
+    assert not u_v.is_contiguous()
+    a = mamba_b200.selective_scan_fn(u_v, dev["delta"], dev["A"], dev["B"], dev["C"], dev["D"], z_v,
+                                     dev["delta_bias"], True)
+    b = mamba_b200.selective_scan_fn(dev["u"], dev["delta"], dev["A"], dev["B"], dev["C"], dev["D"], dev["z"],
+                                     dev["delta_bias"], True)
+    assert torch.equal(a, b)
+
+
+@pytest.mark.slow
+def test_config0_fp32_forward_full():
+    """Config 0: b2 d1536 L2048 N16 fp32 forward + last state, z and D = 1, full size."""
+    inp = make_inputs(2, 1536, 2048, 16, has_z=True, D_ones=True, seed=0)
+    got = run_case(inp, grads=False)
+    out, last = O.selective_scan_ref(inp["u"], inp["delta"], inp["A"], inp["B"], inp["C"], inp["D"], inp["z"],
+                                     inp["delta_bias"], True, return_last_state=True)
+    compare(got, {"out": out, "last_state": last}, torch.float32)
+
+
+@pytest.mark.slow
+def test_config1_bf16_fwd_bwd_full():
+    """Config 1: b2 d1536 L2048 N16, bf16 u/delta/z/B/C, fp32 A/D/bias, fwd + bwd, full size."""
+    inp = make_inputs(2, 1536, 2048, 16, dtype=torch.bfloat16, has_z=True, D_ones=True, seed=1)
+    got = run_case(inp)
+    want = oracle_case(inp)
+    compare(got, want, torch.bfloat16)
+
+
+@pytest.mark.slow
+def test_config2_long_sequence_last_state():
+    """Config 2: b1 d5120 L32768 bf16 forward with cross-tile carry; the oracle checks a
+    slice of channels (rows are independent, so the slice's reference is exact)."""
+    import mamba_b200
+
+    b, d, L, n = 1, 5120, 32768, 16
+    inp = make_inputs(b, d, L, n, dtype=torch.bfloat16, has_z=True, D_ones=True, seed=2)
+    dev = to_dev(inp)
+    with torch.no_grad():
+        out, last = mamba_b200.selective_scan_fn(dev["u"], dev["delta"], dev["A"], dev["B"], dev["C"], dev["D"],
+                                                 dev["z"], dev["delta_bias"], True, return_last_state=True)
+    sl = slice(0, 5120, 160)  # 32 channels spread over the whole width
+    ref_out, ref_last = O.selective_scan_ref(inp["u"][:, sl], inp["delta"][:, sl], inp["A"][sl], inp["B"], inp["C"],
+                                             inp["D"][sl], inp["z"][:, sl], inp["delta_bias"][sl], True,
+                                             return_last_state=True)
+    rtol, atol = TOL[torch.bfloat16]
+    assert_close("out", out[:, sl], ref_out, rtol, atol)
+    assert_close("last_state", last[:, sl], ref_last, rtol, atol)
+    assert torch.isfinite(out).all()

@@ -1,0 +1,69 @@
+"""Decode step (selective_state_update) on the GPU.
+
+The reference has no step function (models/causal_lm.py:61-62), so the step is pinned two
+ways: against the oracle's step, and against the forward scan itself — running the
+forward over a prompt, then stepping token by token from its final state, must
+reproduce the forward over the whole sequence (outputs of the stepped positions and the
+final state).
+"""
+import pytest
+import torch
+
+from common import TOL, assert_close, make_inputs, to_dev
+from oracle import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.mark.parametrize("dtype,n,groups,has_z,has_D", [
+    (torch.float32, 16, 1, True, True),
+    (torch.float32, 8, 2, False, True),
+    (torch.float32, 5, 1, True, False),
+    (torch.bfloat16, 16, 1, True, True),
+    (torch.float16, 16, 4, True, True),
+])
+def test_step_matches_oracle(dtype, n, groups, has_z, has_D):
+    import mamba_b200
+
+    b, d = 5, 64
+    g = torch.Generator().manual_seed(7)
+    state = torch.randn(b, d, n, generator=g)
+    x = torch.randn(b, d, generator=g).to(dtype)
+    dt = (0.5 * torch.randn(b, d, generator=g)).to(dtype)
+    z = torch.randn(b, d, generator=g).to(dtype) if has_z else None
+    A = -torch.exp(0.5 * torch.randn(d, n, generator=g))
+    B = torch.randn(b, groups, n, generator=g).to(dtype)
+    C = torch.randn(b, groups, n, generator=g).to(dtype)
+    D = torch.randn(d, generator=g) if has_D else None
+    bias = torch.randn(d, generator=g) - 3
+    st_ref, out_ref = O.selective_state_update_ref(state.numpy().copy(), x, dt, A, B, C, D, z, bias, True)
+    st = state.cuda()
+    out = mamba_b200.selective_state_update(st, x.cuda(), dt.cuda(), A.cuda(), B.cuda(), C.cuda(),
+                                            None if D is None else D.cuda(), None if z is None else z.cuda(),
+                                            bias.cuda(), dt_softplus=True)
+    rtol, atol = TOL[dtype]
+    assert_close("out", out, out_ref, rtol, atol)
+    assert_close("state", st, st_ref, 1e-4, 1e-5)
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_prompt_then_steps_equals_full_forward(dtype):
+    import mamba_b200
+
+    b, d, L, n, P = 4, 64, 48, 16, 37  # prompt of 37 tokens, then 11 steps
+    inp = to_dev(make_inputs(b, d, L, n, dtype=dtype, has_z=True, seed=11))
+    full, full_last = mamba_b200.selective_scan_fn(inp["u"], inp["delta"], inp["A"], inp["B"], inp["C"], inp["D"],
+                                                   inp["z"], inp["delta_bias"], True, return_last_state=True)
+    _, state = mamba_b200.selective_scan_fn(inp["u"][..., :P], inp["delta"][..., :P], inp["A"],
+                                            inp["B"][..., :P].contiguous(), inp["C"][..., :P].contiguous(),
+                                            inp["D"], inp["z"][..., :P], inp["delta_bias"], True,
+                                            return_last_state=True)
+    outs = []
+    for t in range(P, L):
+        outs.append(mamba_b200.selective_state_update(
+            state, inp["u"][..., t], inp["delta"][..., t], inp["A"], inp["B"][:, :, :, t], inp["C"][:, :, :, t],
+            inp["D"], inp["z"][..., t], inp["delta_bias"], dt_softplus=True))
+    stepped = torch.stack(outs, dim=-1)
+    rtol, atol = TOL[dtype]
+    assert_close("stepped outputs", stepped, full[..., P:], rtol, atol)
+    assert_close("final state", state, full_last, 1e-4, 1e-5)
