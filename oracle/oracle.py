@@ -48,7 +48,7 @@ def lib():
             f.argtypes = [I] * 7 + [P] * 8 + [I] + [P] * 9 + [I]
             f.restype = I
             f = getattr(L, f"ssor_step_{prec}")
-            f.argtypes = [I] * 4 + [P] * 10 + [I, P]
+            f.argtypes = [I] * 4 + [P] * 9 + [I, P]
             f.restype = I
         L.ssor_max_threads.restype = I
         _lib = L

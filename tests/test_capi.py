@@ -1,0 +1,118 @@
+"""The C-ABI library without a GPU: it loads, exports every entry point the header
+declares, agrees with the ctypes struct layouts, and rejects bad arguments with status
+codes before touching the device."""
+import ctypes
+import os
+import re
+
+import pytest
+
+import mamba_b200._lib as L
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADERS = [os.path.join(ROOT, "include", f) for f in os.listdir(os.path.join(ROOT, "include")) if f.endswith(".h")]
+
+
+def declared_symbols():
+    names = set()
+    for h in HEADERS:
+        for m in re.finditer(r"^SS_API\s+[\w\s\*]+?\b(\w+)\s*\(", open(h).read(), re.M):
+            names.add(m.group(1))
+    return names
+
+
+def test_header_declares_the_exports():
+    assert declared_symbols() == set(L.EXPORTS)
+
+
+def test_library_exports_every_declared_symbol():
+    lib = L.lib()
+    for name in declared_symbols():
+        assert hasattr(lib, name), name
+
+
+def test_abi_version_and_struct_layout():
+    lib = L.lib()
+    assert lib.ss_abi_version() == 1
+    for i, st in enumerate((L.FwdArgs, L.BwdArgs, L.StepArgs)):
+        assert lib.ss_struct_size(i) == ctypes.sizeof(st)
+    assert lib.ss_struct_size(7) == 0
+
+
+def test_ckpt_elems():
+    assert L.ckpt_elems(2, 64, 33, 16) == 2 * 3 * 16 * 64
+    assert L.ckpt_elems(8, 1536, 2048, 16) == 8 * 128 * 16 * 1536
+    assert L.ckpt_elems(0, 64, 33, 16) == 0
+
+
+def test_status_strings():
+    lib = L.lib()
+    for s in range(4):
+        assert lib.ss_status_string(s)
+    assert lib.ss_status_string(99) == b"unknown status"
+
+
+def _valid_fwd():
+    a = L.FwdArgs()
+    a.batch, a.dim, a.seqlen, a.dstate, a.ngroups = 2, 64, 128, 16, 1
+    a.var_B = a.var_C = 1
+    a.io_dtype = a.bc_dtype = L.SS_F32
+    # non-null dummies: validation must reject before any device access
+    for f in ("u", "delta", "A", "B", "C", "out"):
+        setattr(a, f, 0x1000)
+    a.u_batch_stride = a.delta_batch_stride = a.out_batch_stride = 64 * 128
+    a.u_dim_stride = a.delta_dim_stride = a.out_dim_stride = 128
+    return a
+
+
+@pytest.mark.parametrize("field,value,status", [
+    ("dstate", 17, L.SS_ERR_UNSUPPORTED),
+    ("dstate", 0, L.SS_ERR_INVALID),
+    ("ngroups", 3, L.SS_ERR_INVALID),          # 64 % 3 != 0
+    ("io_dtype", 7, L.SS_ERR_UNSUPPORTED),
+    ("bc_dtype", L.SS_F16, L.SS_ERR_UNSUPPORTED),  # fp16 B/C with fp32 I/O
+    ("u", None, L.SS_ERR_INVALID),
+    ("A", None, L.SS_ERR_INVALID),
+    ("out", None, L.SS_ERR_INVALID),
+    ("batch", 70000, L.SS_ERR_UNSUPPORTED),
+    ("u_dim_stride", -1, L.SS_ERR_INVALID),
+])
+def test_fwd_validation(field, value, status):
+    a = _valid_fwd()
+    setattr(a, field, value)
+    assert L.lib().ss_fwd(ctypes.byref(a), None) == status
+
+
+def test_bwd_validation():
+    lib = L.lib()
+    b = L.BwdArgs()
+    b.f = _valid_fwd()
+    assert lib.ss_bwd(ctypes.byref(b), None) == L.SS_ERR_INVALID  # no dout / grads
+    for f in ("dout", "du", "ddelta", "dA", "dB", "dC"):
+        setattr(b, f, 0x1000)
+    b.f.z = 0x1000
+    assert lib.ss_bwd(ctypes.byref(b), None) == L.SS_ERR_INVALID  # z given, dz missing
+    b.f.z = None
+    assert lib.ss_bwd(ctypes.byref(b), None) == L.SS_ERR_INVALID  # 128 steps need the checkpoints
+    assert lib.ss_bwd(None, None) == L.SS_ERR_INVALID
+
+
+def test_step_validation():
+    lib = L.lib()
+    s = L.StepArgs()
+    s.batch, s.dim, s.dstate, s.ngroups = 2, 64, 16, 1
+    s.io_dtype = s.bc_dtype = L.SS_F32
+    assert lib.ss_step(ctypes.byref(s), None) == L.SS_ERR_INVALID
+    s.dstate = 40
+    assert lib.ss_step(ctypes.byref(s), None) == L.SS_ERR_UNSUPPORTED
+    assert lib.ss_step(None, None) == L.SS_ERR_INVALID
+
+
+def test_status_codes_map_to_python_errors():
+    with pytest.raises(NotImplementedError):
+        L.check(L.SS_ERR_UNSUPPORTED, "x")
+    with pytest.raises(ValueError):
+        L.check(L.SS_ERR_INVALID, "x")
+    with pytest.raises(RuntimeError):
+        L.check(L.SS_ERR_CUDA, "x")
+    L.check(L.SS_OK, "x")
