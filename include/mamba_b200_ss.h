@@ -124,6 +124,11 @@ SS_API const char* ss_status_string(int status);
 /* The CUDA error (cudaError_t as int) behind the last SS_ERR_CUDA on this thread. */
 SS_API int ss_last_cuda_error(void);
 
+/* Error bits that kernels raised on the current device since the last reset (1: a bounded
+ * wait for a TMA tile gave up), or -1 if the status cannot be read.  Synchronizes `stream`;
+ * reset != 0 clears the bits. */
+SS_API int ss_device_status(int reset, void* stream);
+
 /* SS_ABI_VERSION of the loaded library. */
 SS_API int ss_abi_version(void);
 

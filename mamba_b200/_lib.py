@@ -66,7 +66,7 @@ class StepArgs(ctypes.Structure):
 
 
 EXPORTS = ("ss_fwd", "ss_bwd", "ss_step", "ss_ckpt_elems", "ss_status_string",
-           "ss_last_cuda_error", "ss_abi_version", "ss_struct_size")
+           "ss_last_cuda_error", "ss_abi_version", "ss_struct_size", "ss_device_status")
 
 _lib = None
 _lock = threading.Lock()
@@ -92,6 +92,8 @@ def lib():
                 L.ss_ckpt_elems.restype = ctypes.c_size_t
                 L.ss_status_string.argtypes = [c_int]
                 L.ss_status_string.restype = ctypes.c_char_p
+                L.ss_device_status.argtypes = [c_int, c_vp]
+                L.ss_device_status.restype = c_int
                 L.ss_struct_size.argtypes = [c_int]
                 L.ss_struct_size.restype = ctypes.c_size_t
                 for i, st in enumerate((FwdArgs, BwdArgs, StepArgs)):
@@ -129,6 +131,14 @@ def ptr(t):
 
 def stream_of(device: torch.device) -> int:
     return torch.cuda.current_stream(device).cuda_stream
+
+
+def device_status(device, reset: bool = True) -> int:
+    """Error bits raised by kernels on `device` (1 = a bounded TMA wait timed out)."""
+    import torch
+
+    with torch.cuda.device(device):
+        return int(lib().ss_device_status(int(reset), stream_of(torch.device(device))))
 
 
 def ckpt_elems(batch, dim, seqlen, dstate) -> int:

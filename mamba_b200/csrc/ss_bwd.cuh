@@ -23,34 +23,47 @@
 //     reference's two fp32 atomics per element and state (backward_kernel.cu:466-478);
 //   * leaves the per-step sums over its states (for du, ddelta, dz) in shared memory, where
 //     the element phase combines the warps.
+// Inputs (u, delta, dout, z, the B / C tiles and the checkpointed states) stream through a
+// TMA ring of kStages tiles, as in the forward; kTMA = false loads each tile synchronously.
 #pragma once
 #include "ss_common.cuh"
 
 namespace ssb {
 
 template <typename IT, int kNW, bool kVarB, bool kVarC, bool kHasZ>
+struct BwdSmem {
+  static constexpr int NS = kSPW * kNW;
+  alignas(128) IT u[kStages][kCh][kTile];
+  alignas(128) IT d[kStages][kCh][kTile];
+  alignas(128) IT g[kStages][kCh][kTile];
+  alignas(128) IT z[kHasZ ? kStages : 1][kCh][kTile];
+  alignas(128) float Braw[kVarB ? kStages : 1][NS * kTile];
+  alignas(128) float Craw[kVarC ? kStages : 1][NS * kTile];
+  alignas(128) float hck[kStages][NS][kCh];   // states at the tile start, [n][channel]
+  alignas(16) float4 dt_s[kCh][4];
+  alignas(16) float4 dtu_s[kCh][4];
+  alignas(16) float4 dy_s[kCh][4];
+  alignas(16) float4 sig_s[kCh][4];
+  alignas(16) float4 gz_s[kHasZ ? kCh : 1][4];
+  alignas(16) float B_s[kVarB ? kTile : 1][NS];
+  alignas(16) float C_s[kVarC ? kTile : 1][NS];
+  float s1_s[kNW][kTile][kPad];
+  float s2_s[kNW][kTile][kPad];
+  float y_s[kHasZ ? kNW : 1][kTile][kPad];
+  alignas(8) uint64_t full[kStages];
+};
+
+template <typename IT, int kNW, bool kVarB, bool kVarC, bool kHasZ, bool kTMA>
 __global__ void __launch_bounds__(32 * kNW, 2) ss_bwd_kernel(const __grid_constant__ BwdK P) {
   constexpr int NT = 32 * kNW;
   constexpr int NS = kSPW * kNW;
   constexpr int S = kTile / kNW;
   constexpr int KV = (kVarB ? 64 : 0) + (kVarC ? 64 : 0);   // butterfly values per lane
+  using Sm = BwdSmem<IT, kNW, kVarB, kVarC, kHasZ>;
+  extern __shared__ __align__(128) unsigned char smem_raw[];
+  Sm& sm = *reinterpret_cast<Sm*>(smem_raw);
   const ss_bwd_args& a = P.a;
   const ss_fwd_args& f = a.f;
-
-  __shared__ __align__(16) IT u_raw[kCh][kTile];
-  __shared__ __align__(16) IT d_raw[kCh][kTile];
-  __shared__ __align__(16) IT g_raw[kCh][kTile];
-  __shared__ __align__(16) IT z_raw[kHasZ ? kCh : 1][kTile];
-  __shared__ float4 dt_s[kCh][4];
-  __shared__ float4 dtu_s[kCh][4];
-  __shared__ float4 dy_s[kCh][4];
-  __shared__ float4 sig_s[kCh][4];
-  __shared__ float4 gz_s[kHasZ ? kCh : 1][4];
-  __shared__ __align__(16) float B_s[kVarB ? kTile : 1][NS];
-  __shared__ __align__(16) float C_s[kVarC ? kTile : 1][NS];
-  __shared__ float s1_s[kNW][kTile][kPad];
-  __shared__ float s2_s[kNW][kTile][kPad];
-  __shared__ float y_s[kHasZ ? kNW : 1][kTile][kPad];
 
   const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
   const int grp = blockIdx.x / P.tpg;
@@ -99,31 +112,72 @@ __global__ void __launch_bounds__(32 * kNW, 2) ss_bwd_kernel(const __grid_consta
   IT* dz_row = kHasZ ? (IT*)a.dz + (int64_t)b * a.dz_batch_stride + (int64_t)(c0 + pc) * a.dz_dim_stride : nullptr;
   const int64_t bc_off = ((int64_t)b * f.ngroups + grp) * N * (int64_t)L;
 
-  for (int k = P.ntiles - 1; k >= 0; --k) {
+  const int ntiles = P.ntiles;
+  const uint32_t io_bytes = kCh * kTile * (uint32_t)sizeof(IT);
+  const uint32_t bc_bytes = NS * kTile * (bc_f32 ? 4u : (uint32_t)sizeof(IT));
+  const uint32_t h_bytes = NS * kCh * 4u;
+  // iteration i handles tile ntiles-1-i
+  auto issue = [&](int i, int s) {
+    const int k = ntiles - 1 - i;
+    uint64_t* bar = &sm.full[s];
+    const uint32_t bytes = (3 + (kHasZ ? 1 : 0)) * io_bytes + ((kVarB ? 1 : 0) + (kVarC ? 1 : 0)) * bc_bytes +
+                           (k > 0 ? h_bytes : 0u);
+    mbar_expect_tx(bar, bytes);
     const int t0 = k * kTile;
-    const int tlen = min(kTile, L - t0);
-    load_tile<IT, NT>(u_raw, ub + t0, f.u_dim_stride, nvalid, tlen, P.vec_u);
-    load_tile<IT, NT>(d_raw, db + t0, f.delta_dim_stride, nvalid, tlen, P.vec_d);
-    load_tile<IT, NT>(g_raw, gb + t0, a.dout_dim_stride, nvalid, tlen, P.vec_dout);
-    if constexpr (kHasZ) load_tile<IT, NT>(z_raw, zb + t0, f.z_dim_stride, nvalid, tlen, P.vec_z);
-    if constexpr (kVarB) {
-      if (bc_f32) load_bc_tile<float, NT, NS>(B_s, (const float*)f.B + bc_off + t0, L, N, tlen);
-      else load_bc_tile<IT, NT, NS>(B_s, (const IT*)f.B + bc_off + t0, L, N, tlen);
-    }
-    if constexpr (kVarC) {
-      if (bc_f32) load_bc_tile<float, NT, NS>(C_s, (const float*)f.C + bc_off + t0, L, N, tlen);
-      else load_bc_tile<IT, NT, NS>(C_s, (const IT*)f.C + bc_off + t0, L, N, tlen);
-    }
-    // states at the tile start (end of the previous tile), from the forward's checkpoints
-    float hp[kTile + 1][kSPW];
-#pragma unroll
-    for (int j = 0; j < kSPW; ++j) {
-      const int n = kSPW * w + j;
-      hp[0][j] = (k > 0 && lane_ok && n < N)
-                     ? f.ckpt[(((int64_t)b * P.ntiles + (k - 1)) * N + n) * f.dim + c]
-                     : 0.f;
+    tma_load_3d(&sm.u[s][0][0], &P.tm_u, t0, c0, b, bar);
+    tma_load_3d(&sm.d[s][0][0], &P.tm_d, t0, c0, b, bar);
+    tma_load_3d(&sm.g[s][0][0], &P.tm_g, t0, c0, b, bar);
+    if constexpr (kHasZ) tma_load_3d(&sm.z[s][0][0], &P.tm_z, t0, c0, b, bar);
+    if constexpr (kVarB) tma_load_3d(&sm.Braw[s][0], &P.tm_B, t0, 0, b * f.ngroups + grp, bar);
+    if constexpr (kVarC) tma_load_3d(&sm.Craw[s][0], &P.tm_C, t0, 0, b * f.ngroups + grp, bar);
+    if (k > 0) tma_load_3d(&sm.hck[s][0][0], &P.tm_h, c0, 0, b * ntiles + (k - 1), bar);
+  };
+  if constexpr (kTMA) {
+    if (tid == 0) {
+      for (int s = 0; s < kStages; ++s) mbar_init(&sm.full[s], 1);
+      mbar_fence_init();
     }
     __syncthreads();
+    if (tid == 0)
+      for (int s = 0; s < kStages && s < ntiles; ++s) issue(s, s);
+  }
+
+  for (int it = 0; it < ntiles; ++it) {
+    const int k = ntiles - 1 - it;
+    const int t0 = k * kTile;
+    const int tlen = min(kTile, L - t0);
+    const int stg = kTMA ? it % kStages : 0;
+    bool failed = false;
+    float hp[kTile + 1][kSPW];
+    if constexpr (kTMA) {
+      failed = !mbar_wait_bounded(&sm.full[stg], (it / kStages) & 1);
+      if constexpr (kVarB) widen_bc<IT, NT, NS>(sm.B_s, sm.Braw[stg], bc_f32);
+      if constexpr (kVarC) widen_bc<IT, NT, NS>(sm.C_s, sm.Craw[stg], bc_f32);
+#pragma unroll
+      for (int j = 0; j < kSPW; ++j) hp[0][j] = (k > 0) ? sm.hck[stg][kSPW * w + j][lane] : 0.f;
+    } else {
+      load_tile<IT, NT>(sm.u[0], ub + t0, f.u_dim_stride, nvalid, tlen, P.vec_u);
+      load_tile<IT, NT>(sm.d[0], db + t0, f.delta_dim_stride, nvalid, tlen, P.vec_d);
+      load_tile<IT, NT>(sm.g[0], gb + t0, a.dout_dim_stride, nvalid, tlen, P.vec_dout);
+      if constexpr (kHasZ) load_tile<IT, NT>(sm.z[0], zb + t0, f.z_dim_stride, nvalid, tlen, P.vec_z);
+      if constexpr (kVarB) {
+        if (bc_f32) load_bc_tile<float, NT, NS>(sm.B_s, (const float*)f.B + bc_off + t0, L, N, tlen);
+        else load_bc_tile<IT, NT, NS>(sm.B_s, (const IT*)f.B + bc_off + t0, L, N, tlen);
+      }
+      if constexpr (kVarC) {
+        if (bc_f32) load_bc_tile<float, NT, NS>(sm.C_s, (const float*)f.C + bc_off + t0, L, N, tlen);
+        else load_bc_tile<IT, NT, NS>(sm.C_s, (const IT*)f.C + bc_off + t0, L, N, tlen);
+      }
+      // states at the tile start (end of the previous tile), from the forward's checkpoints
+#pragma unroll
+      for (int j = 0; j < kSPW; ++j) {
+        const int n = kSPW * w + j;
+        hp[0][j] = (k > 0 && lane_ok && n < N)
+                       ? f.ckpt[(((int64_t)b * ntiles + (k - 1)) * N + n) * f.dim + c]
+                       : 0.f;
+      }
+      __syncthreads();
+    }
 
     // ---- element phase 1: delta', delta'u, dy, softplus slope, gate slope
     {
@@ -132,17 +186,17 @@ __global__ void __launch_bounds__(32 * kNW, 2) ss_bwd_kernel(const __grid_consta
       for (int i = 0; i < S; ++i) {
         const int t = pq * S + i;
         const bool ok = pc_ok && t < tlen;
-        const float uv = to_f<IT>(u_raw[pc][t]);
-        const float v = to_f<IT>(d_raw[pc][t]) + bias;
+        const float uv = to_f<IT>(sm.u[stg][pc][t]);
+        const float v = to_f<IT>(sm.d[stg][pc][t]) + bias;
         float dt = v, sg = 1.f;
         if (f.delta_softplus && v <= 20.f) {
           dt = log1pf(exp_fast(v));
           sg = sigmoid_fast(v);
         }
-        const float go = to_f<IT>(g_raw[pc][t]);
+        const float go = to_f<IT>(sm.g[stg][pc][t]);
         float dy = go, gz = 0.f;
         if constexpr (kHasZ) {
-          const float zv = to_f<IT>(z_raw[pc][t]);
+          const float zv = to_f<IT>(sm.z[stg][pc][t]);
           const float sz = sigmoid_fast(zv);
           dy = go * zv * sz;
           gz = go * sz * (1.f + zv * (1.f - sz));
@@ -161,22 +215,30 @@ __global__ void __launch_bounds__(32 * kNW, 2) ss_bwd_kernel(const __grid_consta
 #pragma unroll
       for (int q = 0; q < S / 4; ++q) {
         const int ch = swz(pc, pq * (S / 4) + q);
-        dt_s[pc][ch] = make_float4(dtv[4 * q], dtv[4 * q + 1], dtv[4 * q + 2], dtv[4 * q + 3]);
-        dtu_s[pc][ch] = make_float4(dtuv[4 * q], dtuv[4 * q + 1], dtuv[4 * q + 2], dtuv[4 * q + 3]);
-        dy_s[pc][ch] = make_float4(dyv[4 * q], dyv[4 * q + 1], dyv[4 * q + 2], dyv[4 * q + 3]);
-        sig_s[pc][ch] = make_float4(sgv[4 * q], sgv[4 * q + 1], sgv[4 * q + 2], sgv[4 * q + 3]);
+        sm.dt_s[pc][ch] = make_float4(dtv[4 * q], dtv[4 * q + 1], dtv[4 * q + 2], dtv[4 * q + 3]);
+        sm.dtu_s[pc][ch] = make_float4(dtuv[4 * q], dtuv[4 * q + 1], dtuv[4 * q + 2], dtuv[4 * q + 3]);
+        sm.dy_s[pc][ch] = make_float4(dyv[4 * q], dyv[4 * q + 1], dyv[4 * q + 2], dyv[4 * q + 3]);
+        sm.sig_s[pc][ch] = make_float4(sgv[4 * q], sgv[4 * q + 1], sgv[4 * q + 2], sgv[4 * q + 3]);
         if constexpr (kHasZ)
-          gz_s[pc][ch] = make_float4(gzv[4 * q], gzv[4 * q + 1], gzv[4 * q + 2], gzv[4 * q + 3]);
+          sm.gz_s[pc][ch] = make_float4(gzv[4 * q], gzv[4 * q + 1], gzv[4 * q + 2], gzv[4 * q + 3]);
       }
     }
-    __syncthreads();
+    if (__syncthreads_or(failed)) {
+      if (tid == 0) {
+        if (P.status != nullptr) atomicOr(P.status, kStatusTimeout);
+        for (int j = it + 1; j < ntiles && j < it + kStages; ++j)
+          mbar_wait_bounded(&sm.full[j % kStages], (j / kStages) & 1);
+      }
+      __syncthreads();
+      return;
+    }
 
     // ---- scan phase, forward: decays and states of the tile in registers
     float da[kTile][kSPW];
 #pragma unroll
     for (int i4 = 0; i4 < 4; ++i4) {
-      const float4 dt4 = dt_s[lane][swz(lane, i4)];
-      const float4 du4 = dtu_s[lane][swz(lane, i4)];
+      const float4 dt4 = sm.dt_s[lane][swz(lane, i4)];
+      const float4 du4 = sm.dtu_s[lane][swz(lane, i4)];
       const float dts[4] = {dt4.x, dt4.y, dt4.z, dt4.w};
       const float dus[4] = {du4.x, du4.y, du4.z, du4.w};
 #pragma unroll
@@ -184,7 +246,7 @@ __global__ void __launch_bounds__(32 * kNW, 2) ss_bwd_kernel(const __grid_consta
         const int t = 4 * i4 + s;
         float Bv[kSPW];
         if constexpr (kVarB) {
-          const float4 q = *reinterpret_cast<const float4*>(&B_s[t][kSPW * w]);
+          const float4 q = *reinterpret_cast<const float4*>(&sm.B_s[t][kSPW * w]);
           Bv[0] = q.x; Bv[1] = q.y; Bv[2] = q.z; Bv[3] = q.w;
         } else {
 #pragma unroll
@@ -198,7 +260,7 @@ __global__ void __launch_bounds__(32 * kNW, 2) ss_bwd_kernel(const __grid_consta
         if constexpr (kHasZ) {
           float Cv[kSPW];
           if constexpr (kVarC) {
-            const float4 q = *reinterpret_cast<const float4*>(&C_s[t][kSPW * w]);
+            const float4 q = *reinterpret_cast<const float4*>(&sm.C_s[t][kSPW * w]);
             Cv[0] = q.x; Cv[1] = q.y; Cv[2] = q.z; Cv[3] = q.w;
           } else {
 #pragma unroll
@@ -207,7 +269,7 @@ __global__ void __launch_bounds__(32 * kNW, 2) ss_bwd_kernel(const __grid_consta
           float yp = 0.f;
 #pragma unroll
           for (int j = 0; j < kSPW; ++j) yp = fmaf(Cv[j], hp[t + 1][j], yp);
-          y_s[w][t][lane] = yp;
+          sm.y_s[w][t][lane] = yp;
         }
       }
     }
@@ -218,9 +280,9 @@ __global__ void __launch_bounds__(32 * kNW, 2) ss_bwd_kernel(const __grid_consta
     float W[kTile];
 #pragma unroll
     for (int i4 = 3; i4 >= 0; --i4) {
-      const float4 dt4 = dt_s[lane][swz(lane, i4)];
-      const float4 du4 = dtu_s[lane][swz(lane, i4)];
-      const float4 dy4 = dy_s[lane][swz(lane, i4)];
+      const float4 dt4 = sm.dt_s[lane][swz(lane, i4)];
+      const float4 du4 = sm.dtu_s[lane][swz(lane, i4)];
+      const float4 dy4 = sm.dy_s[lane][swz(lane, i4)];
       const float dts[4] = {dt4.x, dt4.y, dt4.z, dt4.w};
       const float dus[4] = {du4.x, du4.y, du4.z, du4.w};
       const float dys[4] = {dy4.x, dy4.y, dy4.z, dy4.w};
@@ -229,14 +291,14 @@ __global__ void __launch_bounds__(32 * kNW, 2) ss_bwd_kernel(const __grid_consta
         const int t = 4 * i4 + s;
         float Bv[kSPW], Cv[kSPW];
         if constexpr (kVarB) {
-          const float4 q = *reinterpret_cast<const float4*>(&B_s[t][kSPW * w]);
+          const float4 q = *reinterpret_cast<const float4*>(&sm.B_s[t][kSPW * w]);
           Bv[0] = q.x; Bv[1] = q.y; Bv[2] = q.z; Bv[3] = q.w;
         } else {
 #pragma unroll
           for (int j = 0; j < kSPW; ++j) Bv[j] = Bc[j];
         }
         if constexpr (kVarC) {
-          const float4 q = *reinterpret_cast<const float4*>(&C_s[t][kSPW * w]);
+          const float4 q = *reinterpret_cast<const float4*>(&sm.C_s[t][kSPW * w]);
           Cv[0] = q.x; Cv[1] = q.y; Cv[2] = q.z; Cv[3] = q.w;
         } else {
 #pragma unroll
@@ -257,8 +319,8 @@ __global__ void __launch_bounds__(32 * kNW, 2) ss_bwd_kernel(const __grid_consta
           if constexpr (!kVarC) dCc[j] = fmaf(dys[s], hp[t + 1][j], dCc[j]);
           e[j] = ee;
         }
-        s1_s[w][t][lane] = s1;
-        s2_s[w][t][lane] = s2;
+        sm.s1_s[w][t][lane] = s1;
+        sm.s2_s[w][t][lane] = s2;
         if constexpr (KV == 128) W[t] = fold_step_bc(vB, vC, lane);
         else if constexpr (kVarB) W[t] = fold_step_one(vB, lane);
         else if constexpr (kVarC) W[t] = fold_step_one(vC, lane);
@@ -295,9 +357,9 @@ __global__ void __launch_bounds__(32 * kNW, 2) ss_bwd_kernel(const __grid_consta
 #pragma unroll
       for (int q = 0; q < S / 4; ++q) {
         const int ch = swz(pc, pq * (S / 4) + q);
-        const float4 dt4 = dt_s[pc][ch], dy4 = dy_s[pc][ch], sg4 = sig_s[pc][ch];
+        const float4 dt4 = sm.dt_s[pc][ch], dy4 = sm.dy_s[pc][ch], sg4 = sm.sig_s[pc][ch];
         float4 gz4 = make_float4(0.f, 0.f, 0.f, 0.f);
-        if constexpr (kHasZ) gz4 = gz_s[pc][ch];
+        if constexpr (kHasZ) gz4 = sm.gz_s[pc][ch];
         const float dts[4] = {dt4.x, dt4.y, dt4.z, dt4.w};
         const float dys[4] = {dy4.x, dy4.y, dy4.z, dy4.w};
         const float sgs[4] = {sg4.x, sg4.y, sg4.z, sg4.w};
@@ -309,11 +371,11 @@ __global__ void __launch_bounds__(32 * kNW, 2) ss_bwd_kernel(const __grid_consta
           float S1 = 0.f, S2 = 0.f, yv = 0.f;
 #pragma unroll
           for (int g = 0; g < kNW; ++g) {
-            S1 += s1_s[g][t][pc];
-            S2 += s2_s[g][t][pc];
-            if constexpr (kHasZ) yv += y_s[g][t][pc];
+            S1 += sm.s1_s[g][t][pc];
+            S2 += sm.s2_s[g][t][pc];
+            if constexpr (kHasZ) yv += sm.y_s[g][t][pc];
           }
-          const float uv = to_f<IT>(u_raw[pc][t]);
+          const float uv = to_f<IT>(sm.u[stg][pc][t]);
           duv[i] = fmaf(Dv, dys[r], dts[r] * S2);
           const float dd = fmaf(uv, S2, S1) * sgs[r];
           ddv[i] = dd;
@@ -327,6 +389,9 @@ __global__ void __launch_bounds__(32 * kNW, 2) ss_bwd_kernel(const __grid_consta
       if constexpr (kHasZ) store_run<IT, S>(dz_row + t0 + pq * S, dzv, nv, P.vec_dz);
     }
     __syncthreads();
+    if constexpr (kTMA) {
+      if (tid == 0 && it + kStages < ntiles) issue(it + kStages, stg);
+    }
   }
 
   // ---- per-channel parameter gradients (summed over batch rows by the atomics)

@@ -2,21 +2,95 @@
 // dtype dispatch.  The reference has no input checks at all (its binding,
 // csrc/selective_scan/selective_scan.cpp:184-329, passes raw pointers straight through);
 // here every call is checked first and reports a status code instead of faulting.
+#include <cuda.h>
+#include <cudaTypedefs.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
+
+#include <mutex>
 
 #include "../../include/mamba_b200_ss.h"
 #include "ss_common.cuh"
 
 namespace ssb {
-template <typename IT> cudaError_t launch_fwd(const FwdK&, cudaStream_t);
-template <typename IT> cudaError_t launch_bwd(const BwdK&, cudaStream_t);
+template <typename IT> cudaError_t launch_fwd(const FwdK&, cudaStream_t, bool);
+template <typename IT> cudaError_t launch_bwd(const BwdK&, cudaStream_t, bool);
 template <typename IT> cudaError_t launch_step(const ss_step_args&, cudaStream_t);
 }  // namespace ssb
+
+// One status word per device that loads the library: kernels OR kStatus* bits into it when
+// a bounded wait gives up (see ss_device_status).
+__device__ int g_ss_status;
 
 namespace {
 
 thread_local int g_last_cuda = 0;
+
+int* status_ptr() {
+  void* p = nullptr;
+  if (cudaGetSymbolAddress(&p, g_ss_status) != cudaSuccess) {
+    cudaGetLastError();
+    return nullptr;
+  }
+  return static_cast<int*>(p);
+}
+
+// cuTensorMapEncodeTiled from the driver, fetched through the runtime (no -lcuda link)
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    else
+      cudaGetLastError();
+  });
+  return fn;
+}
+
+CUtensorMapDataType tm_type(int dt) {
+  return dt == SS_F32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                      : (dt == SS_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16);
+}
+
+// 3-D tiled map: extents (d0 innermost, d1, d2), byte strides of d1 and d2, box (b0, b1, 1).
+// Returns false when TMA cannot describe the tensor (alignment), so the caller falls back.
+bool map3(CUtensorMap* m, const void* base, int dt, uint64_t d0, uint64_t d1, uint64_t d2, uint64_t s1,
+          uint64_t s2, uint32_t b0, uint32_t b1) {
+  auto fn = encode_fn();
+  const uint64_t es = dt == SS_F32 ? 4 : 2;
+  if (fn == nullptr || base == nullptr || (reinterpret_cast<uintptr_t>(base) & 15) || (s1 & 15) || (s2 & 15) ||
+      ((b0 * es) & 15) || s1 >= (1ull << 40) || s2 >= (1ull << 40))
+    return false;
+  cuuint64_t dims[3] = {d0, d1, d2};
+  cuuint64_t strides[2] = {s1, s2};
+  cuuint32_t box[3] = {b0, b1, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  return fn(m, tm_type(dt), 3, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+            CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// (batch, dim, seqlen) view with element strides -> box of 16 steps x 32 channels
+bool map_rows(CUtensorMap* m, const void* p, int dt, const ss_fwd_args& a, int64_t bs, int64_t ds) {
+  const uint64_t es = dt == SS_F32 ? 4 : 2;
+  const uint64_t s1 = a.dim > 1 ? (uint64_t)ds * es : (uint64_t)a.seqlen * es;
+  const uint64_t s2 = a.batch > 1 ? (uint64_t)bs * es : s1 * (uint64_t)a.dim;
+  if (ds < 0 || bs < 0) return false;
+  return map3(m, p, dt, (uint64_t)a.seqlen, (uint64_t)a.dim, (uint64_t)a.batch, s1, s2, ssb::kTile, ssb::kCh);
+}
+
+// variable B / C (batch, ngroups, dstate, seqlen) -> box of 16 steps x (padded) dstate
+bool map_bc(CUtensorMap* m, const void* p, const ss_fwd_args& a) {
+  const uint64_t es = a.bc_dtype == SS_F32 ? 4 : 2;
+  const uint32_t ns = 4u * (uint32_t)(a.dstate <= 4 ? 1 : (a.dstate <= 8 ? 2 : 4));
+  return map3(m, p, a.bc_dtype, (uint64_t)a.seqlen, (uint64_t)a.dstate, (uint64_t)a.batch * a.ngroups,
+              (uint64_t)a.seqlen * es, (uint64_t)a.seqlen * a.dstate * es, ssb::kTile, ns);
+}
 
 int cuda_status(cudaError_t e) {
   if (e == cudaSuccess) return SS_OK;
@@ -87,8 +161,15 @@ int ss_fwd(const ss_fwd_args* args, void* stream) {
   P.vec_d = rows16(args->delta, args->delta_batch_stride, args->delta_dim_stride, es);
   P.vec_z = args->z ? rows16(args->z, args->z_batch_stride, args->z_dim_stride, es) : 0;
   P.vec_out = rows16(args->out, args->out_batch_stride, args->out_dim_stride, es);
+  P.status = status_ptr();
+  const ss_fwd_args& a = *args;
+  bool tma = map_rows(&P.tm_u, a.u, a.io_dtype, a, a.u_batch_stride, a.u_dim_stride) &&
+             map_rows(&P.tm_d, a.delta, a.io_dtype, a, a.delta_batch_stride, a.delta_dim_stride);
+  if (tma && a.z) tma = map_rows(&P.tm_z, a.z, a.io_dtype, a, a.z_batch_stride, a.z_dim_stride);
+  if (tma && a.var_B) tma = map_bc(&P.tm_B, a.B, a);
+  if (tma && a.var_C) tma = map_bc(&P.tm_C, a.C, a);
   cudaStream_t st = (cudaStream_t)stream;
-  return dispatch(args->io_dtype, [&](auto tag) { return ssb::launch_fwd<decltype(tag)>(P, st); });
+  return dispatch(args->io_dtype, [&](auto tag) { return ssb::launch_fwd<decltype(tag)>(P, st, tma); });
 }
 
 int ss_bwd(const ss_bwd_args* args, void* stream) {
@@ -125,7 +206,23 @@ int ss_bwd(const ss_bwd_args* args, void* stream) {
   P.vec_dz = f.z ? rows16(args->dz, args->dz_batch_stride, args->dz_dim_stride, es) : 0;
   P.vec_dbc = (f.seqlen % 4) == 0 && (reinterpret_cast<uintptr_t>(args->dB) & 15) == 0 &&
               (reinterpret_cast<uintptr_t>(args->dC) & 15) == 0;
-  return dispatch(f.io_dtype, [&](auto tag) { return ssb::launch_bwd<decltype(tag)>(P, st); });
+  P.status = status_ptr();
+  // the checkpoint tile starts at channel c0: TMA needs c0 * 4 bytes to be 16-byte aligned
+  bool tma = (f.ngroups == 1 || (P.dpg % 4) == 0) &&
+             map_rows(&P.tm_u, f.u, f.io_dtype, f, f.u_batch_stride, f.u_dim_stride) &&
+             map_rows(&P.tm_d, f.delta, f.io_dtype, f, f.delta_batch_stride, f.delta_dim_stride) &&
+             map_rows(&P.tm_g, args->dout, f.io_dtype, f, args->dout_batch_stride, args->dout_dim_stride);
+  if (tma && f.z) tma = map_rows(&P.tm_z, f.z, f.io_dtype, f, f.z_batch_stride, f.z_dim_stride);
+  if (tma && f.var_B) tma = map_bc(&P.tm_B, f.B, f);
+  if (tma && f.var_C) tma = map_bc(&P.tm_C, f.C, f);
+  if (tma && f.ckpt) {
+    const uint32_t ns = 4u * (uint32_t)(f.dstate <= 4 ? 1 : (f.dstate <= 8 ? 2 : 4));
+    tma = map3(&P.tm_h, f.ckpt, SS_F32, (uint64_t)f.dim, (uint64_t)f.dstate, (uint64_t)f.batch * P.ntiles,
+               (uint64_t)f.dim * 4, (uint64_t)f.dim * f.dstate * 4, ssb::kCh, ns);
+  } else if (tma && P.ntiles > 1) {
+    tma = false;
+  }
+  return dispatch(f.io_dtype, [&](auto tag) { return ssb::launch_bwd<decltype(tag)>(P, st, tma); });
 }
 
 int ss_step(const ss_step_args* a, void* stream) {
@@ -153,6 +250,17 @@ const char* ss_status_string(int s) {
 int ss_last_cuda_error(void) { return g_last_cuda; }
 
 int ss_abi_version(void) { return SS_ABI_VERSION; }
+
+int ss_device_status(int reset, void* stream) {
+  int* p = status_ptr();
+  if (p == nullptr) return -1;
+  int v = 0;
+  cudaStream_t st = (cudaStream_t)stream;
+  if (cudaMemcpyAsync(&v, p, sizeof(int), cudaMemcpyDeviceToHost, st) != cudaSuccess) return -1;
+  if (reset && cudaMemsetAsync(p, 0, sizeof(int), st) != cudaSuccess) return -1;
+  if (cudaStreamSynchronize(st) != cudaSuccess) return -1;
+  return v;
+}
 
 size_t ss_struct_size(int which) {
   switch (which) {

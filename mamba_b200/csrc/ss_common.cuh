@@ -13,6 +13,7 @@
 //     :285) so the backward can restart any tile without a second forward scan.
 #pragma once
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
@@ -26,7 +27,12 @@ constexpr int kTile = 16;   // time steps per tile = checkpoint interval
 constexpr int kCh = 32;     // channels per CTA (one per lane)
 constexpr int kSPW = 4;     // states per warp
 constexpr int kPad = 34;    // row stride (floats) of the [t][channel] partial-sum arrays
+constexpr int kStages = 4;  // tiles of input in flight per CTA (TMA ring)
 constexpr float kLog2e = 1.4426950408889634f;
+
+// device status word codes (OR-ed into the caller-visible status buffer)
+constexpr int kStatusTimeout = 1;   // a bounded wait on a TMA barrier gave up
+constexpr long long kWaitCycles = 4000000000LL;  // ~2 s at 1.9 GHz
 
 // ---- scalar conversions -----------------------------------------------------------
 template <typename T> __device__ __forceinline__ float to_f(T x);
@@ -75,6 +81,47 @@ __device__ __forceinline__ void red_add_v2(float* p, float a, float b) {
   asm volatile("red.global.add.v2.f32 [%0], {%1,%2};" ::"l"(p), "f"(a), "f"(b) : "memory");
 }
 __device__ __forceinline__ void red_add(float* p, float a) { atomicAdd(p, a); }
+
+// ---- mbarrier / TMA (cp.async.bulk.tensor) helpers ---------------------------------------
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_fence_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Wait for the phase `parity` of an mbarrier, giving up after ~kWaitCycles.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const long long t0 = clock64();
+  while (!mbar_try_wait(bar, parity)) {
+    if (clock64() - t0 > kWaitCycles) return false;
+  }
+  return true;
+}
+// 3-D tiled TMA load global -> shared, completion counted on `bar`.
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, int x, int y, int z, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], "
+      "[%5];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar))
+      : "memory");
+}
 
 // Copy a (32 channels x kTile steps) tile of a (.., dim, seqlen) tensor into shared memory
 // as dst[channel][t] (row-major, no padding).  Rows >= nrows and steps >= tlen read as 0.
@@ -201,20 +248,25 @@ __device__ __forceinline__ void fold_tile(const float (&W)[16], float (&out)[PER
   }
 }
 
-// Kernel-side parameter blocks (host fills the derived fields).
+// Kernel-side parameter blocks (host fills the derived fields).  Tensor maps come first:
+// CUtensorMap is 64-byte aligned.
 struct FwdK {
+  CUtensorMap tm_u, tm_d, tm_z, tm_B, tm_C;  // valid when the kernel is launched with TMA
   ss_fwd_args a;
   int dpg;        // channels per group
   int tpg;        // 32-channel tiles per group
   int ntiles;     // ceil(seqlen / kTile)
   int vec_u, vec_d, vec_z, vec_out;
+  int* status;    // device status word (kStatus* bits), nullable
 };
 
 struct BwdK {
+  CUtensorMap tm_u, tm_d, tm_z, tm_g, tm_B, tm_C, tm_h;
   ss_bwd_args a;
   int dpg, tpg, ntiles;
   int vec_u, vec_d, vec_z, vec_dout, vec_du, vec_dd, vec_dz;
   int vec_dbc;    // dB/dC rows are 16-byte aligned (seqlen % 4 == 0)
+  int* status;
 };
 
 }  // namespace ssb

@@ -7,37 +7,59 @@
 //   out_t    = y_t * silu(z_t)   when z is given (modules/mamba_simple.py:143-146)
 //
 // CTA = (32 channels of one group, one batch row); lane = channel, warp w = states 4w..4w+3.
-// Per 16-step tile:
-//   1. u, delta, z tiles (32 x 16) and the variable B / C tiles (16 x dstate) are staged in
-//      shared memory with 16-byte vector loads (B and C once per CTA for all 32 channels);
-//   2. each element's delta' and delta'*u is computed once (one thread per element run)
-//      and stored as fp32;
-//   3. every lane advances its 4 states through the 16 steps in registers — one ex2, one
+// Inputs stream through a ring of kStages tile buffers in shared memory filled by TMA
+// (cp.async.bulk.tensor, one elected thread, completion on an mbarrier per stage), so
+// several 16-step tiles are in flight while the current one is computed.  Per tile:
+//   1. each element's delta' and delta'*u is computed once and stored as fp32; the B / C
+//      tiles (shared by all 32 channels) are widened to fp32 in [t][n] order;
+//   2. every lane advances its 4 states through the 16 steps in registers — one ex2, one
 //      FMUL, two FFMA per (element, state); the partial sum over its 4 states of C*h goes
 //      to shared memory;
-//   4. the warps' partial sums are added, D*u and the gate applied, and the tile stored.
+//   3. the warps' partial sums are added, D*u and the gate applied, and the tile stored;
+//   4. the freed ring slot is refilled with the tile kStages ahead.
 // At each tile end the 4 states of every lane go to the checkpoint buffer
 // ckpt[b][tile][n][c] (coalesced over channels); the last tile's entry is the final state.
+// When a tensor cannot be described by a TMA map (unaligned pointer or stride) the same
+// kernel loads each tile synchronously with vector or scalar loads instead (kTMA = false).
 #pragma once
 #include "ss_common.cuh"
 
 namespace ssb {
 
 template <typename IT, int kNW, bool kVarB, bool kVarC, bool kHasZ>
+struct FwdSmem {
+  static constexpr int NS = kSPW * kNW;
+  alignas(128) IT u[kStages][kCh][kTile];
+  alignas(128) IT d[kStages][kCh][kTile];
+  alignas(128) IT z[kHasZ ? kStages : 1][kCh][kTile];
+  alignas(128) float Braw[kVarB ? kStages : 1][NS * kTile];  // TMA tile of B (its own dtype)
+  alignas(128) float Craw[kVarC ? kStages : 1][NS * kTile];
+  alignas(16) float4 dt_s[kCh][4];
+  alignas(16) float4 dtu_s[kCh][4];
+  alignas(16) float B_s[kVarB ? kTile : 1][NS];
+  alignas(16) float C_s[kVarC ? kTile : 1][NS];
+  float y_s[kNW][kTile][kPad];
+  alignas(8) uint64_t full[kStages];
+};
+
+// widen a TMA'd [n][t] tile of B or C (dtype IT or fp32) into fp32 [t][n]
+template <typename IT, int NT, int NS>
+__device__ __forceinline__ void widen_bc(float (*dst)[NS], const float* raw, bool f32) {
+  for (int i = threadIdx.x; i < NS * kTile; i += NT) {
+    const int n = i / kTile, t = i % kTile;
+    dst[t][n] = f32 ? raw[i] : to_f<IT>(reinterpret_cast<const IT*>(raw)[i]);
+  }
+}
+
+template <typename IT, int kNW, bool kVarB, bool kVarC, bool kHasZ, bool kTMA>
 __global__ void __launch_bounds__(32 * kNW, 4) ss_fwd_kernel(const __grid_constant__ FwdK P) {
   constexpr int NT = 32 * kNW;
   constexpr int NS = kSPW * kNW;   // states covered by the CTA (dstate padded up)
   constexpr int S = kTile / kNW;   // steps per thread in the element-wise phases
+  using Sm = FwdSmem<IT, kNW, kVarB, kVarC, kHasZ>;
+  extern __shared__ __align__(128) unsigned char smem_raw[];
+  Sm& sm = *reinterpret_cast<Sm*>(smem_raw);
   const ss_fwd_args& a = P.a;
-
-  __shared__ __align__(16) IT u_raw[kCh][kTile];
-  __shared__ __align__(16) IT d_raw[kCh][kTile];
-  __shared__ __align__(16) IT z_raw[kHasZ ? kCh : 1][kTile];
-  __shared__ float4 dt_s[kCh][4];
-  __shared__ float4 dtu_s[kCh][4];
-  __shared__ __align__(16) float B_s[kVarB ? kTile : 1][NS];
-  __shared__ __align__(16) float C_s[kVarC ? kTile : 1][NS];
-  __shared__ float y_s[kNW][kTile][kPad];
 
   const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
   const int grp = blockIdx.x / P.tpg;
@@ -47,6 +69,7 @@ __global__ void __launch_bounds__(32 * kNW, 4) ss_fwd_kernel(const __grid_consta
   const int b = blockIdx.y;
   const int N = a.dstate, L = a.seqlen;
   const bool bc_f32 = a.bc_dtype == SS_F32;
+  const int ntiles = P.ntiles;
 
   // ---- scan role: channel c0 + lane, states kSPW*w + j
   const bool lane_ok = lane < nvalid;
@@ -70,30 +93,62 @@ __global__ void __launch_bounds__(32 * kNW, 4) ss_fwd_kernel(const __grid_consta
   const bool pc_ok = pc < nvalid;
   const float Dv = (a.D != nullptr && pc_ok) ? a.D[c0 + pc] : 0.f;
   const float bias = (a.delta_bias != nullptr && pc_ok) ? a.delta_bias[c0 + pc] : 0.f;
+  IT* orow = (IT*)a.out + (int64_t)b * a.out_batch_stride + (int64_t)(c0 + pc) * a.out_dim_stride;
+  const int64_t bc_off = ((int64_t)b * a.ngroups + grp) * N * (int64_t)L;
+
+  // ---- producer (thread 0): TMA ring
+  const uint32_t bc_bytes = NS * kTile * (bc_f32 ? 4u : (uint32_t)sizeof(IT));
+  const uint32_t stage_bytes = (2 + (kHasZ ? 1 : 0)) * kCh * kTile * (uint32_t)sizeof(IT) +
+                               ((kVarB ? 1 : 0) + (kVarC ? 1 : 0)) * bc_bytes;
+  auto issue = [&](int k, int s) {
+    uint64_t* bar = &sm.full[s];
+    mbar_expect_tx(bar, stage_bytes);
+    const int t0 = k * kTile;
+    tma_load_3d(&sm.u[s][0][0], &P.tm_u, t0, c0, b, bar);
+    tma_load_3d(&sm.d[s][0][0], &P.tm_d, t0, c0, b, bar);
+    if constexpr (kHasZ) tma_load_3d(&sm.z[s][0][0], &P.tm_z, t0, c0, b, bar);
+    if constexpr (kVarB) tma_load_3d(&sm.Braw[s][0], &P.tm_B, t0, 0, b * a.ngroups + grp, bar);
+    if constexpr (kVarC) tma_load_3d(&sm.Craw[s][0], &P.tm_C, t0, 0, b * a.ngroups + grp, bar);
+  };
+  if constexpr (kTMA) {
+    if (tid == 0) {
+      for (int s = 0; s < kStages; ++s) mbar_init(&sm.full[s], 1);
+      mbar_fence_init();
+    }
+    __syncthreads();
+    if (tid == 0)
+      for (int s = 0; s < kStages && s < ntiles; ++s) issue(s, s);
+  }
 
   const IT* ub = (const IT*)a.u + (int64_t)b * a.u_batch_stride + (int64_t)c0 * a.u_dim_stride;
   const IT* db = (const IT*)a.delta + (int64_t)b * a.delta_batch_stride + (int64_t)c0 * a.delta_dim_stride;
   const IT* zb = kHasZ ? (const IT*)a.z + (int64_t)b * a.z_batch_stride + (int64_t)c0 * a.z_dim_stride : nullptr;
-  IT* orow = (IT*)a.out + (int64_t)b * a.out_batch_stride + (int64_t)(c0 + pc) * a.out_dim_stride;
-  const int64_t bc_off = ((int64_t)b * a.ngroups + grp) * N * (int64_t)L;
 
-  for (int k = 0; k < P.ntiles; ++k) {
+  for (int k = 0; k < ntiles; ++k) {
     const int t0 = k * kTile;
     const int tlen = min(kTile, L - t0);
-    load_tile<IT, NT>(u_raw, ub + t0, a.u_dim_stride, nvalid, tlen, P.vec_u);
-    load_tile<IT, NT>(d_raw, db + t0, a.delta_dim_stride, nvalid, tlen, P.vec_d);
-    if constexpr (kHasZ) load_tile<IT, NT>(z_raw, zb + t0, a.z_dim_stride, nvalid, tlen, P.vec_z);
-    if constexpr (kVarB) {
-      if (bc_f32) load_bc_tile<float, NT, NS>(B_s, (const float*)a.B + bc_off + t0, L, N, tlen);
-      else load_bc_tile<IT, NT, NS>(B_s, (const IT*)a.B + bc_off + t0, L, N, tlen);
+    const int stg = kTMA ? k % kStages : 0;
+    bool failed = false;
+    if constexpr (kTMA) {
+      failed = !mbar_wait_bounded(&sm.full[stg], (k / kStages) & 1);
+      if constexpr (kVarB) widen_bc<IT, NT, NS>(sm.B_s, sm.Braw[stg], bc_f32);
+      if constexpr (kVarC) widen_bc<IT, NT, NS>(sm.C_s, sm.Craw[stg], bc_f32);
+    } else {
+      load_tile<IT, NT>(sm.u[0], ub + t0, a.u_dim_stride, nvalid, tlen, P.vec_u);
+      load_tile<IT, NT>(sm.d[0], db + t0, a.delta_dim_stride, nvalid, tlen, P.vec_d);
+      if constexpr (kHasZ) load_tile<IT, NT>(sm.z[0], zb + t0, a.z_dim_stride, nvalid, tlen, P.vec_z);
+      if constexpr (kVarB) {
+        if (bc_f32) load_bc_tile<float, NT, NS>(sm.B_s, (const float*)a.B + bc_off + t0, L, N, tlen);
+        else load_bc_tile<IT, NT, NS>(sm.B_s, (const IT*)a.B + bc_off + t0, L, N, tlen);
+      }
+      if constexpr (kVarC) {
+        if (bc_f32) load_bc_tile<float, NT, NS>(sm.C_s, (const float*)a.C + bc_off + t0, L, N, tlen);
+        else load_bc_tile<IT, NT, NS>(sm.C_s, (const IT*)a.C + bc_off + t0, L, N, tlen);
+      }
+      __syncthreads();
     }
-    if constexpr (kVarC) {
-      if (bc_f32) load_bc_tile<float, NT, NS>(C_s, (const float*)a.C + bc_off + t0, L, N, tlen);
-      else load_bc_tile<IT, NT, NS>(C_s, (const IT*)a.C + bc_off + t0, L, N, tlen);
-    }
-    __syncthreads();
 
-    // ---- 2. delta' and delta'*u, once per element (steps past seqlen get delta' = 0,
+    // ---- 1. delta' and delta'*u, once per element (steps past seqlen get delta' = 0,
     //         so the states pass through them unchanged)
     {
       float dtv[S], dtuv[S];
@@ -101,8 +156,8 @@ __global__ void __launch_bounds__(32 * kNW, 4) ss_fwd_kernel(const __grid_consta
       for (int i = 0; i < S; ++i) {
         const int t = pq * S + i;
         const bool ok = pc_ok && t < tlen;
-        const float uv = to_f<IT>(u_raw[pc][t]);
-        const float v = to_f<IT>(d_raw[pc][t]) + bias;
+        const float uv = to_f<IT>(sm.u[stg][pc][t]);
+        const float v = to_f<IT>(sm.d[stg][pc][t]) + bias;
         float dt = a.delta_softplus ? softplus_thr(v) : v;
         dt = ok ? dt : 0.f;
         dtv[i] = dt;
@@ -111,32 +166,41 @@ __global__ void __launch_bounds__(32 * kNW, 4) ss_fwd_kernel(const __grid_consta
 #pragma unroll
       for (int q = 0; q < S / 4; ++q) {
         const int ch = swz(pc, pq * (S / 4) + q);
-        dt_s[pc][ch] = make_float4(dtv[4 * q], dtv[4 * q + 1], dtv[4 * q + 2], dtv[4 * q + 3]);
-        dtu_s[pc][ch] = make_float4(dtuv[4 * q], dtuv[4 * q + 1], dtuv[4 * q + 2], dtuv[4 * q + 3]);
+        sm.dt_s[pc][ch] = make_float4(dtv[4 * q], dtv[4 * q + 1], dtv[4 * q + 2], dtv[4 * q + 3]);
+        sm.dtu_s[pc][ch] = make_float4(dtuv[4 * q], dtuv[4 * q + 1], dtuv[4 * q + 2], dtuv[4 * q + 3]);
       }
     }
-    __syncthreads();
+    if (__syncthreads_or(failed)) {
+      // a TMA stage never completed: report, let the copies in flight land, and leave
+      if (tid == 0) {
+        if (P.status != nullptr) atomicOr(P.status, kStatusTimeout);
+        for (int j = k + 1; j < ntiles && j < k + kStages; ++j)
+          mbar_wait_bounded(&sm.full[j % kStages], (j / kStages) & 1);
+      }
+      __syncthreads();
+      return;
+    }
 
-    // ---- 3. the recurrence, 4 states per lane, 16 steps
+    // ---- 2. the recurrence, 4 states per lane, 16 steps
 #pragma unroll
     for (int i4 = 0; i4 < 4; ++i4) {
-      const float4 dt4 = dt_s[lane][swz(lane, i4)];
-      const float4 du4 = dtu_s[lane][swz(lane, i4)];
+      const float4 dt4 = sm.dt_s[lane][swz(lane, i4)];
+      const float4 du4 = sm.dtu_s[lane][swz(lane, i4)];
       const float dts[4] = {dt4.x, dt4.y, dt4.z, dt4.w};
       const float dus[4] = {du4.x, du4.y, du4.z, du4.w};
 #pragma unroll
-      for (int s = 0; s < 4; ++s) {
-        const int t = 4 * i4 + s;
+      for (int st = 0; st < 4; ++st) {
+        const int t = 4 * i4 + st;
         float Bv[kSPW], Cv[kSPW];
         if constexpr (kVarB) {
-          const float4 q = *reinterpret_cast<const float4*>(&B_s[t][kSPW * w]);
+          const float4 q = *reinterpret_cast<const float4*>(&sm.B_s[t][kSPW * w]);
           Bv[0] = q.x; Bv[1] = q.y; Bv[2] = q.z; Bv[3] = q.w;
         } else {
 #pragma unroll
           for (int j = 0; j < kSPW; ++j) Bv[j] = Bc[j];
         }
         if constexpr (kVarC) {
-          const float4 q = *reinterpret_cast<const float4*>(&C_s[t][kSPW * w]);
+          const float4 q = *reinterpret_cast<const float4*>(&sm.C_s[t][kSPW * w]);
           Cv[0] = q.x; Cv[1] = q.y; Cv[2] = q.z; Cv[3] = q.w;
         } else {
 #pragma unroll
@@ -145,15 +209,15 @@ __global__ void __launch_bounds__(32 * kNW, 4) ss_fwd_kernel(const __grid_consta
         float yp = 0.f;
 #pragma unroll
         for (int j = 0; j < kSPW; ++j) {
-          const float da = ex2(dts[s] * A2[j]);
-          h[j] = fmaf(da, h[j], dus[s] * Bv[j]);
+          const float da = ex2(dts[st] * A2[j]);
+          h[j] = fmaf(da, h[j], dus[st] * Bv[j]);
           yp = fmaf(Cv[j], h[j], yp);
         }
-        y_s[w][t][lane] = yp;
+        sm.y_s[w][t][lane] = yp;
       }
     }
     if (a.ckpt != nullptr && lane_ok) {
-      float* ck = a.ckpt + ((int64_t)b * P.ntiles + k) * N * (int64_t)a.dim + c;
+      float* ck = a.ckpt + ((int64_t)b * ntiles + k) * N * (int64_t)a.dim + c;
 #pragma unroll
       for (int j = 0; j < kSPW; ++j) {
         const int n = kSPW * w + j;
@@ -162,17 +226,17 @@ __global__ void __launch_bounds__(32 * kNW, 4) ss_fwd_kernel(const __grid_consta
     }
     __syncthreads();
 
-    // ---- 4. combine the warps' partial sums, add D*u, gate, store
+    // ---- 3. combine the warps' partial sums, add D*u, gate, store
     {
       float yv[S];
 #pragma unroll
       for (int i = 0; i < S; ++i) {
         const int t = pq * S + i;
-        float y = Dv * to_f<IT>(u_raw[pc][t]);
+        float y = Dv * to_f<IT>(sm.u[stg][pc][t]);
 #pragma unroll
-        for (int g = 0; g < kNW; ++g) y += y_s[g][t][pc];
+        for (int g = 0; g < kNW; ++g) y += sm.y_s[g][t][pc];
         if constexpr (kHasZ) {
-          const float zv = to_f<IT>(z_raw[pc][t]);
+          const float zv = to_f<IT>(sm.z[stg][pc][t]);
           y *= zv * sigmoid_fast(zv);
         }
         yv[i] = y;
@@ -181,6 +245,10 @@ __global__ void __launch_bounds__(32 * kNW, 4) ss_fwd_kernel(const __grid_consta
       store_run<IT, S>(orow + t0 + pq * S, yv, nv, P.vec_out);
     }
     __syncthreads();
+    // ---- 4. refill the freed slot
+    if constexpr (kTMA) {
+      if (tid == 0 && k + kStages < ntiles) issue(k + kStages, stg);
+    }
   }
 
   if (a.last_state != nullptr && lane_ok) {
