@@ -40,6 +40,8 @@ extern "C" {
 
 #define SS_ABI_VERSION 1
 #define SS_MAX_DSTATE 16
+/* capacity (floats) of the library-held state array used by ss_bwd_noalloc: 16 MiB */
+#define SS_NOALLOC_MAX_CKPT_ELEMS 4194304
 
 #if defined(__GNUC__)
 #define SS_API __attribute__((visibility("default")))
@@ -114,6 +116,18 @@ SS_API int ss_fwd(const ss_fwd_args* args, void* stream);
 
 /* Backward scan: all input gradients from dout, using the forward's ckpt. */
 SS_API int ss_bwd(const ss_bwd_args* args, void* stream);
+
+/* Backward scan for callers that cannot allocate device memory (an FFI host without a
+ * CUDA allocator, a process whose device memory belongs to its own pool, any caller for
+ * which a cudaMalloc mid-step would fail or synchronise the device).  No counterpart in
+ * the reference.  It ignores args->f.ckpt: it recomputes the forward states into a
+ * state array held by the library (one per GPU that loads it, kept until exit) and runs
+ * the backward from there, calling no allocator.  Limits: ss_ckpt_elems(...) of the call
+ * must be <= SS_NOALLOC_MAX_CKPT_ELEMS, else SS_ERR_UNSUPPORTED.  The first call on a
+ * device looks up that array's address (do it before any stream capture).  All calls on a
+ * device share the array: calls that overlap on the GPU race.  du receives the recomputed
+ * forward output before the backward overwrites it, so du must not alias an input. */
+SS_API int ss_bwd_noalloc(const ss_bwd_args* args, void* stream);
 
 /* One decode step: state <- exp(dt'*A) state + dt'*x*B; out = (C.state + D x) [* silu(z)]. */
 SS_API int ss_step(const ss_step_args* args, void* stream);

@@ -66,7 +66,9 @@ class StepArgs(ctypes.Structure):
 
 
 EXPORTS = ("ss_fwd", "ss_bwd", "ss_step", "ss_ckpt_elems", "ss_status_string",
-           "ss_last_cuda_error", "ss_abi_version", "ss_struct_size", "ss_device_status")
+           "ss_last_cuda_error", "ss_abi_version", "ss_struct_size", "ss_device_status",
+           "ss_bwd_noalloc")
+NOALLOC_MAX_CKPT_ELEMS = 4194304  # SS_NOALLOC_MAX_CKPT_ELEMS
 
 _lib = None
 _lock = threading.Lock()
@@ -85,6 +87,8 @@ def lib():
                 L = ctypes.CDLL(LIB_PATH)
                 L.ss_fwd.argtypes = [ctypes.POINTER(FwdArgs), c_vp]
                 L.ss_bwd.argtypes = [ctypes.POINTER(BwdArgs), c_vp]
+                L.ss_bwd_noalloc.argtypes = [ctypes.POINTER(BwdArgs), c_vp]
+                L.ss_bwd_noalloc.restype = c_int
                 L.ss_step.argtypes = [ctypes.POINTER(StepArgs), c_vp]
                 for f in ("ss_fwd", "ss_bwd", "ss_step", "ss_last_cuda_error", "ss_abi_version"):
                     getattr(L, f).restype = c_int
