@@ -25,6 +25,7 @@
  *   D, delta_bias, dD, ddelta_bias         : (dim) fp32
  *   ckpt                                   : opaque fp32 buffer of ss_ckpt_elems() floats;
  *                                            written by ss_fwd, read by ss_bwd
+ *   out_y, y                               : (batch, dim, seqlen) ungated output, I/O dtype
  *   last_state                             : (batch, dim, dstate) fp32
  * Channel c uses group c / (dim / ngroups), as forward_kernel.cu:144 of the reference.
  */
@@ -38,7 +39,7 @@
 extern "C" {
 #endif
 
-#define SS_ABI_VERSION 1
+#define SS_ABI_VERSION 2
 #define SS_MAX_DSTATE 16
 /* capacity (floats) of the library-held state array used by ss_bwd_noalloc: 16 MiB */
 #define SS_NOALLOC_MAX_CKPT_ELEMS 4194304
@@ -75,6 +76,9 @@ typedef struct ss_fwd_args {
   void* out;         int64_t out_batch_stride, out_dim_stride; /* y or y * silu(z)        */
   float* ckpt;              /* nullable: skip the states the backward needs               */
   float* last_state;        /* nullable                                                   */
+  void* out_y;       int64_t out_y_batch_stride, out_y_dim_stride;
+                            /* nullable: the ungated y (D*u + C.h), which ss_bwd needs when
+                               z is given; written only when z is given                   */
 } ss_fwd_args;
 
 typedef struct ss_bwd_args {
@@ -84,6 +88,9 @@ typedef struct ss_bwd_args {
   void* du;          int64_t du_batch_stride, du_dim_stride;
   void* ddelta;      int64_t ddelta_batch_stride, ddelta_dim_stride;
   void* dz;          int64_t dz_batch_stride, dz_dim_stride;   /* required iff f.z       */
+  const void* y;     int64_t y_batch_stride, y_dim_stride;     /* required iff f.z: the
+                               forward's out_y (may alias dz: each element of y is read
+                               before the same element of dz is written)                 */
   float* dA;                /* overwritten (zeroed, then accumulated)                     */
   float* dB;                /* overwritten                                                */
   float* dC;                /* overwritten                                                */
@@ -125,8 +132,9 @@ SS_API int ss_bwd(const ss_bwd_args* args, void* stream);
  * the backward from there, calling no allocator.  Limits: ss_ckpt_elems(...) of the call
  * must be <= SS_NOALLOC_MAX_CKPT_ELEMS, else SS_ERR_UNSUPPORTED.  The first call on a
  * device looks up that array's address (do it before any stream capture).  All calls on a
- * device share the array: calls that overlap on the GPU race.  du receives the recomputed
- * forward output before the backward overwrites it, so du must not alias an input. */
+ * device share the array: calls that overlap on the GPU race.  du (and dz, with a gate)
+ * receive the recomputed forward outputs before the backward overwrites them, so they must
+ * not alias an input; args->y is ignored. */
 SS_API int ss_bwd_noalloc(const ss_bwd_args* args, void* stream);
 
 /* One decode step: state <- exp(dt'*A) state + dt'*x*B; out = (C.state + D x) [* silu(z)]. */

@@ -37,6 +37,7 @@ class FwdArgs(ctypes.Structure):
         ("delta_bias", c_vp),
         ("out", c_vp), ("out_batch_stride", c_i64), ("out_dim_stride", c_i64),
         ("ckpt", c_vp), ("last_state", c_vp),
+        ("out_y", c_vp), ("out_y_batch_stride", c_i64), ("out_y_dim_stride", c_i64),
     ]
 
 
@@ -47,6 +48,7 @@ class BwdArgs(ctypes.Structure):
         ("du", c_vp), ("du_batch_stride", c_i64), ("du_dim_stride", c_i64),
         ("ddelta", c_vp), ("ddelta_batch_stride", c_i64), ("ddelta_dim_stride", c_i64),
         ("dz", c_vp), ("dz_batch_stride", c_i64), ("dz_dim_stride", c_i64),
+        ("y", c_vp), ("y_batch_stride", c_i64), ("y_dim_stride", c_i64),
         ("dA", c_vp), ("dB", c_vp), ("dC", c_vp), ("dD", c_vp), ("ddelta_bias", c_vp),
     ]
 

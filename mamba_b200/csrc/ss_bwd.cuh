@@ -12,34 +12,47 @@
 //   dC_t[n]    += dy_t h_t[n]              (summed over the channels of the group)
 //   dz_t        = dout_t * y_t * silu'(z_t)
 //
-// Same CTA shape as the forward (lane = channel, warp = 4 states).  Tiles of 16 steps are
-// visited last to first.  For each tile a lane
+// Same CTA shape as the forward (lane = channel, warp = 4 states, handled as two pairs
+// with packed fp32x2 arithmetic).  Tiles of 16 steps are visited last to first.  Per tile a
+// lane
 //   * restarts its 4 states from the forward's checkpoint of the previous tile boundary,
-//   * runs the 16 forward steps keeping exp(delta'A) and h_{t-1} in registers (128 values),
+//   * runs the 16 forward steps keeping exp(delta'A) and h_{t-1} in registers,
 //   * runs the 16 reverse steps, carrying dh across tiles in registers,
-//   * reduces its dB / dC contributions over the warp's 32 channels with a butterfly
-//     transpose (each lane ends with 4 consecutive steps of one (B|C, n) row) and adds them
-//     to global memory with one 16-byte vector reduction per lane — instead of the
-//     reference's two fp32 atomics per element and state (backward_kernel.cu:466-478);
-//   * leaves the per-step sums over its states (for du, ddelta, dz) in shared memory, where
-//     the element phase combines the warps.
-// Inputs (u, delta, dout, z, the B / C tiles and the checkpointed states) stream through a
-// TMA ring of kStages tiles, as in the forward; kTMA = false loads each tile synchronously.
+//   * hands its dB / dC contributions to a per-warp shared-memory block every 4 steps; the
+//     warp then sums them over its 32 channels (each lane one (step, B|C, state-pair) row,
+//     16-byte reads) and, once per tile, adds 4 consecutive steps of one (B|C, n) row to
+//     global memory with a 16-byte vector reduction — instead of the reference's two fp32
+//     atomics per element and state (backward_kernel.cu:466-478);
+//   * leaves the per-step sums over its states (for du, ddelta) in shared memory, where the
+//     element phase combines the warps (dz uses the ungated y the forward saved).
+// Inputs (u, delta, dout, z, y, the B / C tiles and the checkpointed states) stream through
+// a TMA ring of kStagesBwd tiles; kTMA = false loads each tile synchronously.  Shared memory
+// is kept under ~72 KB (bf16) so that three CTAs fit on an SM next to their registers.
 #pragma once
 #include "ss_common.cuh"
+#include "ss_fwd.cuh"  // widen_bc
 
 namespace ssb {
+
+constexpr int kStagesBwd = 3;  // tiles in flight per CTA
+constexpr int kS12Row = 66;    // floats per row of the packed (S1, S2) partials (64 + 2 pad)
+
+// dB/dC fold block: 16 rows of 64 floats (32 lanes x float2); 16-byte unit q of row r is
+// stored at unit q ^ (2 * (r & 3)), which keeps both the per-row float2 writes and the
+// per-lane 16-byte reads of the reduction free of bank conflicts.
+__device__ __forceinline__ int fold_off(int r, int unit) { return r * 64 + 4 * (unit ^ (2 * (r & 3))); }
 
 template <typename IT, int kNW, bool kVarB, bool kVarC, bool kHasZ>
 struct BwdSmem {
   static constexpr int NS = kSPW * kNW;
-  alignas(128) IT u[kStages][kCh][kTile];
-  alignas(128) IT d[kStages][kCh][kTile];
-  alignas(128) IT g[kStages][kCh][kTile];
-  alignas(128) IT z[kHasZ ? kStages : 1][kCh][kTile];
-  alignas(128) float Braw[kVarB ? kStages : 1][NS * kTile];
-  alignas(128) float Craw[kVarC ? kStages : 1][NS * kTile];
-  alignas(128) float hck[kStages][NS][kCh];   // states at the tile start, [n][channel]
+  alignas(128) IT u[kStagesBwd][kCh][kTile];
+  alignas(128) IT d[kStagesBwd][kCh][kTile];
+  alignas(128) IT g[kStagesBwd][kCh][kTile];
+  alignas(128) IT z[kHasZ ? kStagesBwd : 1][kCh][kTile];
+  alignas(128) IT y[kHasZ ? kStagesBwd : 1][kCh][kTile];
+  alignas(128) IT Braw[kVarB ? kStagesBwd : 1][NS * kTile];  // TMA path: B / C have the I/O dtype
+  alignas(128) IT Craw[kVarC ? kStagesBwd : 1][NS * kTile];
+  alignas(128) float hck[kStagesBwd][NS][kCh];   // states at the tile start, [n][channel]
   alignas(16) float4 dt_s[kCh][4];
   alignas(16) float4 dtu_s[kCh][4];
   alignas(16) float4 dy_s[kCh][4];
@@ -47,18 +60,18 @@ struct BwdSmem {
   alignas(16) float4 gz_s[kHasZ ? kCh : 1][4];
   alignas(16) float B_s[kVarB ? kTile : 1][NS];
   alignas(16) float C_s[kVarC ? kTile : 1][NS];
-  float s1_s[kNW][kTile][kPad];
-  float s2_s[kNW][kTile][kPad];
-  float y_s[kHasZ ? kNW : 1][kTile][kPad];
-  alignas(8) uint64_t full[kStages];
+  alignas(16) float s12_s[kNW][kTile][kS12Row];                        // (S1, S2) per channel
+  alignas(16) float fold[(kVarB || kVarC) ? kNW : 1][16 * 64];         // 4 steps x 2 pairs x B|C
+  alignas(16) float fout[(kVarB || kVarC) ? kNW : 1][2][kSPW][kTile];  // [B|C][j][t] sums
+  alignas(8) uint64_t full[kStagesBwd];
 };
 
 template <typename IT, int kNW, bool kVarB, bool kVarC, bool kHasZ, bool kTMA>
-__global__ void __launch_bounds__(32 * kNW, 2) ss_bwd_kernel(const __grid_constant__ BwdK P) {
+__global__ void __launch_bounds__(32 * kNW, 3) ss_bwd_kernel(const __grid_constant__ BwdK P) {
   constexpr int NT = 32 * kNW;
   constexpr int NS = kSPW * kNW;
   constexpr int S = kTile / kNW;
-  constexpr int KV = (kVarB ? 64 : 0) + (kVarC ? 64 : 0);   // butterfly values per lane
+  constexpr bool kFold = kVarB || kVarC;
   using Sm = BwdSmem<IT, kNW, kVarB, kVarC, kHasZ>;
   extern __shared__ __align__(128) unsigned char smem_raw[];
   Sm& sm = *reinterpret_cast<Sm*>(smem_raw);
@@ -74,26 +87,29 @@ __global__ void __launch_bounds__(32 * kNW, 2) ss_bwd_kernel(const __grid_consta
   const int N = f.dstate, L = f.seqlen;
   const bool bc_f32 = f.bc_dtype == SS_F32;
 
-  // ---- scan role
+  // ---- scan role: channel c0 + lane, states 4w .. 4w+3 as pairs (4w, 4w+1), (4w+2, 4w+3)
   const bool lane_ok = lane < nvalid;
   const int c = c0 + lane;
-  float A2[kSPW], Ad[kSPW], Bc[kSPW], Cc[kSPW];
-  float dAacc[kSPW], e[kSPW], dBc[kSPW], dCc[kSPW];
+  float2 A2[2], Ad[2], Bc[2], Cc[2], dA2[2], e2[2], dBc[2], dCc[2];
 #pragma unroll
-  for (int j = 0; j < kSPW; ++j) {
-    const int n = kSPW * w + j;
-    const bool ok = lane_ok && n < N;
-    const int64_t ia = (int64_t)c * N + n;
-    Ad[j] = ok ? f.A[ia] : 0.f;
-    A2[j] = Ad[j] * kLog2e;
-    Bc[j] = 0.f;
-    Cc[j] = 0.f;
-    if (!kVarB && ok) Bc[j] = bc_f32 ? ((const float*)f.B)[ia] : to_f<IT>(((const IT*)f.B)[ia]);
-    if (!kVarC && ok) Cc[j] = bc_f32 ? ((const float*)f.C)[ia] : to_f<IT>(((const IT*)f.C)[ia]);
-    dAacc[j] = 0.f;
-    e[j] = 0.f;
-    dBc[j] = 0.f;
-    dCc[j] = 0.f;
+  for (int p = 0; p < 2; ++p) {
+    float av[2], bv[2], cv[2];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int n = kSPW * w + 2 * p + h;
+      const bool ok = lane_ok && n < N;
+      const int64_t ia = (int64_t)c * N + n;
+      av[h] = ok ? f.A[ia] : 0.f;
+      bv[h] = 0.f;
+      cv[h] = 0.f;
+      if (!kVarB && ok) bv[h] = bc_f32 ? ((const float*)f.B)[ia] : to_f<IT>(((const IT*)f.B)[ia]);
+      if (!kVarC && ok) cv[h] = bc_f32 ? ((const float*)f.C)[ia] : to_f<IT>(((const IT*)f.C)[ia]);
+    }
+    Ad[p] = make_float2(av[0], av[1]);
+    A2[p] = make_float2(av[0] * kLog2e, av[1] * kLog2e);
+    Bc[p] = make_float2(bv[0], bv[1]);
+    Cc[p] = make_float2(cv[0], cv[1]);
+    dA2[p] = e2[p] = dBc[p] = dCc[p] = make_float2(0.f, 0.f);
   }
 
   // ---- element role
@@ -107,6 +123,7 @@ __global__ void __launch_bounds__(32 * kNW, 2) ss_bwd_kernel(const __grid_consta
   const IT* db = (const IT*)f.delta + (int64_t)b * f.delta_batch_stride + (int64_t)c0 * f.delta_dim_stride;
   const IT* gb = (const IT*)a.dout + (int64_t)b * a.dout_batch_stride + (int64_t)c0 * a.dout_dim_stride;
   const IT* zb = kHasZ ? (const IT*)f.z + (int64_t)b * f.z_batch_stride + (int64_t)c0 * f.z_dim_stride : nullptr;
+  const IT* yb = kHasZ ? (const IT*)a.y + (int64_t)b * a.y_batch_stride + (int64_t)c0 * a.y_dim_stride : nullptr;
   IT* du_row = (IT*)a.du + (int64_t)b * a.du_batch_stride + (int64_t)(c0 + pc) * a.du_dim_stride;
   IT* dd_row = (IT*)a.ddelta + (int64_t)b * a.ddelta_batch_stride + (int64_t)(c0 + pc) * a.ddelta_dim_stride;
   IT* dz_row = kHasZ ? (IT*)a.dz + (int64_t)b * a.dz_batch_stride + (int64_t)(c0 + pc) * a.dz_dim_stride : nullptr;
@@ -114,52 +131,60 @@ __global__ void __launch_bounds__(32 * kNW, 2) ss_bwd_kernel(const __grid_consta
 
   const int ntiles = P.ntiles;
   const uint32_t io_bytes = kCh * kTile * (uint32_t)sizeof(IT);
-  const uint32_t bc_bytes = NS * kTile * (bc_f32 ? 4u : (uint32_t)sizeof(IT));
+  const uint32_t bc_bytes = NS * kTile * (uint32_t)sizeof(IT);
   const uint32_t h_bytes = NS * kCh * 4u;
   // iteration i handles tile ntiles-1-i
   auto issue = [&](int i, int s) {
     const int k = ntiles - 1 - i;
     uint64_t* bar = &sm.full[s];
-    const uint32_t bytes = (3 + (kHasZ ? 1 : 0)) * io_bytes + ((kVarB ? 1 : 0) + (kVarC ? 1 : 0)) * bc_bytes +
+    const uint32_t bytes = (3 + (kHasZ ? 2 : 0)) * io_bytes + ((kVarB ? 1 : 0) + (kVarC ? 1 : 0)) * bc_bytes +
                            (k > 0 ? h_bytes : 0u);
     mbar_expect_tx(bar, bytes);
     const int t0 = k * kTile;
     tma_load_3d(&sm.u[s][0][0], &P.tm_u, t0, c0, b, bar);
     tma_load_3d(&sm.d[s][0][0], &P.tm_d, t0, c0, b, bar);
     tma_load_3d(&sm.g[s][0][0], &P.tm_g, t0, c0, b, bar);
-    if constexpr (kHasZ) tma_load_3d(&sm.z[s][0][0], &P.tm_z, t0, c0, b, bar);
+    if constexpr (kHasZ) {
+      tma_load_3d(&sm.z[s][0][0], &P.tm_z, t0, c0, b, bar);
+      tma_load_3d(&sm.y[s][0][0], &P.tm_y, t0, c0, b, bar);
+    }
     if constexpr (kVarB) tma_load_3d(&sm.Braw[s][0], &P.tm_B, t0, 0, b * f.ngroups + grp, bar);
     if constexpr (kVarC) tma_load_3d(&sm.Craw[s][0], &P.tm_C, t0, 0, b * f.ngroups + grp, bar);
     if (k > 0) tma_load_3d(&sm.hck[s][0][0], &P.tm_h, c0, 0, b * ntiles + (k - 1), bar);
   };
   if constexpr (kTMA) {
     if (tid == 0) {
-      for (int s = 0; s < kStages; ++s) mbar_init(&sm.full[s], 1);
+      for (int s = 0; s < kStagesBwd; ++s) mbar_init(&sm.full[s], 1);
       mbar_fence_init();
     }
     __syncthreads();
     if (tid == 0)
-      for (int s = 0; s < kStages && s < ntiles; ++s) issue(s, s);
+      for (int s = 0; s < kStagesBwd && s < ntiles; ++s) issue(s, s);
   }
 
   for (int it = 0; it < ntiles; ++it) {
     const int k = ntiles - 1 - it;
     const int t0 = k * kTile;
     const int tlen = min(kTile, L - t0);
-    const int stg = kTMA ? it % kStages : 0;
+    const int stg = kTMA ? it % kStagesBwd : 0;
     bool failed = false;
-    float hp[kTile + 1][kSPW];
+    float2 hp[kTile + 1][2];
     if constexpr (kTMA) {
-      failed = !mbar_wait_bounded(&sm.full[stg], (it / kStages) & 1);
-      if constexpr (kVarB) widen_bc<IT, NT, NS>(sm.B_s, sm.Braw[stg], bc_f32);
-      if constexpr (kVarC) widen_bc<IT, NT, NS>(sm.C_s, sm.Craw[stg], bc_f32);
+      failed = !mbar_wait_bounded(&sm.full[stg], (it / kStagesBwd) & 1);
+      if constexpr (kVarB) widen_bc<IT, NT, NS>(sm.B_s, reinterpret_cast<const float*>(sm.Braw[stg]), false);
+      if constexpr (kVarC) widen_bc<IT, NT, NS>(sm.C_s, reinterpret_cast<const float*>(sm.Craw[stg]), false);
 #pragma unroll
-      for (int j = 0; j < kSPW; ++j) hp[0][j] = (k > 0) ? sm.hck[stg][kSPW * w + j][lane] : 0.f;
+      for (int p = 0; p < 2; ++p)
+        hp[0][p] = (k > 0) ? make_float2(sm.hck[stg][kSPW * w + 2 * p][lane], sm.hck[stg][kSPW * w + 2 * p + 1][lane])
+                           : make_float2(0.f, 0.f);
     } else {
       load_tile<IT, NT>(sm.u[0], ub + t0, f.u_dim_stride, nvalid, tlen, P.vec_u);
       load_tile<IT, NT>(sm.d[0], db + t0, f.delta_dim_stride, nvalid, tlen, P.vec_d);
       load_tile<IT, NT>(sm.g[0], gb + t0, a.dout_dim_stride, nvalid, tlen, P.vec_dout);
-      if constexpr (kHasZ) load_tile<IT, NT>(sm.z[0], zb + t0, f.z_dim_stride, nvalid, tlen, P.vec_z);
+      if constexpr (kHasZ) {
+        load_tile<IT, NT>(sm.z[0], zb + t0, f.z_dim_stride, nvalid, tlen, P.vec_z);
+        load_tile<IT, NT>(sm.y[0], yb + t0, a.y_dim_stride, nvalid, tlen, P.vec_y);
+      }
       if constexpr (kVarB) {
         if (bc_f32) load_bc_tile<float, NT, NS>(sm.B_s, (const float*)f.B + bc_off + t0, L, N, tlen);
         else load_bc_tile<IT, NT, NS>(sm.B_s, (const IT*)f.B + bc_off + t0, L, N, tlen);
@@ -170,44 +195,46 @@ __global__ void __launch_bounds__(32 * kNW, 2) ss_bwd_kernel(const __grid_consta
       }
       // states at the tile start (end of the previous tile), from the forward's checkpoints
 #pragma unroll
-      for (int j = 0; j < kSPW; ++j) {
-        const int n = kSPW * w + j;
-        hp[0][j] = (k > 0 && lane_ok && n < N)
-                       ? f.ckpt[(((int64_t)b * ntiles + (k - 1)) * N + n) * f.dim + c]
-                       : 0.f;
+      for (int p = 0; p < 2; ++p) {
+        float hv[2];
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int n = kSPW * w + 2 * p + h;
+          hv[h] = (k > 0 && lane_ok && n < N) ? f.ckpt[(((int64_t)b * ntiles + (k - 1)) * N + n) * f.dim + c] : 0.f;
+        }
+        hp[0][p] = make_float2(hv[0], hv[1]);
       }
       __syncthreads();
     }
 
     // ---- element phase 1: delta', delta'u, dy, softplus slope, gate slope
     {
+      float uv[S], dv[S], gv[S], zv[S];
+      lds_run<IT, S>(&sm.u[stg][pc][pq * S], uv);
+      lds_run<IT, S>(&sm.d[stg][pc][pq * S], dv);
+      lds_run<IT, S>(&sm.g[stg][pc][pq * S], gv);
+      if constexpr (kHasZ) lds_run<IT, S>(&sm.z[stg][pc][pq * S], zv);
       float dtv[S], dtuv[S], dyv[S], sgv[S], gzv[S];
 #pragma unroll
       for (int i = 0; i < S; ++i) {
         const int t = pq * S + i;
         const bool ok = pc_ok && t < tlen;
-        const float uv = to_f<IT>(sm.u[stg][pc][t]);
-        const float v = to_f<IT>(sm.d[stg][pc][t]) + bias;
+        const float v = dv[i] + bias;
         float dt = v, sg = 1.f;
-        if (f.delta_softplus && v <= 20.f) {
-          dt = log1pf(exp_fast(v));
-          sg = sigmoid_fast(v);
-        }
-        const float go = to_f<IT>(sm.g[stg][pc][t]);
-        float dy = go, gz = 0.f;
+        if (f.delta_softplus) softplus_and_slope(v, dt, sg);
+        float dy = gv[i], gz = 0.f;
         if constexpr (kHasZ) {
-          const float zv = to_f<IT>(sm.z[stg][pc][t]);
-          const float sz = sigmoid_fast(zv);
-          dy = go * zv * sz;
-          gz = go * sz * (1.f + zv * (1.f - sz));
+          const float sz = sigmoid_fast(zv[i]);
+          dy = gv[i] * zv[i] * sz;
+          gz = gv[i] * sz * fmaf(zv[i], 1.f - sz, 1.f);
         }
         if (!ok) {
           dt = 0.f;
           dy = 0.f;
         }
-        dD_acc = fmaf(dy, uv, dD_acc);
+        dD_acc = fmaf(dy, uv[i], dD_acc);
         dtv[i] = dt;
-        dtuv[i] = dt * uv;
+        dtuv[i] = dt * uv[i];
         dyv[i] = dy;
         sgv[i] = sg;
         gzv[i] = gz;
@@ -226,15 +253,15 @@ __global__ void __launch_bounds__(32 * kNW, 2) ss_bwd_kernel(const __grid_consta
     if (__syncthreads_or(failed)) {
       if (tid == 0) {
         if (P.status != nullptr) atomicOr(P.status, kStatusTimeout);
-        for (int j = it + 1; j < ntiles && j < it + kStages; ++j)
-          mbar_wait_bounded(&sm.full[j % kStages], (j / kStages) & 1);
+        for (int j = it + 1; j < ntiles && j < it + kStagesBwd; ++j)
+          mbar_wait_bounded(&sm.full[j % kStagesBwd], (j / kStagesBwd) & 1);
       }
       __syncthreads();
       return;
     }
 
     // ---- scan phase, forward: decays and states of the tile in registers
-    float da[kTile][kSPW];
+    float2 da[kTile][2];
 #pragma unroll
     for (int i4 = 0; i4 < 4; ++i4) {
       const float4 dt4 = sm.dt_s[lane][swz(lane, i4)];
@@ -242,42 +269,28 @@ __global__ void __launch_bounds__(32 * kNW, 2) ss_bwd_kernel(const __grid_consta
       const float dts[4] = {dt4.x, dt4.y, dt4.z, dt4.w};
       const float dus[4] = {du4.x, du4.y, du4.z, du4.w};
 #pragma unroll
-      for (int s = 0; s < 4; ++s) {
-        const int t = 4 * i4 + s;
-        float Bv[kSPW];
+      for (int st = 0; st < 4; ++st) {
+        const int t = 4 * i4 + st;
+        float2 Bv[2];
         if constexpr (kVarB) {
           const float4 q = *reinterpret_cast<const float4*>(&sm.B_s[t][kSPW * w]);
-          Bv[0] = q.x; Bv[1] = q.y; Bv[2] = q.z; Bv[3] = q.w;
+          Bv[0] = make_float2(q.x, q.y);
+          Bv[1] = make_float2(q.z, q.w);
         } else {
-#pragma unroll
-          for (int j = 0; j < kSPW; ++j) Bv[j] = Bc[j];
+          Bv[0] = Bc[0];
+          Bv[1] = Bc[1];
         }
 #pragma unroll
-        for (int j = 0; j < kSPW; ++j) {
-          da[t][j] = ex2(dts[s] * A2[j]);
-          hp[t + 1][j] = fmaf(da[t][j], hp[t][j], dus[s] * Bv[j]);
-        }
-        if constexpr (kHasZ) {
-          float Cv[kSPW];
-          if constexpr (kVarC) {
-            const float4 q = *reinterpret_cast<const float4*>(&sm.C_s[t][kSPW * w]);
-            Cv[0] = q.x; Cv[1] = q.y; Cv[2] = q.z; Cv[3] = q.w;
-          } else {
-#pragma unroll
-            for (int j = 0; j < kSPW; ++j) Cv[j] = Cc[j];
-          }
-          float yp = 0.f;
-#pragma unroll
-          for (int j = 0; j < kSPW; ++j) yp = fmaf(Cv[j], hp[t + 1][j], yp);
-          sm.y_s[w][t][lane] = yp;
+        for (int p = 0; p < 2; ++p) {
+          const float2 x = mul2(f2(dts[st]), A2[p]);
+          da[t][p] = make_float2(ex2(x.x), ex2(x.y));
+          hp[t + 1][p] = fma2(da[t][p], hp[t][p], mul2(f2(dus[st]), Bv[p]));
         }
       }
     }
 
-    // ---- scan phase, reverse.  The dB / dC contributions of each step are folded across
-    //      the warp's lanes right away (the first three butterfly stages pair values of the
-    //      same step), leaving one partial per lane and step in W[t].
-    float W[kTile];
+    // ---- scan phase, reverse
+    float* fold = kFold ? &sm.fold[w][0] : nullptr;
 #pragma unroll
     for (int i4 = 3; i4 >= 0; --i4) {
       const float4 dt4 = sm.dt_s[lane][swz(lane, i4)];
@@ -287,72 +300,99 @@ __global__ void __launch_bounds__(32 * kNW, 2) ss_bwd_kernel(const __grid_consta
       const float dus[4] = {du4.x, du4.y, du4.z, du4.w};
       const float dys[4] = {dy4.x, dy4.y, dy4.z, dy4.w};
 #pragma unroll
-      for (int s = 3; s >= 0; --s) {
-        const int t = 4 * i4 + s;
-        float Bv[kSPW], Cv[kSPW];
+      for (int st = 3; st >= 0; --st) {
+        const int t = 4 * i4 + st;
+        float2 Bv[2], Cv[2];
         if constexpr (kVarB) {
           const float4 q = *reinterpret_cast<const float4*>(&sm.B_s[t][kSPW * w]);
-          Bv[0] = q.x; Bv[1] = q.y; Bv[2] = q.z; Bv[3] = q.w;
+          Bv[0] = make_float2(q.x, q.y);
+          Bv[1] = make_float2(q.z, q.w);
         } else {
-#pragma unroll
-          for (int j = 0; j < kSPW; ++j) Bv[j] = Bc[j];
+          Bv[0] = Bc[0];
+          Bv[1] = Bc[1];
         }
         if constexpr (kVarC) {
           const float4 q = *reinterpret_cast<const float4*>(&sm.C_s[t][kSPW * w]);
-          Cv[0] = q.x; Cv[1] = q.y; Cv[2] = q.z; Cv[3] = q.w;
+          Cv[0] = make_float2(q.x, q.y);
+          Cv[1] = make_float2(q.z, q.w);
         } else {
-#pragma unroll
-          for (int j = 0; j < kSPW; ++j) Cv[j] = Cc[j];
+          Cv[0] = Cc[0];
+          Cv[1] = Cc[1];
         }
-        float s1 = 0.f, s2 = 0.f, vB[kSPW], vC[kSPW];
+        const float2 dy2 = f2(dys[st]), du2 = f2(dus[st]), dt2 = f2(dts[st]);
+        float2 s1 = make_float2(0.f, 0.f), s2 = make_float2(0.f, 0.f);
 #pragma unroll
-        for (int j = 0; j < kSPW; ++j) {
-          const float dh = fmaf(Cv[j], dys[s], e[j]);
-          const float ee = da[t][j] * dh;
-          const float g = ee * hp[t][j];
-          dAacc[j] = fmaf(dts[s], g, dAacc[j]);
-          s1 = fmaf(Ad[j], g, s1);
-          s2 = fmaf(Bv[j], dh, s2);
-          vB[j] = dh * dus[s];
-          vC[j] = dys[s] * hp[t + 1][j];
-          if constexpr (!kVarB) dBc[j] = fmaf(dh, dus[s], dBc[j]);
-          if constexpr (!kVarC) dCc[j] = fmaf(dys[s], hp[t + 1][j], dCc[j]);
-          e[j] = ee;
+        for (int p = 0; p < 2; ++p) {
+          const float2 dh = fma2(Cv[p], dy2, e2[p]);
+          const float2 ee = mul2(da[t][p], dh);
+          const float2 g = mul2(ee, hp[t][p]);
+          dA2[p] = fma2(dt2, g, dA2[p]);
+          s1 = fma2(Ad[p], g, s1);
+          s2 = fma2(Bv[p], dh, s2);
+          const float2 vB = mul2(dh, du2);
+          const float2 vC = mul2(dy2, hp[t + 1][p]);
+          if constexpr (kVarB)
+            *reinterpret_cast<float2*>(fold + fold_off((st * 2 + p) * 2 + 0, lane >> 1) + 2 * (lane & 1)) = vB;
+          else dBc[p] = add2(dBc[p], vB);
+          if constexpr (kVarC)
+            *reinterpret_cast<float2*>(fold + fold_off((st * 2 + p) * 2 + 1, lane >> 1) + 2 * (lane & 1)) = vC;
+          else dCc[p] = add2(dCc[p], vC);
+          e2[p] = ee;
         }
-        sm.s1_s[w][t][lane] = s1;
-        sm.s2_s[w][t][lane] = s2;
-        if constexpr (KV == 128) W[t] = fold_step_bc(vB, vC, lane);
-        else if constexpr (kVarB) W[t] = fold_step_one(vB, lane);
-        else if constexpr (kVarC) W[t] = fold_step_one(vC, lane);
+        *reinterpret_cast<float2*>(&sm.s12_s[w][t][2 * lane]) = make_float2(s1.x + s1.y, s2.x + s2.y);
+      }
+      if constexpr (kFold) {
+        // sum the warp's 32 channels: lane l owns row r = l >> 1 = (step, pair, B|C) and reads
+        // the float2 pairs of lanes 2(2m + h), 2(2m + h) + 1 for m = 0..7 (h = l & 1)
+        __syncwarp();
+        const int r = lane >> 1, h = lane & 1;
+        const int type = r & 1;
+        float2 acc = make_float2(0.f, 0.f);
+        if ((type == 0 && kVarB) || (type == 1 && kVarC)) {
+#pragma unroll
+          float2 part[4];
+#pragma unroll
+          for (int m = 0; m < 8; ++m) {
+            const float4 q = *reinterpret_cast<const float4*>(fold + fold_off(r, 2 * m + h));
+            const float2 s2q = add2(make_float2(q.x, q.y), make_float2(q.z, q.w));
+            part[m & 3] = (m < 4) ? s2q : add2(part[m & 3], s2q);
+          }
+          acc = add2(add2(part[0], part[1]), add2(part[2], part[3]));
+        }
+        acc.x += __shfl_xor_sync(0xffffffffu, acc.x, 1);
+        acc.y += __shfl_xor_sync(0xffffffffu, acc.y, 1);
+        const int st = r >> 2, p = (r >> 1) & 1;
+        sm.fout[w][type][2 * p + h][4 * i4 + st] = h ? acc.y : acc.x;
+        __syncwarp();
       }
     }
 
-    // ---- dB / dC of this tile: reduce over the warp's channels, one vector add per lane
-    if constexpr (KV > 0) {
-      float V[KV / 32];
-      fold_tile<KV / 32>(W, V, lane);
-      constexpr int PER = KV / 32;                 // 4 (both variable) or 2
-      const int type = (KV == 128) ? (lane >> 4) : (kVarB ? 0 : 1);
-      const int j = (KV == 128) ? ((lane >> 2) & 3) : (lane >> 3);
-      const int tt = (KV == 128) ? 4 * (lane & 3) : 2 * (lane & 7);
+    // ---- dB / dC of this tile: 4 consecutive steps of one (B|C, n) row per lane
+    if constexpr (kFold) {
+      const int type = lane >> 4, j = (lane >> 2) & 3, tt = 4 * (lane & 3);
       const int n = kSPW * w + j;
-      if (n < N) {
+      const bool want = (type == 0) ? kVarB : kVarC;
+      if (want && n < N) {
+        const float4 v = *reinterpret_cast<const float4*>(&sm.fout[w][type][j][tt]);
         float* dst = (type == 0 ? a.dB : a.dC) + bc_off + (int64_t)n * L + t0 + tt;
-        if (P.vec_dbc && tt + PER <= tlen) {
-          if constexpr (PER == 4) red_add_v4(dst, V[0], V[1], V[2], V[3]);
-          else red_add_v2(dst, V[0], V[1]);
+        if (P.vec_dbc && tt + 4 <= tlen) {
+          red_add_v4(dst, v.x, v.y, v.z, v.w);
         } else {
+          const float vv[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
-          for (int i = 0; i < PER; ++i)
-            if (tt + i < tlen) red_add(dst + i, V[i]);
+          for (int i = 0; i < 4; ++i)
+            if (tt + i < tlen) red_add(dst + i, vv[i]);
         }
       }
     }
-    // carry for the next (earlier) tile: e = exp(delta'_{t0} A) dh_{t0} is already in e[]
+    // carry for the next (earlier) tile: e = exp(delta'_{t0} A) dh_{t0} is already in e2[]
     __syncthreads();
 
     // ---- element phase 2: du, ddelta, dz
     {
+      float uv[S], yv[S];
+      lds_run<IT, S>(&sm.u[stg][pc][pq * S], uv);
+      if constexpr (kHasZ) lds_run<IT, S>(&sm.y[stg][pc][pq * S], yv);
       float duv[S], ddv[S], dzv[S];
 #pragma unroll
       for (int q = 0; q < S / 4; ++q) {
@@ -368,19 +408,14 @@ __global__ void __launch_bounds__(32 * kNW, 2) ss_bwd_kernel(const __grid_consta
         for (int r = 0; r < 4; ++r) {
           const int i = 4 * q + r;
           const int t = pq * S + i;
-          float S1 = 0.f, S2 = 0.f, yv = 0.f;
+          float2 S12 = make_float2(0.f, 0.f);
 #pragma unroll
-          for (int g = 0; g < kNW; ++g) {
-            S1 += sm.s1_s[g][t][pc];
-            S2 += sm.s2_s[g][t][pc];
-            if constexpr (kHasZ) yv += sm.y_s[g][t][pc];
-          }
-          const float uv = to_f<IT>(sm.u[stg][pc][t]);
-          duv[i] = fmaf(Dv, dys[r], dts[r] * S2);
-          const float dd = fmaf(uv, S2, S1) * sgs[r];
+          for (int g = 0; g < kNW; ++g) S12 = add2(S12, *reinterpret_cast<const float2*>(&sm.s12_s[g][t][2 * pc]));
+          duv[i] = fmaf(Dv, dys[r], dts[r] * S12.y);
+          const float dd = fmaf(uv[i], S12.y, S12.x) * sgs[r];
           ddv[i] = dd;
           if (pc_ok && t < tlen) db_acc += dd;
-          if constexpr (kHasZ) dzv[i] = gzs[r] * fmaf(Dv, uv, yv);
+          if constexpr (kHasZ) dzv[i] = gzs[r] * yv[i];
         }
       }
       const int nv = pc_ok ? max(0, min(S, tlen - pq * S)) : 0;
@@ -390,19 +425,23 @@ __global__ void __launch_bounds__(32 * kNW, 2) ss_bwd_kernel(const __grid_consta
     }
     __syncthreads();
     if constexpr (kTMA) {
-      if (tid == 0 && it + kStages < ntiles) issue(it + kStages, stg);
+      if (tid == 0 && it + kStagesBwd < ntiles) issue(it + kStagesBwd, stg);
     }
   }
 
   // ---- per-channel parameter gradients (summed over batch rows by the atomics)
 #pragma unroll
-  for (int j = 0; j < kSPW; ++j) {
-    const int n = kSPW * w + j;
-    if (lane_ok && n < N) {
-      const int64_t ia = (int64_t)c * N + n;
-      red_add(a.dA + ia, dAacc[j]);
-      if constexpr (!kVarB) red_add(a.dB + ia, dBc[j]);
-      if constexpr (!kVarC) red_add(a.dC + ia, dCc[j]);
+  for (int p = 0; p < 2; ++p) {
+    const float dAv[2] = {dA2[p].x, dA2[p].y}, dBv[2] = {dBc[p].x, dBc[p].y}, dCv[2] = {dCc[p].x, dCc[p].y};
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int n = kSPW * w + 2 * p + h;
+      if (lane_ok && n < N) {
+        const int64_t ia = (int64_t)c * N + n;
+        red_add(a.dA + ia, dAv[h]);
+        if constexpr (!kVarB) red_add(a.dB + ia, dBv[h]);
+        if constexpr (!kVarC) red_add(a.dC + ia, dCv[h]);
+      }
     }
   }
   // the kNW element-role threads of a channel are adjacent lanes

@@ -161,6 +161,7 @@ int ss_fwd(const ss_fwd_args* args, void* stream) {
   P.vec_d = rows16(args->delta, args->delta_batch_stride, args->delta_dim_stride, es);
   P.vec_z = args->z ? rows16(args->z, args->z_batch_stride, args->z_dim_stride, es) : 0;
   P.vec_out = rows16(args->out, args->out_batch_stride, args->out_dim_stride, es);
+  P.vec_y = args->out_y ? rows16(args->out_y, args->out_y_batch_stride, args->out_y_dim_stride, es) : 0;
   P.status = status_ptr();
   const ss_fwd_args& a = *args;
   bool tma = map_rows(&P.tm_u, a.u, a.io_dtype, a, a.u_batch_stride, a.u_dim_stride) &&
@@ -178,7 +179,7 @@ int ss_bwd(const ss_bwd_args* args, void* stream) {
   int rc = check_fwd(&f);
   if (rc != SS_OK) return rc;
   if (!args->dout || !args->du || !args->ddelta || !args->dA || !args->dB || !args->dC) return SS_ERR_INVALID;
-  if (f.z && !args->dz) return SS_ERR_INVALID;
+  if (f.z && (!args->dz || !args->y)) return SS_ERR_INVALID;
   if (!f.ckpt && f.seqlen > ssb::kTile && f.batch > 0) return SS_ERR_INVALID;
   cudaStream_t st = (cudaStream_t)stream;
   // accumulated outputs start from zero
@@ -204,15 +205,19 @@ int ss_bwd(const ss_bwd_args* args, void* stream) {
   P.vec_du = rows16(args->du, args->du_batch_stride, args->du_dim_stride, es);
   P.vec_dd = rows16(args->ddelta, args->ddelta_batch_stride, args->ddelta_dim_stride, es);
   P.vec_dz = f.z ? rows16(args->dz, args->dz_batch_stride, args->dz_dim_stride, es) : 0;
+  P.vec_y = f.z ? rows16(args->y, args->y_batch_stride, args->y_dim_stride, es) : 0;
   P.vec_dbc = (f.seqlen % 4) == 0 && (reinterpret_cast<uintptr_t>(args->dB) & 15) == 0 &&
               (reinterpret_cast<uintptr_t>(args->dC) & 15) == 0;
   P.status = status_ptr();
-  // the checkpoint tile starts at channel c0: TMA needs c0 * 4 bytes to be 16-byte aligned
-  bool tma = (f.ngroups == 1 || (P.dpg % 4) == 0) &&
+  // the checkpoint tile starts at channel c0: TMA needs c0 * 4 bytes to be 16-byte aligned;
+  // the TMA ring stages B / C in the I/O dtype
+  bool tma = (f.ngroups == 1 || (P.dpg % 4) == 0) && (f.bc_dtype == f.io_dtype || (!f.var_B && !f.var_C)) &&
              map_rows(&P.tm_u, f.u, f.io_dtype, f, f.u_batch_stride, f.u_dim_stride) &&
              map_rows(&P.tm_d, f.delta, f.io_dtype, f, f.delta_batch_stride, f.delta_dim_stride) &&
              map_rows(&P.tm_g, args->dout, f.io_dtype, f, args->dout_batch_stride, args->dout_dim_stride);
-  if (tma && f.z) tma = map_rows(&P.tm_z, f.z, f.io_dtype, f, f.z_batch_stride, f.z_dim_stride);
+  if (tma && f.z)
+    tma = map_rows(&P.tm_z, f.z, f.io_dtype, f, f.z_batch_stride, f.z_dim_stride) &&
+          map_rows(&P.tm_y, args->y, f.io_dtype, f, args->y_batch_stride, args->y_dim_stride);
   if (tma && f.var_B) tma = map_bc(&P.tm_B, f.B, f);
   if (tma && f.var_C) tma = map_bc(&P.tm_C, f.C, f);
   if (tma && f.ckpt) {

@@ -58,13 +58,66 @@ __device__ __forceinline__ float fast_rcp(float x) {
   asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
 }
+__device__ __forceinline__ float lg2_fast(float x) {
+  float y;
+  asm("lg2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
 // e^x via ex2 with a log2(e) prescale
 __device__ __forceinline__ float exp_fast(float x) { return ex2(x * kLog2e); }
 // 1 / (1 + e^-x)
 __device__ __forceinline__ float sigmoid_fast(float x) { return fast_rcp(1.f + exp_fast(-x)); }
+// log(1 + e) for e >= 0: the Taylor series e - e^2/2 + ... - e^6/6 below e = 1/16 (truncation
+// error < e^7/7, i.e. < 1e-8 relative), log2(1 + e) * ln 2 above (where 1 + e carries no
+// cancellation).  Replaces log1pf at a third of the instructions.
+__device__ __forceinline__ float log1p_pos(float e) {
+  float p = fmaf(e, -1.f / 6.f, 0.2f);
+  p = fmaf(e, p, -0.25f);
+  p = fmaf(e, p, 1.f / 3.f);
+  p = fmaf(e, p, -0.5f);
+  p = fmaf(e, p, 1.f);
+  const float small = e * p;
+  const float big = lg2_fast(1.f + e) * 0.69314718055994531f;
+  return e < 0.0625f ? small : big;
+}
 // delta' = softplus(v) with the reference's threshold (forward_kernel.cu:216-221):
-// log1p(exp(v)) for v <= 20, v otherwise.  log1pf keeps full precision for small e^v.
-__device__ __forceinline__ float softplus_thr(float v) { return v <= 20.f ? log1pf(exp_fast(v)) : v; }
+// log(1 + e^v) for v <= 20, v otherwise.
+__device__ __forceinline__ float softplus_thr(float v) { return v <= 20.f ? log1p_pos(exp_fast(v)) : v; }
+// softplus and its slope sigmoid(v) together (backward_kernel.cu:499-517): both from e = e^v
+__device__ __forceinline__ void softplus_and_slope(float v, float& sp, float& slope) {
+  const float e = exp_fast(v);
+  const bool lin = v > 20.f;
+  sp = lin ? v : log1p_pos(e);
+  slope = lin ? 1.f : e * fast_rcp(1.f + e);
+}
+
+// packed fp32x2 arithmetic (one instruction for two lanes of work on sm_100)
+__device__ __forceinline__ float2 f2(float a) { return make_float2(a, a); }
+__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) { return __ffma2_rn(a, b, c); }
+__device__ __forceinline__ float2 mul2(float2 a, float2 b) { return __fmul2_rn(a, b); }
+__device__ __forceinline__ float2 add2(float2 a, float2 b) { return __fadd2_rn(a, b); }
+
+// S consecutive shared-memory values of type T as floats (vector load when S*sizeof(T) is
+// 8 or 16 bytes; the caller guarantees that alignment)
+template <typename T, int S>
+__device__ __forceinline__ void lds_run(const T* p, float (&v)[S]) {
+  constexpr int BYTES = S * (int)sizeof(T);
+  if constexpr (BYTES % 16 == 0 || BYTES == 8) {
+    constexpr int CH = (BYTES % 16 == 0) ? 16 : 8;
+    constexpr int PER = CH / (int)sizeof(T);
+#pragma unroll
+    for (int i = 0; i < S; i += PER) {
+      union { uint4 q; uint2 d; T e[PER]; } u;
+      if constexpr (CH == 16) u.q = *reinterpret_cast<const uint4*>(p + i);
+      else u.d = *reinterpret_cast<const uint2*>(p + i);
+#pragma unroll
+      for (int k = 0; k < PER; ++k) v[i + k] = to_f<T>(u.e[k]);
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < S; ++i) v[i] = to_f<T>(p[i]);
+  }
+}
 
 // ---- memory helpers -------------------------------------------------------------------
 __device__ __forceinline__ uint4 ld_stream16(const void* p) {
@@ -256,15 +309,15 @@ struct FwdK {
   int dpg;        // channels per group
   int tpg;        // 32-channel tiles per group
   int ntiles;     // ceil(seqlen / kTile)
-  int vec_u, vec_d, vec_z, vec_out;
+  int vec_u, vec_d, vec_z, vec_out, vec_y;
   int* status;    // device status word (kStatus* bits), nullable
 };
 
 struct BwdK {
-  CUtensorMap tm_u, tm_d, tm_z, tm_g, tm_B, tm_C, tm_h;
+  CUtensorMap tm_u, tm_d, tm_z, tm_g, tm_y, tm_B, tm_C, tm_h;
   ss_bwd_args a;
   int dpg, tpg, ntiles;
-  int vec_u, vec_d, vec_z, vec_dout, vec_du, vec_dd, vec_dz;
+  int vec_u, vec_d, vec_z, vec_dout, vec_du, vec_dd, vec_dz, vec_y;
   int vec_dbc;    // dB/dC rows are 16-byte aligned (seqlen % 4 == 0)
   int* status;
 };

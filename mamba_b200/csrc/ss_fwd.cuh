@@ -74,18 +74,25 @@ __global__ void __launch_bounds__(32 * kNW, 4) ss_fwd_kernel(const __grid_consta
   // ---- scan role: channel c0 + lane, states kSPW*w + j
   const bool lane_ok = lane < nvalid;
   const int c = c0 + lane;
-  float A2[kSPW], Bc[kSPW], Cc[kSPW], h[kSPW];
+  float2 A2[2], Bc[2], Cc[2], h[2];   // states (4w, 4w+1), (4w+2, 4w+3) as packed pairs
 #pragma unroll
-  for (int j = 0; j < kSPW; ++j) {
-    const int n = kSPW * w + j;
-    const bool ok = lane_ok && n < N;
-    const int64_t ia = (int64_t)c * N + n;
-    A2[j] = ok ? a.A[ia] * kLog2e : 0.f;
-    Bc[j] = 0.f;
-    Cc[j] = 0.f;
-    if (!kVarB && ok) Bc[j] = bc_f32 ? ((const float*)a.B)[ia] : to_f<IT>(((const IT*)a.B)[ia]);
-    if (!kVarC && ok) Cc[j] = bc_f32 ? ((const float*)a.C)[ia] : to_f<IT>(((const IT*)a.C)[ia]);
-    h[j] = 0.f;
+  for (int p = 0; p < 2; ++p) {
+    float av[2], bv[2], cv[2];
+#pragma unroll
+    for (int q = 0; q < 2; ++q) {
+      const int n = kSPW * w + 2 * p + q;
+      const bool ok = lane_ok && n < N;
+      const int64_t ia = (int64_t)c * N + n;
+      av[q] = ok ? a.A[ia] * kLog2e : 0.f;
+      bv[q] = 0.f;
+      cv[q] = 0.f;
+      if (!kVarB && ok) bv[q] = bc_f32 ? ((const float*)a.B)[ia] : to_f<IT>(((const IT*)a.B)[ia]);
+      if (!kVarC && ok) cv[q] = bc_f32 ? ((const float*)a.C)[ia] : to_f<IT>(((const IT*)a.C)[ia]);
+    }
+    A2[p] = make_float2(av[0], av[1]);
+    Bc[p] = make_float2(bv[0], bv[1]);
+    Cc[p] = make_float2(cv[0], cv[1]);
+    h[p] = make_float2(0.f, 0.f);
   }
 
   // ---- element role: channel c0 + pc, steps pq*S .. pq*S + S - 1 of each tile
@@ -94,6 +101,9 @@ __global__ void __launch_bounds__(32 * kNW, 4) ss_fwd_kernel(const __grid_consta
   const float Dv = (a.D != nullptr && pc_ok) ? a.D[c0 + pc] : 0.f;
   const float bias = (a.delta_bias != nullptr && pc_ok) ? a.delta_bias[c0 + pc] : 0.f;
   IT* orow = (IT*)a.out + (int64_t)b * a.out_batch_stride + (int64_t)(c0 + pc) * a.out_dim_stride;
+  IT* yrow = (kHasZ && a.out_y != nullptr)
+                 ? (IT*)a.out_y + (int64_t)b * a.out_y_batch_stride + (int64_t)(c0 + pc) * a.out_y_dim_stride
+                 : nullptr;
   const int64_t bc_off = ((int64_t)b * a.ngroups + grp) * N * (int64_t)L;
 
   // ---- producer (thread 0): TMA ring
@@ -151,17 +161,18 @@ __global__ void __launch_bounds__(32 * kNW, 4) ss_fwd_kernel(const __grid_consta
     // ---- 1. delta' and delta'*u, once per element (steps past seqlen get delta' = 0,
     //         so the states pass through them unchanged)
     {
-      float dtv[S], dtuv[S];
+      float uv[S], dv[S], dtv[S], dtuv[S];
+      lds_run<IT, S>(&sm.u[stg][pc][pq * S], uv);
+      lds_run<IT, S>(&sm.d[stg][pc][pq * S], dv);
 #pragma unroll
       for (int i = 0; i < S; ++i) {
         const int t = pq * S + i;
         const bool ok = pc_ok && t < tlen;
-        const float uv = to_f<IT>(sm.u[stg][pc][t]);
-        const float v = to_f<IT>(sm.d[stg][pc][t]) + bias;
+        const float v = dv[i] + bias;
         float dt = a.delta_softplus ? softplus_thr(v) : v;
         dt = ok ? dt : 0.f;
         dtv[i] = dt;
-        dtuv[i] = dt * uv;
+        dtuv[i] = dt * uv[i];
       }
 #pragma unroll
       for (int q = 0; q < S / 4; ++q) {
@@ -191,58 +202,64 @@ __global__ void __launch_bounds__(32 * kNW, 4) ss_fwd_kernel(const __grid_consta
 #pragma unroll
       for (int st = 0; st < 4; ++st) {
         const int t = 4 * i4 + st;
-        float Bv[kSPW], Cv[kSPW];
+        float2 Bv[2], Cv[2];
         if constexpr (kVarB) {
           const float4 q = *reinterpret_cast<const float4*>(&sm.B_s[t][kSPW * w]);
-          Bv[0] = q.x; Bv[1] = q.y; Bv[2] = q.z; Bv[3] = q.w;
+          Bv[0] = make_float2(q.x, q.y);
+          Bv[1] = make_float2(q.z, q.w);
         } else {
-#pragma unroll
-          for (int j = 0; j < kSPW; ++j) Bv[j] = Bc[j];
+          Bv[0] = Bc[0];
+          Bv[1] = Bc[1];
         }
         if constexpr (kVarC) {
           const float4 q = *reinterpret_cast<const float4*>(&sm.C_s[t][kSPW * w]);
-          Cv[0] = q.x; Cv[1] = q.y; Cv[2] = q.z; Cv[3] = q.w;
+          Cv[0] = make_float2(q.x, q.y);
+          Cv[1] = make_float2(q.z, q.w);
         } else {
-#pragma unroll
-          for (int j = 0; j < kSPW; ++j) Cv[j] = Cc[j];
+          Cv[0] = Cc[0];
+          Cv[1] = Cc[1];
         }
-        float yp = 0.f;
 #pragma unroll
-        for (int j = 0; j < kSPW; ++j) {
-          const float da = ex2(dts[st] * A2[j]);
-          h[j] = fmaf(da, h[j], dus[st] * Bv[j]);
-          yp = fmaf(Cv[j], h[j], yp);
+        for (int p = 0; p < 2; ++p) {
+          const float2 x = mul2(f2(dts[st]), A2[p]);
+          h[p] = fma2(make_float2(ex2(x.x), ex2(x.y)), h[p], mul2(f2(dus[st]), Bv[p]));
         }
+        const float2 y2 = fma2(Cv[1], h[1], mul2(Cv[0], h[0]));
+        const float yp = y2.x + y2.y;
         sm.y_s[w][t][lane] = yp;
       }
     }
     if (a.ckpt != nullptr && lane_ok) {
       float* ck = a.ckpt + ((int64_t)b * ntiles + k) * N * (int64_t)a.dim + c;
+      const float hv[kSPW] = {h[0].x, h[0].y, h[1].x, h[1].y};
 #pragma unroll
       for (int j = 0; j < kSPW; ++j) {
         const int n = kSPW * w + j;
-        if (n < N) ck[(int64_t)n * a.dim] = h[j];
+        if (n < N) ck[(int64_t)n * a.dim] = hv[j];
       }
     }
     __syncthreads();
 
     // ---- 3. combine the warps' partial sums, add D*u, gate, store
     {
-      float yv[S];
+      float yv[S], uo[S], zo[S], yu[S];
+      lds_run<IT, S>(&sm.u[stg][pc][pq * S], uo);
+      if constexpr (kHasZ) lds_run<IT, S>(&sm.z[stg][pc][pq * S], zo);
 #pragma unroll
       for (int i = 0; i < S; ++i) {
         const int t = pq * S + i;
-        float y = Dv * to_f<IT>(sm.u[stg][pc][t]);
+        float y = Dv * uo[i];
 #pragma unroll
         for (int g = 0; g < kNW; ++g) y += sm.y_s[g][t][pc];
+        yu[i] = y;
         if constexpr (kHasZ) {
-          const float zv = to_f<IT>(sm.z[stg][pc][t]);
-          y *= zv * sigmoid_fast(zv);
+          y *= zo[i] * sigmoid_fast(zo[i]);
         }
         yv[i] = y;
       }
       const int nv = pc_ok ? max(0, min(S, tlen - pq * S)) : 0;
       store_run<IT, S>(orow + t0 + pq * S, yv, nv, P.vec_out);
+      if (kHasZ && yrow != nullptr) store_run<IT, S>(yrow + t0 + pq * S, yu, nv, P.vec_y);
     }
     __syncthreads();
     // ---- 4. refill the freed slot
@@ -253,10 +270,11 @@ __global__ void __launch_bounds__(32 * kNW, 4) ss_fwd_kernel(const __grid_consta
 
   if (a.last_state != nullptr && lane_ok) {
     float* ls = a.last_state + ((int64_t)b * a.dim + c) * N;
+    const float hv[kSPW] = {h[0].x, h[0].y, h[1].x, h[1].y};
 #pragma unroll
     for (int j = 0; j < kSPW; ++j) {
       const int n = kSPW * w + j;
-      if (n < N) ls[n] = h[j];
+      if (n < N) ls[n] = hv[j];
     }
   }
 }

@@ -19,8 +19,8 @@
 //     work overlaps on the GPU (other streams, other threads) race and must be serialised by
 //     the caller; nothing in the array needs clearing, the recomputation overwrites every
 //     element the backward reads;
-//   * du is used as the destination of the recomputed forward output before the backward
-//     overwrites it, so it must not alias any input.
+//   * du (and dz, with a gate) receive the recomputed forward outputs before the backward
+//     overwrites them, so they must not alias any input.
 #include <cuda_runtime.h>
 
 #include <mutex>
@@ -66,18 +66,25 @@ extern "C" SS_API int ss_bwd_noalloc(const ss_bwd_args* args, void* stream) {
   int rc = scratch_for_current_device(&scratch);
   if (rc != SS_OK) return rc;
 
-  // 1. recompute the states into the scratch array (the forward output lands in du)
+  // 1. recompute the states into the scratch array; the forward output lands in du and,
+  //    with a gate, the ungated output the backward needs lands in dz
   ss_fwd_args fa = f;
   fa.out = args->du;
   fa.out_batch_stride = args->du_batch_stride;
   fa.out_dim_stride = args->du_dim_stride;
   fa.ckpt = scratch;
   fa.last_state = nullptr;
+  fa.out_y = f.z ? args->dz : nullptr;
+  fa.out_y_batch_stride = args->dz_batch_stride;
+  fa.out_y_dim_stride = args->dz_dim_stride;
   rc = ss_fwd(&fa, stream);
   if (rc != SS_OK) return rc;
 
-  // 2. the backward from those states
+  // 2. the backward from those states (each element of y is read before dz overwrites it)
   ss_bwd_args ba = *args;
   ba.f.ckpt = scratch;
+  ba.y = fa.out_y;
+  ba.y_batch_stride = args->dz_batch_stride;
+  ba.y_dim_stride = args->dz_dim_stride;
   return ss_bwd(&ba, stream);
 }

@@ -24,7 +24,7 @@ from .selective_scan_interface import _Prepared, scan_backward, scan_forward
 
 def forward(u, delta, A, B, C, D=None, delta_bias=None, use_delta_softplus=True):
     p = _Prepared(u, delta, A, B, C, D, None, delta_bias, use_delta_softplus)
-    out, x, _ = scan_forward(p, True, False)
+    out, x, _, _ = scan_forward(p, True, False)
     if out.dtype != delta.dtype:  # the reference allocates out like delta
         out = out.to(delta.dtype)
     return [out, x]

@@ -102,7 +102,7 @@ class _Prepared:
         self.b, self.d, self.l, self.n = b, d, l, n
         self.io = io
 
-    def fwd_args(self, out, ckpt=None, last=None):
+    def fwd_args(self, out, ckpt=None, last=None, out_y=None):
         u, dl, z = self.u, self.delta, self.z
         return L.FwdArgs(
             self.b, self.d, self.l, self.n, self.ngroups, self.var_B, self.var_C, self.softplus,
@@ -113,7 +113,9 @@ class _Prepared:
             L.ptr(z), z.stride(0) if z is not None else 0, z.stride(1) if z is not None else 0,
             L.ptr(self.delta_bias),
             out.data_ptr(), out.stride(0), out.stride(1),
-            L.ptr(ckpt), L.ptr(last))
+            L.ptr(ckpt), L.ptr(last),
+            L.ptr(out_y), out_y.stride(0) if out_y is not None else 0,
+            out_y.stride(1) if out_y is not None else 0)
 
 
 def _new_ckpt(p: _Prepared):
@@ -121,21 +123,25 @@ def _new_ckpt(p: _Prepared):
 
 
 def scan_forward(p: _Prepared, want_ckpt: bool, want_last: bool):
-    """Run the native forward.  Returns (out, ckpt | None, last_state | None)."""
+    """Run the native forward.  Returns (out, ckpt | None, last_state | None, y | None):
+    with want_ckpt the state buffer the backward needs and, when there is a gate z, the
+    ungated output y it needs as well."""
     out = torch.empty((p.b, p.d, p.l), dtype=p.io, device=p.device)
     ckpt = _new_ckpt(p) if want_ckpt else None
+    y = torch.empty_like(out) if (want_ckpt and p.z is not None) else None
     last = torch.empty((p.b, p.d, p.n), dtype=torch.float32, device=p.device) if want_last else None
-    args = p.fwd_args(out, ckpt, last)
+    args = p.fwd_args(out, ckpt, last, y)
     with torch.cuda.device(p.device):
         L.check(L.lib().ss_fwd(args, L.stream_of(p.device)), "ss_fwd")
-    return out, ckpt, last
+    return out, ckpt, last, y
 
 
-def scan_backward(p: _Prepared, dout, ckpt):
+def scan_backward(p: _Prepared, dout, ckpt, y=None):
     """Run the native backward.  Returns (du, ddelta, dA, dB, dC, dD, dz, ddelta_bias) with
-    fp32 dA / dB / dC / dD / ddelta_bias shaped like the normalised operands."""
-    if ckpt is None:  # the forward's states were not kept: recompute them
-        _, ckpt, _ = scan_forward(p, True, False)
+    fp32 dA / dB / dC / dD / ddelta_bias shaped like the normalised operands.  ckpt (and y
+    when there is a gate) come from scan_forward; without them the forward is recomputed."""
+    if ckpt is None or (p.z is not None and y is None):  # not kept: recompute
+        _, ckpt, _, y = scan_forward(p, True, False)
     dout = _rows(dout if dout.dtype == p.io else dout.to(p.io))
     if dout.shape != p.u.shape:
         raise ValueError("dout must have the shape of u")
@@ -155,6 +161,7 @@ def scan_backward(p: _Prepared, dout, ckpt):
         du.data_ptr(), du.stride(0), du.stride(1),
         ddelta.data_ptr(), ddelta.stride(0), ddelta.stride(1),
         L.ptr(dz), dz.stride(0) if dz is not None else 0, dz.stride(1) if dz is not None else 0,
+        L.ptr(y), y.stride(0) if y is not None else 0, y.stride(1) if y is not None else 0,
         dA.data_ptr(), dB.data_ptr(), dC.data_ptr(), L.ptr(dD), L.ptr(dbias))
     with torch.cuda.device(dev):
         L.check(L.lib().ss_bwd(args, L.stream_of(dev)), "ss_bwd")
@@ -175,13 +182,13 @@ class SelectiveScanFn(torch.autograd.Function):
                 return_last_state=False):
         p = _Prepared(u, delta, A, B, C, D, z, delta_bias, delta_softplus)
         need_grad = any(ctx.needs_input_grad[:8])
-        out, ckpt, last = scan_forward(p, need_grad, return_last_state)
+        out, ckpt, last, y = scan_forward(p, need_grad, return_last_state)
         ctx.delta_softplus = delta_softplus
         ctx.shapes = (B.shape, C.shape)
         ctx.dtypes = (u.dtype, delta.dtype, A.dtype, B.dtype, C.dtype,
                       None if D is None else D.dtype, None if z is None else z.dtype,
                       None if delta_bias is None else delta_bias.dtype)
-        ctx.save_for_backward(u, delta, A, B, C, D, z, delta_bias, ckpt)
+        ctx.save_for_backward(u, delta, A, B, C, D, z, delta_bias, ckpt, y)
         if return_last_state:
             ctx.mark_non_differentiable(last)
             return out, last
@@ -189,9 +196,9 @@ class SelectiveScanFn(torch.autograd.Function):
 
     @staticmethod
     def backward(ctx, dout, *unused):
-        u, delta, A, B, C, D, z, delta_bias, ckpt = ctx.saved_tensors
+        u, delta, A, B, C, D, z, delta_bias, ckpt, y = ctx.saved_tensors
         p = _Prepared(u, delta, A, B, C, D, z, delta_bias, ctx.delta_softplus)
-        du, ddelta, dA, dB, dC, dD, dz, dbias = scan_backward(p, dout, ckpt)
+        du, ddelta, dA, dB, dC, dD, dz, dbias = scan_backward(p, dout, ckpt, y)
         tu, tdl, tA, tB, tC, tD, tz, tbias = ctx.dtypes
         dB = dB.reshape(ctx.shapes[0]).to(tB)
         dC = dC.reshape(ctx.shapes[1]).to(tC)

@@ -33,7 +33,7 @@ def test_library_exports_every_declared_symbol():
 
 def test_abi_version_and_struct_layout():
     lib = L.lib()
-    assert lib.ss_abi_version() == 1
+    assert lib.ss_abi_version() == 2
     for i, st in enumerate((L.FwdArgs, L.BwdArgs, L.StepArgs)):
         assert lib.ss_struct_size(i) == ctypes.sizeof(st)
     assert lib.ss_struct_size(7) == 0
@@ -92,6 +92,9 @@ def test_bwd_validation():
         setattr(b, f, 0x1000)
     b.f.z = 0x1000
     assert lib.ss_bwd(ctypes.byref(b), None) == L.SS_ERR_INVALID  # z given, dz missing
+    b.dz = 0x1000
+    assert lib.ss_bwd(ctypes.byref(b), None) == L.SS_ERR_INVALID  # z given, y missing
+    b.dz = None
     b.f.z = None
     assert lib.ss_bwd(ctypes.byref(b), None) == L.SS_ERR_INVALID  # 128 steps need the checkpoints
     assert lib.ss_bwd(None, None) == L.SS_ERR_INVALID

@@ -32,9 +32,9 @@ def ref_pkg(monkeypatch):
 
     def fake_forward(p, want_ckpt, want_last):
         out = O.selective_scan_ref(p.u, p.delta, p.A, p.B, p.C, p.D, p.z, p.delta_bias, bool(p.softplus))
-        return torch.from_numpy(out).to(p.io), torch.zeros(1), None
+        return torch.from_numpy(out).to(p.io), torch.zeros(1), None, None
 
-    def fake_backward(p, dout, ckpt):
+    def fake_backward(p, dout, ckpt, y=None):
         g = O.selective_scan_ref_bwd(p.u, p.delta, p.A, p.B, p.C, p.D, p.z, p.delta_bias, bool(p.softplus), dout)
         t = lambda k: None if g[k] is None else torch.from_numpy(g[k])
         return (t("du").to(p.io), t("ddelta").to(p.io), t("dA"), t("dB"), t("dC"), t("dD"), t("dz"),

@@ -21,7 +21,7 @@ import mamba_b200._lib as L
 from common import TOL, assert_close, make_inputs, to_dev
 
 
-def _args(inp, out_bufs, ckpt):
+def _args(inp, out_bufs, ckpt, y=None):
     from mamba_b200.selective_scan_interface import _Prepared
 
     p = _Prepared(inp["u"], inp["delta"], inp["A"], inp["B"], inp["C"], inp["D"], inp["z"], inp["delta_bias"],
@@ -34,6 +34,7 @@ def _args(inp, out_bufs, ckpt):
         du.data_ptr(), du.stride(0), du.stride(1),
         dd.data_ptr(), dd.stride(0), dd.stride(1),
         L.ptr(dz), dz.stride(0) if dz is not None else 0, dz.stride(1) if dz is not None else 0,
+        L.ptr(y), y.stride(0) if y is not None else 0, y.stride(1) if y is not None else 0,
         dA.data_ptr(), dB.data_ptr(), dC.data_ptr(), L.ptr(dD), L.ptr(dbias))
     return p, args
 
@@ -57,9 +58,9 @@ def test_noalloc_backward_matches_ss_bwd_twice(dtype):
     lib = L.lib()
     inp = to_dev(make_inputs(2, 96, 300, 16, dtype=dtype, has_z=True, seed=21))
     p = _Prepared(inp["u"], inp["delta"], inp["A"], inp["B"], inp["C"], inp["D"], inp["z"], inp["delta_bias"], True)
-    _, ckpt, _ = scan_forward(p, True, False)
+    _, ckpt, _, y = scan_forward(p, True, False)
     ref_bufs = _outputs(inp, p)
-    _, ref_args = _args(inp, ref_bufs, ckpt)
+    _, ref_args = _args(inp, ref_bufs, ckpt, y)
     stream = torch.cuda.current_stream().cuda_stream
     L.check(lib.ss_bwd(ctypes.byref(ref_args), stream), "ss_bwd")
     torch.cuda.synchronize()
