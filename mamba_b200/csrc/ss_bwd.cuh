@@ -16,7 +16,8 @@
 // with packed fp32x2 arithmetic).  Tiles of 16 steps are visited last to first.  Per tile a
 // lane
 //   * restarts its 4 states from the forward's checkpoint of the previous tile boundary,
-//   * runs the 16 forward steps keeping exp(delta'A) and h_{t-1} in registers,
+//   * runs the 16 forward steps keeping h_{t-1} in registers (exp(delta'A) is recomputed
+//     in the reverse steps rather than kept: registers, not MUFU, are the scarce resource),
 //   * runs the 16 reverse steps, carrying dh across tiles in registers,
 //   * hands its dB / dC contributions to a per-warp shared-memory block every 4 steps; the
 //     warp then sums them over its 32 channels (each lane one (step, B|C, state-pair) row,
@@ -260,14 +261,15 @@ __global__ void __launch_bounds__(32 * kNW, 3) ss_bwd_kernel(const __grid_consta
       return;
     }
 
-    // ---- scan phase, forward: decays and states of the tile in registers
-    float2 da[kTile][2];
+    // ---- scan phase, forward: the states of the tile in registers.  The decays are not
+    //      kept (the reverse sweep recomputes them): MUFU has headroom, registers do not,
+    //      and the freed registers let the scheduler hide the shared-memory latencies.
 #pragma unroll
     for (int i4 = 0; i4 < 4; ++i4) {
-      const float4 dt4 = sm.dt_s[lane][swz(lane, i4)];
       const float4 du4 = sm.dtu_s[lane][swz(lane, i4)];
-      const float dts[4] = {dt4.x, dt4.y, dt4.z, dt4.w};
+      const float4 dt4 = sm.dt_s[lane][swz(lane, i4)];
       const float dus[4] = {du4.x, du4.y, du4.z, du4.w};
+      const float dts[4] = {dt4.x, dt4.y, dt4.z, dt4.w};
 #pragma unroll
       for (int st = 0; st < 4; ++st) {
         const int t = 4 * i4 + st;
@@ -283,8 +285,7 @@ __global__ void __launch_bounds__(32 * kNW, 3) ss_bwd_kernel(const __grid_consta
 #pragma unroll
         for (int p = 0; p < 2; ++p) {
           const float2 x = mul2(f2(dts[st]), A2[p]);
-          da[t][p] = make_float2(ex2(x.x), ex2(x.y));
-          hp[t + 1][p] = fma2(da[t][p], hp[t][p], mul2(f2(dus[st]), Bv[p]));
+          hp[t + 1][p] = fma2(make_float2(ex2(x.x), ex2(x.y)), hp[t][p], mul2(f2(dus[st]), Bv[p]));
         }
       }
     }
@@ -324,7 +325,8 @@ __global__ void __launch_bounds__(32 * kNW, 3) ss_bwd_kernel(const __grid_consta
 #pragma unroll
         for (int p = 0; p < 2; ++p) {
           const float2 dh = fma2(Cv[p], dy2, e2[p]);
-          const float2 ee = mul2(da[t][p], dh);
+          const float2 x = mul2(dt2, A2[p]);
+          const float2 ee = mul2(make_float2(ex2(x.x), ex2(x.y)), dh);
           const float2 g = mul2(ee, hp[t][p]);
           dA2[p] = fma2(dt2, g, dA2[p]);
           s1 = fma2(Ad[p], g, s1);

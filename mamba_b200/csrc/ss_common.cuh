@@ -53,6 +53,14 @@ __device__ __forceinline__ float ex2(float x) {
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
 }
+// ex2 kept in program order with the other ordered ex2 (asm volatile): a tile's block of
+// independent decays is issued back to back ahead of the FMA chain that consumes it,
+// instead of being sunk next to each use by the scheduler
+__device__ __forceinline__ float ex2_ordered(float x) {
+  float y;
+  asm volatile("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
 __device__ __forceinline__ float fast_rcp(float x) {
   float y;
   asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
@@ -102,7 +110,12 @@ __device__ __forceinline__ float2 add2(float2 a, float2 b) { return __fadd2_rn(a
 template <typename T, int S>
 __device__ __forceinline__ void lds_run(const T* p, float (&v)[S]) {
   constexpr int BYTES = S * (int)sizeof(T);
-  if constexpr (BYTES % 16 == 0 || BYTES == 8) {
+  if constexpr (BYTES == 4 && sizeof(T) == 2) {
+    union { uint32_t w; T e[2]; } u;
+    u.w = *reinterpret_cast<const uint32_t*>(p);
+    v[0] = to_f<T>(u.e[0]);
+    v[1] = to_f<T>(u.e[1]);
+  } else if constexpr (BYTES % 16 == 0 || BYTES == 8) {
     constexpr int CH = (BYTES % 16 == 0) ? 16 : 8;
     constexpr int PER = CH / (int)sizeof(T);
 #pragma unroll
@@ -225,6 +238,15 @@ __device__ __forceinline__ int swz(int r, int q) { return q ^ ((r >> 1) & 3); }
 // vectorized when aligned and complete.
 template <typename T, int S>
 __device__ __forceinline__ void store_run(T* __restrict__ dst, const float (&v)[S], int nvalid, bool vec) {
+  if constexpr (S * sizeof(T) == 4 && sizeof(T) == 2) {
+    if (vec && nvalid == S) {
+      union { uint32_t w; T e[2]; } pk;
+      pk.e[0] = from_f<T>(v[0]);
+      pk.e[1] = from_f<T>(v[1]);
+      *reinterpret_cast<uint32_t*>(dst) = pk.w;
+      return;
+    }
+  }
   if (vec && nvalid == S && (S * sizeof(T)) % 8 == 0) {
     if constexpr (S * sizeof(T) % 16 == 0) {
 #pragma unroll

@@ -192,12 +192,25 @@ __global__ void __launch_bounds__(32 * kNW, 4) ss_fwd_kernel(const __grid_consta
       return;
     }
 
-    // ---- 2. the recurrence, 4 states per lane, 16 steps
+    // ---- 2. the recurrence, 4 states per lane, 16 steps.  All 64 decays of the tile are
+    //         issued first (independent ex2, so the MUFU pipe stays full), then the FMA
+    //         recurrence consumes them.
+    float2 da[kTile][2];
 #pragma unroll
     for (int i4 = 0; i4 < 4; ++i4) {
       const float4 dt4 = sm.dt_s[lane][swz(lane, i4)];
-      const float4 du4 = sm.dtu_s[lane][swz(lane, i4)];
       const float dts[4] = {dt4.x, dt4.y, dt4.z, dt4.w};
+#pragma unroll
+      for (int st = 0; st < 4; ++st)
+#pragma unroll
+        for (int p = 0; p < 2; ++p) {
+          const float2 x = mul2(f2(dts[st]), A2[p]);
+          da[4 * i4 + st][p] = make_float2(ex2_ordered(x.x), ex2_ordered(x.y));
+        }
+    }
+#pragma unroll
+    for (int i4 = 0; i4 < 4; ++i4) {
+      const float4 du4 = sm.dtu_s[lane][swz(lane, i4)];
       const float dus[4] = {du4.x, du4.y, du4.z, du4.w};
 #pragma unroll
       for (int st = 0; st < 4; ++st) {
@@ -220,13 +233,9 @@ __global__ void __launch_bounds__(32 * kNW, 4) ss_fwd_kernel(const __grid_consta
           Cv[1] = Cc[1];
         }
 #pragma unroll
-        for (int p = 0; p < 2; ++p) {
-          const float2 x = mul2(f2(dts[st]), A2[p]);
-          h[p] = fma2(make_float2(ex2(x.x), ex2(x.y)), h[p], mul2(f2(dus[st]), Bv[p]));
-        }
+        for (int p = 0; p < 2; ++p) h[p] = fma2(da[t][p], h[p], mul2(f2(dus[st]), Bv[p]));
         const float2 y2 = fma2(Cv[1], h[1], mul2(Cv[0], h[0]));
-        const float yp = y2.x + y2.y;
-        sm.y_s[w][t][lane] = yp;
+        sm.y_s[w][t][lane] = y2.x + y2.y;
       }
     }
     if (a.ckpt != nullptr && lane_ok) {
