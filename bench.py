@@ -27,7 +27,6 @@ import json
 import math
 import os
 import statistics
-import subprocess
 import sys
 import time
 
@@ -85,51 +84,80 @@ def profile_traffic():
 
 # ----------------------------------------------------------------------------- clocks
 class ClockSampler:
-    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    """SM clock and clock-event reasons of this process's GPU, polled through NVML from a
+    thread every ~2 ms while the timed region runs, with one sample at each end, so even a
+    short region is covered.  The GPU is found by UUID (then PCI bus id), never by index,
+    because CUDA_VISIBLE_DEVICES may renumber devices."""
+    PERIOD_S = 0.002
 
-    def __init__(self, index):
-        self.index = index
-        self.proc = None
+    def __init__(self, device_index):
+        self.dev = device_index
+        self.rows, self.h, self.err = [], None, None
+
+    def _handle(self):
+        import pynvml as N
+        import torch
+
+        N.nvmlInit()
+        pr = torch.cuda.get_device_properties(self.dev)
+        try:
+            return N.nvmlDeviceGetHandleByUUID("GPU-" + str(pr.uuid))
+        except Exception:
+            return N.nvmlDeviceGetHandleByPciBusId(f"{pr.pci_domain_id:08X}:{pr.pci_bus_id:02X}:{pr.pci_device_id:02X}.0")
+
+    def _sample(self):
+        import pynvml as N
+
+        self.rows.append((N.nvmlDeviceGetClockInfo(self.h, N.NVML_CLOCK_SM),
+                          N.nvmlDeviceGetCurrentClocksEventReasons(self.h)))
+
+    def _loop(self):
+        while not self.stop.wait(self.PERIOD_S):
+            try:
+                self._sample()
+            except Exception as e:  # keep the samples taken so far
+                self.err = repr(e)
+                return
 
     def __enter__(self):
+        import threading
+
         try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}",
-                 "--format=csv,noheader,nounits", "-lms", "100"],
-                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-        except OSError:
-            self.proc = None
+            import pynvml as N
+
+            self.h = self._handle()
+            self.max_mhz = N.nvmlDeviceGetMaxClockInfo(self.h, N.NVML_CLOCK_SM)
+            self._sample()
+        except Exception as e:
+            self.h, self.err = None, repr(e)
+            return self
+        self.stop = threading.Event()
+        self.thread = threading.Thread(target=self._loop, daemon=True)
+        self.thread.start()
         return self
 
     def __exit__(self, *exc):
-        self.out = ""
-        if self.proc is not None:
-            self.proc.terminate()
+        if self.h is not None:
+            self.stop.set()
+            self.thread.join(timeout=5)
             try:
-                self.out, _ = self.proc.communicate(timeout=5)
-            except subprocess.TimeoutExpired:
-                self.proc.kill()
-                self.out, _ = self.proc.communicate()
+                self._sample()
+            except Exception as e:
+                self.err = repr(e)
         return False
 
     def summary(self):
-        rows = []
-        for line in (self.out or "").strip().splitlines():
-            p = [x.strip() for x in line.split(",")]
-            if len(p) < 8:
-                continue
-            try:
-                rows.append((float(p[0]), float(p[1]), p[4:8]))
-            except ValueError:
-                continue
-        if not rows:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for _, _, r in rows for i, v in enumerate(r) if v.lower() == "active"})
-        return {"sm_mhz": statistics.median(r[0] for r in rows), "sm_max_mhz": max(r[1] for r in rows),
-                "reasons": reasons, "samples": len(rows)}
+        if not self.rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "error": self.err}
+        import pynvml as N
+
+        bits = {"hw_slowdown": N.nvmlClocksEventReasonHwSlowdown,
+                "hw_thermal_slowdown": N.nvmlClocksEventReasonHwThermalSlowdown,
+                "sw_thermal_slowdown": N.nvmlClocksEventReasonSwThermalSlowdown,
+                "sw_power_cap": N.nvmlClocksEventReasonSwPowerCap}
+        reasons = sorted({k for _, r in self.rows for k, bit in bits.items() if r & bit})
+        return {"sm_mhz": statistics.median(r[0] for r in self.rows), "sm_max_mhz": self.max_mhz,
+                "reasons": reasons, "samples": len(self.rows), "source": "NVML, 2 ms poll"}
 
 
 # ----------------------------------------------------------------------------- inputs
@@ -156,8 +184,9 @@ def cpu_sample_rate(n_full_elems, tokens_full, budget_s, seed=0):
 
     d_full, L, n = PER_GPU["d"], PER_GPU["L"], PER_GPU["n"]
 
-    def run(dsl):
-        h = make_inputs(1, dsl, L, n, seed, "cpu")
+    def run(rows):
+        bsl, dsl = (1, rows) if rows <= d_full else (rows // d_full, d_full)
+        h = make_inputs(bsl, dsl, L, n, seed, "cpu")
         t = time.perf_counter()
         O.selective_scan_ref(h["u"], h["delta"], h["A"], h["B"], h["C"], h["D"], h["z"], h["delta_bias"], True,
                              precision="f32")
@@ -166,14 +195,21 @@ def cpu_sample_rate(n_full_elems, tokens_full, budget_s, seed=0):
         return time.perf_counter() - t
 
     threads = O.max_threads()
-    t_cal = run(8)
-    dsl = int(min(d_full, max(8, 8 * budget_s / max(t_cal, 1e-3))))
-    dsl = max(8, dsl - dsl % 8)
-    t = run(dsl)
-    elems = dsl * L
-    rate_elems = elems / t
+    # calibrate on a slice that keeps every thread busy, then grow the slice (channels first,
+    # then whole batch rows) towards ~budget_s, never past the per-GPU workload
+    cal = max(8, 8 * threads)
+    t_cal = run(cal)
+    rows = int(min(n_full_elems // L, PER_GPU["b"] * d_full, max(cal, cal * budget_s / max(t_cal, 1e-3))))
+    rows = max(8, rows - rows % 8) if rows <= d_full else rows - rows % d_full
+    t, reps = run(rows), 1
+    while t < budget_s and reps < 64:  # the whole slice was fast: repeat it to fill the budget
+        t += run(rows)
+        reps += 1
+    bsl, dsl = (1, rows) if rows <= d_full else (rows // d_full, d_full)
+    rate_elems = reps * rows * L / t
     value = tokens_full / (n_full_elems / rate_elems)
-    return value, threads, f"batch 1 x {dsl} channels x {L} steps (fwd+bwd, fp32 port) in {t:.2f} s", t
+    return value, threads, (f"{reps} x batch {bsl} x {dsl} channels x {L} steps (fwd+bwd, fp32 port) "
+                            f"in {t:.2f} s"), t
 
 
 def reference_arm(a, world, rank):
@@ -266,7 +302,7 @@ def main():
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier()
     torch.cuda.synchronize()
-    with ClockSampler(local) as clk:
+    with ClockSampler(dev.index) as clk:
         t0.record()
         for i in range(K):
             ev[i][0].record()
