@@ -46,6 +46,11 @@ def args_():
     ap.add_argument("--e2e-steps", type=int, default=5)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="CPU-baseline sample budget")
+    ap.add_argument("--workload", default="scan", choices=["scan", "block"],
+                    help="scan: the north-star selective scan (default); block: one MambaSimple block "
+                         "(d_model 768) fwd+bwd, fused mamba_inner_fn against the reference's op sequence")
+    ap.add_argument("--block-path", default="both", choices=["both", "fused", "unfused"],
+                    help="block workload: time both paths, or only one (for a launch list of one path)")
     return ap.parse_args()
 
 
@@ -250,6 +255,102 @@ def config_dict(world):
 
 
 # ----------------------------------------------------------------------------- gpu arm
+# ----------------------------------------------------------------------------- block workload
+def block_bench(a):
+    """One MambaSimple block (d_model 768 -> d_inner 1536, N 16, conv width 4; the layer of the
+    24-layer model config) fwd+bwd at batch 8 x seqlen 2048, bf16, through
+      fused:   mamba_b200.mamba_simple_forward (conv+SiLU kernel, GEMMs on transposed views,
+               scan with the gate fused, no permute copies), and
+      unfused: the reference's own op sequence (modules/mamba_simple.py:87-151: permute +
+               contiguous copies, cuDNN depthwise conv, SiLU, the gate as separate kernels)
+               with mamba_b200.selective_scan_fn as its SelectiveScanFn — what a user of the
+               reference gets from the drop-in scan alone.
+    Same parameters, inputs and output gradient for both."""
+    import torch
+    import torch.nn as nn
+    import torch.nn.functional as F
+
+    import mamba_b200
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    dm, d, n, K, b, L = 768, 1536, 16, 4, 8, 2048
+    R = math.ceil(dm / 16)
+    torch.manual_seed(0)
+    blk = nn.Module()
+    blk.input_proj = nn.Linear(dm, 2 * d, bias=False)
+    blk.short_conv = nn.Conv1d(d, d, K, padding=K - 1, groups=d, bias=False)
+    blk.ssm_param_proj = nn.Linear(d, R + 2 * n, bias=False)
+    blk.delta_proj = nn.Linear(R, d, bias=True)
+    dt = torch.exp(torch.rand(d) * (math.log(0.1) - math.log(1e-3)) + math.log(1e-3)).clamp(min=1e-4)
+    with torch.no_grad():
+        blk.delta_proj.bias.copy_(dt + torch.log(-torch.expm1(-dt)))
+    blk.log_A = nn.Parameter(torch.log(torch.arange(1, n + 1, dtype=torch.float32)).repeat(d, 1))
+    blk.D = nn.Parameter(torch.ones(d))
+    blk.output_proj = nn.Linear(d, dm, bias=False)
+    blk = blk.to(dev, torch.bfloat16)
+    g = torch.Generator().manual_seed(1)
+    h = torch.randn(b, L, dm, generator=g).to(dev, torch.bfloat16).requires_grad_()
+    dy = torch.randn(b, L, dm, generator=g).to(dev, torch.bfloat16)
+
+    def unfused(x):
+        xs, zs = torch.chunk(blk.input_proj(x).permute(0, 2, 1).contiguous(), 2, dim=1)
+        xs = F.silu(blk.short_conv(xs)[..., :L])
+        dbl = blk.ssm_param_proj(xs.permute(0, 2, 1).contiguous().view(b * L, d))
+        dr, B, C = torch.split(dbl, [R, n, n], dim=-1)
+        delta = (blk.delta_proj.weight @ dr.t()).view(d, b, L).permute(1, 0, 2).contiguous()
+        B = B.view(b, L, n).permute(0, 2, 1).contiguous().unsqueeze(1)
+        C = C.view(b, L, n).permute(0, 2, 1).contiguous().unsqueeze(1)
+        A = -torch.exp(blk.log_A.float())
+        y = mamba_b200.selective_scan_fn(xs, delta, A, B, C, blk.D.float(), None, blk.delta_proj.bias.float(), True)
+        hs = y.permute(0, 2, 1).contiguous()
+        hs = hs * F.silu(zs.permute(0, 2, 1).contiguous())
+        return blk.output_proj(hs)
+
+    def fused(x):
+        return mamba_b200.mamba_simple_forward(blk, x)
+
+    def timed(fn):
+        def step():
+            out = fn(h)
+            out.backward(dy)
+            h.grad = None
+            for p_ in blk.parameters():
+                p_.grad = None
+        for _ in range(a.warmup):
+            step()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with ClockSampler(dev.index) as clk:
+            e0.record()
+            for _ in range(a.steps):
+                step()
+            e1.record()
+            torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / a.steps, clk.summary()
+
+    ms_u = ms_f = float("nan")
+    clocks = None
+    if a.block_path in ("both", "unfused"):
+        ms_u, clocks = timed(unfused)
+    if a.block_path in ("both", "fused"):
+        ms_f, clocks = timed(fused)
+    tokens = b * L
+    line = {
+        "workload": "block", "metric": "Mamba block (MambaSimple, d_model 768) fwd+bwd tokens/s",
+        "value": tokens / (ms_f / 1e3), "unit": "tokens/s", "ms_per_step": ms_f,
+        "unfused_value": tokens / (ms_u / 1e3), "unfused_ms_per_step": ms_u, "speedup_vs_unfused": ms_u / ms_f,
+        "n_gpus": 1, "steps": a.steps, "warmup": a.warmup, "higher_is_better": True, "dtype": "bf16",
+        "data": "synthetic",
+        "config": {"workload": "one MambaSimple block fwd+bwd, batch 8, seqlen 2048, d_model 768, d_inner 1536, "
+                               "d_state 16, conv width 4, dt_rank 48, bf16 parameters and activations",
+                   "global_batch": b, "seq_len": L, "l2": "activations larger than L2"},
+        "clocks": clocks,
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 def main():
     a = args_()
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -259,6 +360,8 @@ def main():
         return reference_arm(a, world, rank)
     if a.warmup < 3:
         a.warmup = 3
+    if a.workload == "block":
+        return block_bench(a) if rank == 0 else 0
 
     import torch
     import torch.distributed as dist

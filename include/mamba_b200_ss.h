@@ -15,6 +15,14 @@
  *              (kernel launcher backward_kernel_launch, backward_kernel.cu:588-618)
  *   ss_step <- no counterpart: the reference has no decode step (models/causal_lm.py:61-62
  *              is a stub).  It is one step of the same recurrence from a stored state.
+ *   ss_conv_fwd / ss_conv_bwd <- the input side of the reference's MambaSimple.forward,
+ *              modules/mamba_simple.py:91-98 (input_proj output -> permute(0,2,1).contiguous()
+ *              -> chunk -> short_conv (nn.Conv1d depthwise, padding width-1, cut to seqlen,
+ *              :41-48) -> SiLU), which the reference runs as separate PyTorch kernels with
+ *              copies; here one pass reads the projection's (batch, seqlen, dim) layout
+ *              directly and writes the scan's (batch, dim, seqlen) layout.
+ *   ss_conv_step <- no counterpart (no decode in the reference): the same convolution for
+ *              one new input from a rolling state of the previous width-1 inputs.
  *
  * Tensor layouts (element strides; the innermost sequence axis must have stride 1):
  *   u, delta, z, out, dout, du, ddelta, dz : (batch, dim, seqlen), batch/dim strides given
@@ -39,8 +47,9 @@
 extern "C" {
 #endif
 
-#define SS_ABI_VERSION 2
+#define SS_ABI_VERSION 3
 #define SS_MAX_DSTATE 16
+#define SS_MAX_CONV_WIDTH 4
 /* capacity (floats) of the library-held state array used by ss_bwd_noalloc: 16 MiB */
 #define SS_NOALLOC_MAX_CKPT_ELEMS 4194304
 
@@ -115,6 +124,55 @@ typedef struct ss_step_args {
   void* out;         int64_t out_batch_stride;    /* (batch, dim)                         */
 } ss_step_args;
 
+/* Causal depthwise convolution (+ SiLU) of the (batch, seqlen, dim) input x into the scan's
+ * (batch, dim, seqlen) layout:
+ *   pre[b,c,t] = bias[c] + sum_{k<width} weight[c,k] * x[b, t-(width-1)+k, c]
+ *   u[b,c,t]   = silu ? pre * sigmoid(pre) : pre
+ * x at t < 0 is state_in[b, c, t + width-1] (oldest first) or zero when state_in is NULL (the
+ * reference's zero padding).  z, when given, is copied from (batch, seqlen, dim) to zt
+ * (batch, dim, seqlen) in the same pass.  state_out, when given, receives the last width-1
+ * inputs (for a following chunk or ss_conv_step); it must not alias state_in.  ss_conv_fwd and
+ * ss_conv_bwd use state_in entries at the I/O precision (exact for states this library wrote,
+ * which are earlier inputs of the same dtype); ss_conv_step keeps them in fp32. */
+typedef struct ss_conv_args {
+  int batch, dim, seqlen, width; /* width 1..SS_MAX_CONV_WIDTH                              */
+  int silu;                      /* apply SiLU                                              */
+  int io_dtype;                  /* dtype of x, z, u, zt                                    */
+  const void* x;     int64_t x_batch_stride, x_seq_stride;   /* (batch, seqlen, dim), dim stride 1 */
+  const float* weight;           /* (dim, width) fp32 contiguous                            */
+  const float* bias;             /* (dim) fp32, nullable                                    */
+  const float* state_in;         /* (batch, dim, width-1) fp32 contiguous, nullable        */
+  float* state_out;              /* (batch, dim, width-1) fp32 contiguous, nullable        */
+  void* u;           int64_t u_batch_stride, u_dim_stride;   /* (batch, dim, seqlen), seq stride 1 */
+  const void* z;     int64_t z_batch_stride, z_seq_stride;   /* nullable (batch, seqlen, dim)      */
+  void* zt;          int64_t zt_batch_stride, zt_dim_stride; /* (batch, dim, seqlen); iff z        */
+} ss_conv_args;
+
+/* Backward of ss_conv_fwd: from du (gradient of u) it writes dx in the (batch, seqlen, dim)
+ * layout and overwrites dweight / dbias; dzt, when given, is copied transposed into dz (the
+ * gate half of the projection's gradient).  f holds the forward's arguments (x, weight,
+ * bias, state_in, silu; its u / z / zt / state_out are ignored). */
+typedef struct ss_conv_bwd_args {
+  ss_conv_args f;
+  const void* du;    int64_t du_batch_stride, du_dim_stride;   /* (batch, dim, seqlen)        */
+  void* dx;          int64_t dx_batch_stride, dx_seq_stride;   /* (batch, seqlen, dim)        */
+  const void* dzt;   int64_t dzt_batch_stride, dzt_dim_stride; /* nullable (batch, dim, seqlen) */
+  void* dz;          int64_t dz_batch_stride, dz_seq_stride;   /* (batch, seqlen, dim); iff dzt */
+  float* dweight;    /* (dim, width) fp32, overwritten                                      */
+  float* dbias;      /* (dim) fp32, nullable, overwritten                                   */
+} ss_conv_bwd_args;
+
+/* One decode step of the convolution: window = [state (oldest first), x];
+ * u = silu(bias + weight . window); state <- window[1:]. */
+typedef struct ss_conv_step_args {
+  int batch, dim, width, silu, io_dtype;
+  float* state;      int64_t state_batch_stride;  /* (batch, dim, width-1) fp32, in/out      */
+  const void* x;     int64_t x_batch_stride;      /* (batch, dim)                           */
+  const float* weight;                            /* (dim, width) fp32                      */
+  const float* bias;                              /* (dim) fp32, nullable                   */
+  void* u;           int64_t u_batch_stride;      /* (batch, dim)                           */
+} ss_conv_step_args;
+
 /* Number of fp32 elements of the forward-to-backward state buffer. */
 SS_API size_t ss_ckpt_elems(int batch, int dim, int seqlen, int dstate);
 
@@ -140,6 +198,15 @@ SS_API int ss_bwd_noalloc(const ss_bwd_args* args, void* stream);
 /* One decode step: state <- exp(dt'*A) state + dt'*x*B; out = (C.state + D x) [* silu(z)]. */
 SS_API int ss_step(const ss_step_args* args, void* stream);
 
+/* Convolution + SiLU on the input side of a Mamba block (see ss_conv_args). */
+SS_API int ss_conv_fwd(const ss_conv_args* args, void* stream);
+
+/* Its backward (see ss_conv_bwd_args). */
+SS_API int ss_conv_bwd(const ss_conv_bwd_args* args, void* stream);
+
+/* One decode step of the convolution (see ss_conv_step_args). */
+SS_API int ss_conv_step(const ss_conv_step_args* args, void* stream);
+
 /* Static description of a status code. */
 SS_API const char* ss_status_string(int status);
 
@@ -155,8 +222,9 @@ SS_API int ss_device_status(int reset, void* stream);
 SS_API int ss_abi_version(void);
 
 /* sizeof the argument structs as compiled into the library (0: ss_fwd_args,
- * 1: ss_bwd_args, 2: ss_step_args; 0 for other values) — lets an FFI binding check
- * its own struct layout against the library's. */
+ * 1: ss_bwd_args, 2: ss_step_args, 3: ss_conv_args, 4: ss_conv_bwd_args,
+ * 5: ss_conv_step_args; 0 for other values) — lets an FFI binding check its own struct
+ * layout against the library's. */
 SS_API size_t ss_struct_size(int which);
 
 #ifdef __cplusplus

@@ -4,8 +4,13 @@ Public operators (all CUDA-only, backed by libmamba_b200_ss.so):
   selective_scan_fn, SelectiveScanFn   forward / backward scan with optional SiLU(z) gate
   selective_state_update               single-token decode step
   selective_scan_ext                   drop-in for the reference's native `selective_scan`
+  mamba_inner_fn, MambaInnerFn         the whole Mamba block from the input projection's output
+                                       (conv + SiLU, projections, scan + gate, output projection)
+  mamba_simple_forward                 a MambaSimple module's forward through mamba_inner_fn
 """
+from .inner import MambaInnerFn, mamba_inner_fn, mamba_simple_forward
 from .selective_scan_interface import SelectiveScanFn, selective_scan_fn, selective_state_update
 
-__all__ = ["SelectiveScanFn", "selective_scan_fn", "selective_state_update"]
+__all__ = ["SelectiveScanFn", "selective_scan_fn", "selective_state_update", "MambaInnerFn", "mamba_inner_fn",
+           "mamba_simple_forward"]
 __version__ = "0.1.0"

@@ -67,9 +67,46 @@ class StepArgs(ctypes.Structure):
     ]
 
 
+class ConvArgs(ctypes.Structure):
+    _fields_ = [
+        ("batch", c_int), ("dim", c_int), ("seqlen", c_int), ("width", c_int), ("silu", c_int),
+        ("io_dtype", c_int),
+        ("x", c_vp), ("x_batch_stride", c_i64), ("x_seq_stride", c_i64),
+        ("weight", c_vp), ("bias", c_vp), ("state_in", c_vp), ("state_out", c_vp),
+        ("u", c_vp), ("u_batch_stride", c_i64), ("u_dim_stride", c_i64),
+        ("z", c_vp), ("z_batch_stride", c_i64), ("z_seq_stride", c_i64),
+        ("zt", c_vp), ("zt_batch_stride", c_i64), ("zt_dim_stride", c_i64),
+    ]
+
+
+class ConvBwdArgs(ctypes.Structure):
+    _fields_ = [
+        ("f", ConvArgs),
+        ("du", c_vp), ("du_batch_stride", c_i64), ("du_dim_stride", c_i64),
+        ("dx", c_vp), ("dx_batch_stride", c_i64), ("dx_seq_stride", c_i64),
+        ("dzt", c_vp), ("dzt_batch_stride", c_i64), ("dzt_dim_stride", c_i64),
+        ("dz", c_vp), ("dz_batch_stride", c_i64), ("dz_seq_stride", c_i64),
+        ("dweight", c_vp), ("dbias", c_vp),
+    ]
+
+
+class ConvStepArgs(ctypes.Structure):
+    _fields_ = [
+        ("batch", c_int), ("dim", c_int), ("width", c_int), ("silu", c_int), ("io_dtype", c_int),
+        ("state", c_vp), ("state_batch_stride", c_i64),
+        ("x", c_vp), ("x_batch_stride", c_i64),
+        ("weight", c_vp), ("bias", c_vp),
+        ("u", c_vp), ("u_batch_stride", c_i64),
+    ]
+
+
+STRUCTS = (FwdArgs, BwdArgs, StepArgs, ConvArgs, ConvBwdArgs, ConvStepArgs)  # ss_struct_size index order
+ABI_VERSION = 3
+MAX_CONV_WIDTH = 4
+
 EXPORTS = ("ss_fwd", "ss_bwd", "ss_step", "ss_ckpt_elems", "ss_status_string",
            "ss_last_cuda_error", "ss_abi_version", "ss_struct_size", "ss_device_status",
-           "ss_bwd_noalloc")
+           "ss_bwd_noalloc", "ss_conv_fwd", "ss_conv_bwd", "ss_conv_step")
 NOALLOC_MAX_CKPT_ELEMS = 4194304  # SS_NOALLOC_MAX_CKPT_ELEMS
 
 _lib = None
@@ -92,7 +129,11 @@ def lib():
                 L.ss_bwd_noalloc.argtypes = [ctypes.POINTER(BwdArgs), c_vp]
                 L.ss_bwd_noalloc.restype = c_int
                 L.ss_step.argtypes = [ctypes.POINTER(StepArgs), c_vp]
-                for f in ("ss_fwd", "ss_bwd", "ss_step", "ss_last_cuda_error", "ss_abi_version"):
+                L.ss_conv_fwd.argtypes = [ctypes.POINTER(ConvArgs), c_vp]
+                L.ss_conv_bwd.argtypes = [ctypes.POINTER(ConvBwdArgs), c_vp]
+                L.ss_conv_step.argtypes = [ctypes.POINTER(ConvStepArgs), c_vp]
+                for f in ("ss_fwd", "ss_bwd", "ss_step", "ss_last_cuda_error", "ss_abi_version",
+                          "ss_conv_fwd", "ss_conv_bwd", "ss_conv_step"):
                     getattr(L, f).restype = c_int
                 L.ss_ckpt_elems.argtypes = [c_int, c_int, c_int, c_int]
                 L.ss_ckpt_elems.restype = ctypes.c_size_t
@@ -102,7 +143,9 @@ def lib():
                 L.ss_device_status.restype = c_int
                 L.ss_struct_size.argtypes = [c_int]
                 L.ss_struct_size.restype = ctypes.c_size_t
-                for i, st in enumerate((FwdArgs, BwdArgs, StepArgs)):
+                if L.ss_abi_version() != ABI_VERSION:
+                    raise RuntimeError(f"{LIB_PATH}: ABI version {L.ss_abi_version()} != {ABI_VERSION}; rebuild it")
+                for i, st in enumerate(STRUCTS):
                     if L.ss_struct_size(i) != ctypes.sizeof(st):
                         raise RuntimeError(f"{LIB_PATH}: struct {st.__name__} layout mismatch "
                                            f"({L.ss_struct_size(i)} != {ctypes.sizeof(st)} bytes)")

@@ -35,7 +35,10 @@
 
 namespace ssb {
 
-constexpr int kStagesBwd = 3;  // tiles in flight per CTA
+// tiles in flight per CTA: 3 for 2-byte I/O; 2 for fp32 I/O, whose larger tiles would
+// otherwise leave room for only two CTAs per SM
+template <typename IT>
+constexpr int kStagesBwd = sizeof(IT) == 4 ? 2 : 3;
 constexpr int kS12Row = 66;    // floats per row of the packed (S1, S2) partials (64 + 2 pad)
 
 // dB/dC fold block: 16 rows of 64 floats (32 lanes x float2); 16-byte unit q of row r is
@@ -46,14 +49,14 @@ __device__ __forceinline__ int fold_off(int r, int unit) { return r * 64 + 4 * (
 template <typename IT, int kNW, bool kVarB, bool kVarC, bool kHasZ>
 struct BwdSmem {
   static constexpr int NS = kSPW * kNW;
-  alignas(128) IT u[kStagesBwd][kCh][kTile];
-  alignas(128) IT d[kStagesBwd][kCh][kTile];
-  alignas(128) IT g[kStagesBwd][kCh][kTile];
-  alignas(128) IT z[kHasZ ? kStagesBwd : 1][kCh][kTile];
-  alignas(128) IT y[kHasZ ? kStagesBwd : 1][kCh][kTile];
-  alignas(128) IT Braw[kVarB ? kStagesBwd : 1][NS * kTile];  // TMA path: B / C have the I/O dtype
-  alignas(128) IT Craw[kVarC ? kStagesBwd : 1][NS * kTile];
-  alignas(128) float hck[kStagesBwd][NS][kCh];   // states at the tile start, [n][channel]
+  alignas(128) IT u[kStagesBwd<IT>][kCh][kTile];
+  alignas(128) IT d[kStagesBwd<IT>][kCh][kTile];
+  alignas(128) IT g[kStagesBwd<IT>][kCh][kTile];
+  alignas(128) IT z[kHasZ ? kStagesBwd<IT> : 1][kCh][kTile];
+  alignas(128) IT y[kHasZ ? kStagesBwd<IT> : 1][kCh][kTile];
+  alignas(128) IT Braw[kVarB ? kStagesBwd<IT> : 1][NS * kTile];  // TMA path: B / C have the I/O dtype
+  alignas(128) IT Craw[kVarC ? kStagesBwd<IT> : 1][NS * kTile];
+  alignas(128) float hck[kStagesBwd<IT>][NS][kCh];   // states at the tile start, [n][channel]
   alignas(16) float4 dt_s[kCh][4];
   alignas(16) float4 dtu_s[kCh][4];
   alignas(16) float4 dy_s[kCh][4];
@@ -64,7 +67,7 @@ struct BwdSmem {
   alignas(16) float s12_s[kNW][kTile][kS12Row];                        // (S1, S2) per channel
   alignas(16) float fold[(kVarB || kVarC) ? kNW : 1][16 * 64];         // 4 steps x 2 pairs x B|C
   alignas(16) float fout[(kVarB || kVarC) ? kNW : 1][2][kSPW][kTile];  // [B|C][j][t] sums
-  alignas(8) uint64_t full[kStagesBwd];
+  alignas(8) uint64_t full[kStagesBwd<IT>];
 };
 
 template <typename IT, int kNW, bool kVarB, bool kVarC, bool kHasZ, bool kTMA>
@@ -155,23 +158,23 @@ __global__ void __launch_bounds__(32 * kNW, 3) ss_bwd_kernel(const __grid_consta
   };
   if constexpr (kTMA) {
     if (tid == 0) {
-      for (int s = 0; s < kStagesBwd; ++s) mbar_init(&sm.full[s], 1);
+      for (int s = 0; s < kStagesBwd<IT>; ++s) mbar_init(&sm.full[s], 1);
       mbar_fence_init();
     }
     __syncthreads();
     if (tid == 0)
-      for (int s = 0; s < kStagesBwd && s < ntiles; ++s) issue(s, s);
+      for (int s = 0; s < kStagesBwd<IT> && s < ntiles; ++s) issue(s, s);
   }
 
   for (int it = 0; it < ntiles; ++it) {
     const int k = ntiles - 1 - it;
     const int t0 = k * kTile;
     const int tlen = min(kTile, L - t0);
-    const int stg = kTMA ? it % kStagesBwd : 0;
+    const int stg = kTMA ? it % kStagesBwd<IT> : 0;
     bool failed = false;
     float2 hp[kTile + 1][2];
     if constexpr (kTMA) {
-      failed = !mbar_wait_bounded(&sm.full[stg], (it / kStagesBwd) & 1);
+      failed = !mbar_wait_bounded(&sm.full[stg], (it / kStagesBwd<IT>) & 1);
       if constexpr (kVarB) widen_bc<IT, NT, NS>(sm.B_s, reinterpret_cast<const float*>(sm.Braw[stg]), false);
       if constexpr (kVarC) widen_bc<IT, NT, NS>(sm.C_s, reinterpret_cast<const float*>(sm.Craw[stg]), false);
 #pragma unroll
@@ -254,8 +257,8 @@ __global__ void __launch_bounds__(32 * kNW, 3) ss_bwd_kernel(const __grid_consta
     if (__syncthreads_or(failed)) {
       if (tid == 0) {
         if (P.status != nullptr) atomicOr(P.status, kStatusTimeout);
-        for (int j = it + 1; j < ntiles && j < it + kStagesBwd; ++j)
-          mbar_wait_bounded(&sm.full[j % kStagesBwd], (j / kStagesBwd) & 1);
+        for (int j = it + 1; j < ntiles && j < it + kStagesBwd<IT>; ++j)
+          mbar_wait_bounded(&sm.full[j % kStagesBwd<IT>], (j / kStagesBwd<IT>) & 1);
       }
       __syncthreads();
       return;
@@ -351,7 +354,6 @@ __global__ void __launch_bounds__(32 * kNW, 3) ss_bwd_kernel(const __grid_consta
         const int type = r & 1;
         float2 acc = make_float2(0.f, 0.f);
         if ((type == 0 && kVarB) || (type == 1 && kVarC)) {
-#pragma unroll
           float2 part[4];
 #pragma unroll
           for (int m = 0; m < 8; ++m) {
@@ -427,7 +429,7 @@ __global__ void __launch_bounds__(32 * kNW, 3) ss_bwd_kernel(const __grid_consta
     }
     __syncthreads();
     if constexpr (kTMA) {
-      if (tid == 0 && it + kStagesBwd < ntiles) issue(it + kStagesBwd, stg);
+      if (tid == 0 && it + kStagesBwd<IT> < ntiles) issue(it + kStagesBwd<IT>, stg);
     }
   }
 

@@ -23,8 +23,17 @@ template <typename IT> cudaError_t launch_step(const ss_step_args&, cudaStream_t
 __device__ int g_ss_status;
 
 namespace {
-
 thread_local int g_last_cuda = 0;
+}  // namespace
+
+// shared with the other translation units of the library (hidden visibility)
+int ssb::record_cuda_status(cudaError_t e) {
+  if (e == cudaSuccess) return SS_OK;
+  g_last_cuda = (int)e;
+  return SS_ERR_CUDA;
+}
+
+namespace {
 
 int* status_ptr() {
   void* p = nullptr;
@@ -92,11 +101,7 @@ bool map_bc(CUtensorMap* m, const void* p, const ss_fwd_args& a) {
               (uint64_t)a.seqlen * es, (uint64_t)a.seqlen * a.dstate * es, ssb::kTile, ns);
 }
 
-int cuda_status(cudaError_t e) {
-  if (e == cudaSuccess) return SS_OK;
-  g_last_cuda = (int)e;
-  return SS_ERR_CUDA;
-}
+int cuda_status(cudaError_t e) { return ssb::record_cuda_status(e); }
 
 size_t esize(int dt) { return dt == SS_F32 ? 4 : 2; }
 bool dtype_ok(int dt) { return dt == SS_F32 || dt == SS_BF16 || dt == SS_F16; }
@@ -272,6 +277,9 @@ size_t ss_struct_size(int which) {
     case 0: return sizeof(ss_fwd_args);
     case 1: return sizeof(ss_bwd_args);
     case 2: return sizeof(ss_step_args);
+    case 3: return sizeof(ss_conv_args);
+    case 4: return sizeof(ss_conv_bwd_args);
+    case 5: return sizeof(ss_conv_step_args);
     default: return 0;
   }
 }

@@ -23,6 +23,10 @@
 
 namespace ssb {
 
+// Records e as the thread's last CUDA error (ss_last_cuda_error) and maps it to a status.
+int record_cuda_status(cudaError_t e);
+
+
 constexpr int kTile = 16;   // time steps per tile = checkpoint interval
 constexpr int kCh = 32;     // channels per CTA (one per lane)
 constexpr int kSPW = 4;     // states per warp

@@ -33,10 +33,10 @@ def test_library_exports_every_declared_symbol():
 
 def test_abi_version_and_struct_layout():
     lib = L.lib()
-    assert lib.ss_abi_version() == 2
-    for i, st in enumerate((L.FwdArgs, L.BwdArgs, L.StepArgs)):
+    assert lib.ss_abi_version() == 3
+    for i, st in enumerate(L.STRUCTS):
         assert lib.ss_struct_size(i) == ctypes.sizeof(st)
-    assert lib.ss_struct_size(7) == 0
+    assert lib.ss_struct_size(len(L.STRUCTS)) == 0
 
 
 def test_ckpt_elems():
@@ -119,3 +119,51 @@ def test_status_codes_map_to_python_errors():
     with pytest.raises(RuntimeError):
         L.check(L.SS_ERR_CUDA, "x")
     L.check(L.SS_OK, "x")
+
+
+def _valid_conv():
+    a = L.ConvArgs()
+    a.batch, a.dim, a.seqlen, a.width, a.silu = 2, 64, 100, 4, 1
+    a.io_dtype = L.SS_BF16
+    for f in ("x", "weight", "u"):
+        setattr(a, f, 0x1000)
+    a.x_batch_stride, a.x_seq_stride = 100 * 128, 128
+    a.u_batch_stride, a.u_dim_stride = 64 * 100, 100
+    return a
+
+
+@pytest.mark.parametrize("field,value,status", [
+    ("width", 5, L.SS_ERR_UNSUPPORTED),
+    ("width", 0, L.SS_ERR_INVALID),
+    ("dim", 0, L.SS_ERR_INVALID),
+    ("io_dtype", 9, L.SS_ERR_UNSUPPORTED),
+    ("x", None, L.SS_ERR_INVALID),
+    ("weight", None, L.SS_ERR_INVALID),
+    ("u", None, L.SS_ERR_INVALID),
+    ("z", 0x2000, L.SS_ERR_INVALID),       # z without zt
+    ("x_seq_stride", -1, L.SS_ERR_INVALID),
+    ("batch", 70000, L.SS_ERR_UNSUPPORTED),
+])
+def test_conv_validation(field, value, status):
+    a = _valid_conv()
+    setattr(a, field, value)
+    assert L.lib().ss_conv_fwd(ctypes.byref(a), None) == status
+
+
+def test_conv_bwd_and_step_validation():
+    lib = L.lib()
+    a = _valid_conv()
+    a.state_in = a.state_out = 0x3000
+    assert lib.ss_conv_fwd(ctypes.byref(a), None) == L.SS_ERR_INVALID  # aliasing states
+    b = L.ConvBwdArgs()
+    b.f = _valid_conv()
+    assert lib.ss_conv_bwd(ctypes.byref(b), None) == L.SS_ERR_INVALID  # no du / dx / dweight
+    b.du = b.dx = b.dweight = 0x1000
+    b.dzt = 0x1000
+    assert lib.ss_conv_bwd(ctypes.byref(b), None) == L.SS_ERR_INVALID  # dzt without dz
+    assert lib.ss_conv_bwd(None, None) == L.SS_ERR_INVALID
+    s = L.ConvStepArgs()
+    s.batch, s.dim, s.width, s.silu, s.io_dtype = 2, 64, 4, 1, L.SS_F32
+    assert lib.ss_conv_step(ctypes.byref(s), None) == L.SS_ERR_INVALID
+    s.width = 8
+    assert lib.ss_conv_step(ctypes.byref(s), None) == L.SS_ERR_UNSUPPORTED

@@ -90,3 +90,24 @@ def test_reference_mamba_simple_runs_unchanged(ref_pkg):
     grads = [p.grad for p in block.parameters()]
     assert all(g_ is not None and torch.isfinite(g_).all() for g_ in grads)
     assert x.grad is not None and torch.isfinite(x.grad).all()
+
+
+def test_mamba_simple_restatement_matches_reference_module(ref_pkg):
+    """Pins tests/torch_ref.MambaSimpleRef (the fused path's GPU oracle) to the reference's
+    MambaSimple: same state_dict, same outputs and parameter gradients."""
+    from torch_ref import MambaSimpleRef
+
+    mod = importlib.import_module("reference.modules.mamba_simple")
+    torch.manual_seed(1)
+    ref = mod.MambaSimple(model_dim=16, state_dim=4, conv_bias=True, bias=True)
+    mine = MambaSimpleRef(16, state_dim=4, conv_bias=True, bias=True)
+    assert set(dict(ref.named_parameters())) == set(dict(mine.named_parameters()))
+    mine.load_state_dict(ref.state_dict())
+    x = torch.randn(2, 20, 16)
+    y_ref, y_mine = ref(x), mine(x)
+    np.testing.assert_allclose(y_mine.detach().numpy(), y_ref.detach().numpy(), rtol=1e-4, atol=1e-5)
+    g = torch.randn_like(y_ref)
+    y_ref.backward(g)
+    y_mine.backward(g)
+    for (name, p), q in zip(ref.named_parameters(), mine.parameters()):
+        np.testing.assert_allclose(q.grad.numpy(), p.grad.numpy(), rtol=1e-3, atol=1e-4, err_msg=name)

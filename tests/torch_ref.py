@@ -38,3 +38,54 @@ def scan_autograd(u, delta, A, B, C, D=None, z=None, delta_bias=None, delta_soft
     if z is not None:
         y = y * F.silu(z)
     return y, h
+
+
+def conv_silu_ref(x_bld, weight, bias=None, state_in=None, silu=True):
+    """Causal depthwise conv of x (b, L, d) -> (b, d, L): the reference's short_conv with
+    padding K-1 cut to L (modules/mamba_simple.py:41-48, :97) and its SiLU (:98).
+    state_in (b, d, K-1) replaces the zero padding."""
+    d, K = x_bld.shape[-1], weight.shape[-1]
+    xt = x_bld.transpose(1, 2)
+    pad = (state_in.to(xt.dtype) if state_in is not None
+           else xt.new_zeros(xt.shape[0], d, K - 1))
+    pre = F.conv1d(torch.cat([pad, xt], -1), weight.reshape(d, 1, K).to(xt.dtype),
+                   None if bias is None else bias.to(xt.dtype), groups=d)
+    return F.silu(pre) if silu else pre
+
+
+class MambaSimpleRef(torch.nn.Module):
+    """The reference's MambaSimple block restated in plain torch: the same parameters (names,
+    shapes, initial values as modules/mamba_simple.py:9-85) and the same forward mathematics
+    (:87-151), with the differentiable scan above in place of the CUDA op.  Tests compare the
+    fused path against it (in float64) and pin it against the reference module itself."""
+
+    def __init__(self, model_dim, state_dim=16, conv_kernel=4, expansion_factor=2, conv_bias=False, bias=False):
+        import math
+
+        super().__init__()
+        d = int(expansion_factor * model_dim)
+        r = math.ceil(model_dim / 16)
+        self.inner_dim, self.delta_rank, self.state_dim = d, r, state_dim
+        self.input_proj = torch.nn.Linear(model_dim, 2 * d, bias=bias)
+        self.short_conv = torch.nn.Conv1d(d, d, conv_kernel, padding=conv_kernel - 1, groups=d, bias=conv_bias)
+        self.ssm_param_proj = torch.nn.Linear(d, r + 2 * state_dim, bias=False)
+        self.delta_proj = torch.nn.Linear(r, d, bias=True)
+        std = r ** -0.5
+        torch.nn.init.uniform_(self.delta_proj.weight, -std, std)
+        dt = torch.exp(torch.rand(d) * (math.log(0.1) - math.log(1e-3)) + math.log(1e-3)).clamp(min=1e-4)
+        with torch.no_grad():
+            self.delta_proj.bias.copy_(dt + torch.log(-torch.expm1(-dt)))
+        self.log_A = torch.nn.Parameter(torch.log(torch.arange(1, state_dim + 1, dtype=torch.float32).repeat(d, 1)))
+        self.D = torch.nn.Parameter(torch.ones(d))
+        self.output_proj = torch.nn.Linear(d, model_dim, bias=bias)
+
+    def forward(self, h):
+        n, r = self.state_dim, self.delta_rank
+        x, z = self.input_proj(h).chunk(2, dim=-1)                      # (b, L, d) each
+        u = conv_silu_ref(x, self.short_conv.weight, self.short_conv.bias)  # (b, d, L)
+        dr, B, C = self.ssm_param_proj(u.transpose(1, 2)).split([r, n, n], dim=-1)
+        delta = (dr @ self.delta_proj.weight.t()).transpose(1, 2)          # (b, d, L)
+        A = -torch.exp(self.log_A.to(u.dtype))
+        y, _ = scan_autograd(u, delta, A, B.transpose(1, 2).unsqueeze(1), C.transpose(1, 2).unsqueeze(1),
+                             self.D.to(u.dtype), None, self.delta_proj.bias.to(u.dtype), True)
+        return self.output_proj(y.transpose(1, 2) * F.silu(z))
