@@ -46,9 +46,11 @@ def args_():
     ap.add_argument("--e2e-steps", type=int, default=5)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="CPU-baseline sample budget")
-    ap.add_argument("--workload", default="scan", choices=["scan", "block"],
+    ap.add_argument("--workload", default="scan", choices=["scan", "block", "decode"],
                     help="scan: the north-star selective scan (default); block: one MambaSimple block "
-                         "(d_model 768) fwd+bwd, fused mamba_inner_fn against the reference's op sequence")
+                         "(d_model 768) fwd+bwd, fused mamba_inner_fn against the reference's op sequence; "
+                         "decode: a 24-layer CausalLM (d_model 768) decoding 256 tokens after a 128-token prompt "
+                         "at batch 64")
     ap.add_argument("--block-path", default="both", choices=["both", "fused", "unfused"],
                     help="block workload: time both paths, or only one (for a launch list of one path)")
     return ap.parse_args()
@@ -255,7 +257,142 @@ def config_dict(world):
 
 
 # ----------------------------------------------------------------------------- gpu arm
-# ----------------------------------------------------------------------------- block workload
+# ----------------------------------------------------------------------------- block / decode workloads
+def _mamba_block(dm, n=16, K=4):
+    """A block with MambaSimple's parameter names, shapes and initial values
+    (modules/mamba_simple.py:9-85; expansion 2, dt_rank ceil(dm / 16), no biases)."""
+    import torch
+    import torch.nn as nn
+
+    d, R = 2 * dm, math.ceil(dm / 16)
+    blk = nn.Module()
+    blk.input_proj = nn.Linear(dm, 2 * d, bias=False)
+    blk.short_conv = nn.Conv1d(d, d, K, padding=K - 1, groups=d, bias=False)
+    blk.ssm_param_proj = nn.Linear(d, R + 2 * n, bias=False)
+    blk.delta_proj = nn.Linear(R, d, bias=True)
+    nn.init.uniform_(blk.delta_proj.weight, -R ** -0.5, R ** -0.5)
+    dt = torch.exp(torch.rand(d) * (math.log(0.1) - math.log(1e-3)) + math.log(1e-3)).clamp(min=1e-4)
+    with torch.no_grad():
+        blk.delta_proj.bias.copy_(dt + torch.log(-torch.expm1(-dt)))
+    blk.log_A = nn.Parameter(torch.log(torch.arange(1, n + 1, dtype=torch.float32)).repeat(d, 1))
+    blk.D = nn.Parameter(torch.ones(d))
+    blk.output_proj = nn.Linear(d, dm, bias=False)
+    return blk
+
+
+def _causal_lm(vocab, dm, layers, n=16, K=4):
+    """A model with the reference CausalLM's module tree (models/causal_lm.py:20-58): embedding,
+    layers of (RMSNorm, MambaSimple block), final RMSNorm, lm_head tied to the embedding."""
+    import torch
+    import torch.nn as nn
+
+    class RMSNorm(nn.Module):  # modules/rms_norm.py:4-30
+        def __init__(self, dim, eps=1e-6):
+            super().__init__()
+            self.eps, self.weight = eps, nn.Parameter(torch.zeros(dim))
+
+        def forward(self, x):
+            xf = x.float()
+            return (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + self.eps) * (1.0 + self.weight.float())
+                    ).type_as(x)
+
+    m = nn.Module()
+    m.embedding = nn.Embedding(vocab, dm)
+    m.layers = nn.ModuleList()
+    for _ in range(layers):
+        layer = nn.Module()
+        layer.norm, layer.mamba = RMSNorm(dm), _mamba_block(dm, n, K)
+        m.layers.append(layer)
+    m.norm = RMSNorm(dm)
+    m.lm_head = nn.Linear(dm, vocab, bias=False)
+    m.lm_head.weight = m.embedding.weight
+    return m
+
+
+def decode_bench(a):
+    """Decoding with a 24-layer CausalLM-shaped model (d_model 768, d_inner 1536, N 16, vocab
+    32000; the decode of the 24-layer model config): batch 64, a 128-token prompt, then 256 new
+    tokens (greedy), bf16.  Reports new tokens per second over the decode loop (prompt prefill
+    timed separately) for the CUDA-graph step and the eager step, and — as the reference's
+    alternative, since its generate() is a stub and MambaSimple has no step — the cost of one
+    full forward over the sequence per new token (fused path, no cache), timed on 8 tokens."""
+    import torch
+
+    from mamba_b200 import mamba_simple_forward
+    from mamba_b200.decode import Decoder
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    vocab, dm, layers, b, L0, T = 32000, 768, 24, 64, 128, 256
+    torch.manual_seed(0)
+    model = _causal_lm(vocab, dm, layers).to(dev, torch.bfloat16).eval()
+    prompt = torch.randint(0, vocab, (b, L0), generator=torch.Generator().manual_seed(1)).to(dev)
+
+    def ev():
+        return torch.cuda.Event(enable_timing=True)
+
+    def run(cuda_graph):
+        dec = Decoder(model, b, cuda_graph=cuda_graph)
+        logits = dec.prefill(prompt)
+        tok = logits.argmax(-1)
+        for _ in range(a.warmup):  # warm-up steps (the graph is captured on the first)
+            tok = dec.step(tok).argmax(-1)
+        dec = Decoder(model, b, cuda_graph=cuda_graph)
+        torch.cuda.synchronize()
+        e0, e1, e2 = ev(), ev(), ev()
+        with ClockSampler(dev.index) as clk:
+            e0.record()
+            logits = dec.prefill(prompt)
+            e1.record()
+            tok = logits.argmax(-1)
+            for _ in range(T):
+                tok = dec.step(tok).argmax(-1)
+            e2.record()
+            torch.cuda.synchronize()
+        return e0.elapsed_time(e1), e1.elapsed_time(e2), clk.summary()
+
+    with torch.no_grad():
+        pre_g, dec_g, clocks = run(True)
+        _, dec_e, _ = run(False)
+        ids = torch.cat([prompt, prompt[:, :8]], 1)
+        fwd = lambda L: model.lm_head(_lm_hidden(model, ids[:, :L], mamba_simple_forward)[:, -1])
+        for _ in range(2):
+            fwd(L0 + 1)
+        torch.cuda.synchronize()
+        e0, e1 = ev(), ev()
+        e0.record()
+        for i in range(8):
+            fwd(L0 + 1 + i).argmax(-1)
+        e1.record()
+        torch.cuda.synchronize()
+        naive_ms = e0.elapsed_time(e1) / 8
+    n_params = sum(p.numel() for p in model.parameters())
+    d, n = 2 * dm, 16
+    step_bytes = 2 * n_params + layers * b * d * (n + 3) * 4 * 2  # weights once + SSM / conv states in and out
+    step_ms = dec_g / T
+    line = {
+        "workload": "decode", "metric": "CausalLM decode tokens/s (24 layers, d_model 768, batch 64)",
+        "value": b * T / (dec_g / 1e3), "unit": "tokens/s", "ms_per_token_step": step_ms,
+        "eager_value": b * T / (dec_e / 1e3), "eager_ms_per_token_step": dec_e / T,
+        "no_cache_value": b / (naive_ms / 1e3), "no_cache_ms_per_token_step": naive_ms,
+        "prefill_ms": pre_g, "prompt_tokens_per_s": b * L0 / (pre_g / 1e3),
+        "roofline": {"bound": "hbm", "bytes_per_step": step_bytes, "achieved": step_bytes / (step_ms / 1e3) / 1e9,
+                     "peak": load_peaks()[0], "unit": "GB/s",
+                     "frac": step_bytes / (step_ms / 1e3) / 1e9 / load_peaks()[0]},
+        "n_gpus": 1, "higher_is_better": True, "dtype": "bf16", "data": "synthetic (random weights, random prompt)",
+        "config": {"workload": "24-layer CausalLM, d_model 768, d_inner 1536, d_state 16, vocab 32000, batch 64, "
+                               "prompt 128, 256 new tokens, greedy", "params": n_params},
+        "clocks": clocks,
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def _lm_hidden(model, ids, block_forward):
+    h = model.embedding(ids)
+    for layer in model.layers:
+        h = h + block_forward(layer.mamba, layer.norm(h))
+    return model.norm(h)
 def block_bench(a):
     """One MambaSimple block (d_model 768 -> d_inner 1536, N 16, conv width 4; the layer of the
     24-layer model config) fwd+bwd at batch 8 x seqlen 2048, bf16, through
@@ -277,18 +414,7 @@ def block_bench(a):
     dm, d, n, K, b, L = 768, 1536, 16, 4, 8, 2048
     R = math.ceil(dm / 16)
     torch.manual_seed(0)
-    blk = nn.Module()
-    blk.input_proj = nn.Linear(dm, 2 * d, bias=False)
-    blk.short_conv = nn.Conv1d(d, d, K, padding=K - 1, groups=d, bias=False)
-    blk.ssm_param_proj = nn.Linear(d, R + 2 * n, bias=False)
-    blk.delta_proj = nn.Linear(R, d, bias=True)
-    dt = torch.exp(torch.rand(d) * (math.log(0.1) - math.log(1e-3)) + math.log(1e-3)).clamp(min=1e-4)
-    with torch.no_grad():
-        blk.delta_proj.bias.copy_(dt + torch.log(-torch.expm1(-dt)))
-    blk.log_A = nn.Parameter(torch.log(torch.arange(1, n + 1, dtype=torch.float32)).repeat(d, 1))
-    blk.D = nn.Parameter(torch.ones(d))
-    blk.output_proj = nn.Linear(d, dm, bias=False)
-    blk = blk.to(dev, torch.bfloat16)
+    blk = _mamba_block(dm, n, K).to(dev, torch.bfloat16)
     g = torch.Generator().manual_seed(1)
     h = torch.randn(b, L, dm, generator=g).to(dev, torch.bfloat16).requires_grad_()
     dy = torch.randn(b, L, dm, generator=g).to(dev, torch.bfloat16)
@@ -362,6 +488,8 @@ def main():
         a.warmup = 3
     if a.workload == "block":
         return block_bench(a) if rank == 0 else 0
+    if a.workload == "decode":
+        return decode_bench(a) if rank == 0 else 0
 
     import torch
     import torch.distributed as dist

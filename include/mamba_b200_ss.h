@@ -23,6 +23,9 @@
  *              directly and writes the scan's (batch, dim, seqlen) layout.
  *   ss_conv_step <- no counterpart (no decode in the reference): the same convolution for
  *              one new input from a rolling state of the previous width-1 inputs.
+ *   ss_rmsnorm_fwd / ss_rmsnorm_bwd <- the reference's RMSNorm.forward (modules/rms_norm.py:
+ *              21-30) fused with its Block's residual add (models/causal_lm.py:30-37), which
+ *              the reference runs as a chain of PyTorch elementwise and reduction kernels.
  *
  * Tensor layouts (element strides; the innermost sequence axis must have stride 1):
  *   u, delta, z, out, dout, du, ddelta, dz : (batch, dim, seqlen), batch/dim strides given
@@ -47,7 +50,7 @@
 extern "C" {
 #endif
 
-#define SS_ABI_VERSION 3
+#define SS_ABI_VERSION 4
 #define SS_MAX_DSTATE 16
 #define SS_MAX_CONV_WIDTH 4
 /* capacity (floats) of the library-held state array used by ss_bwd_noalloc: 16 MiB */
@@ -173,6 +176,36 @@ typedef struct ss_conv_step_args {
   void* u;           int64_t u_batch_stride;      /* (batch, dim)                           */
 } ss_conv_step_args;
 
+/* Residual add + RMSNorm over rows of length dim (dim <= 2048 for 2-byte I/O, <= 1024 for fp32):
+ *   h = x + residual   (rounded to the I/O dtype; h = x when residual is NULL)
+ *   y = h * rsqrt(mean(h^2) + eps) * (unit_offset ? 1 + weight : weight)
+ * residual_out (needs residual) receives h; rstd (rows, fp32) keeps rsqrt(mean(h^2) + eps)
+ * for the backward.  The reference's RMSNorm is unit_offset = 1 (modules/rms_norm.py:29). */
+typedef struct ss_rmsnorm_args {
+  int rows, dim, io_dtype, unit_offset;
+  float eps;
+  const void* x;         int64_t x_row_stride;
+  const void* residual;  int64_t residual_row_stride;       /* nullable                      */
+  const float* weight;                                       /* (dim) fp32                    */
+  void* y;               int64_t y_row_stride;
+  void* residual_out;    int64_t residual_out_row_stride;   /* nullable                      */
+  float* rstd;                                               /* (rows) fp32, nullable         */
+} ss_rmsnorm_args;
+
+/* Backward of ss_rmsnorm_fwd from dy: dh = d loss / d h (plus dh_in, the gradient already
+ * flowing into h through the residual stream, when given) — also the gradient of x and of
+ * residual — and dweight (overwritten).  h is the normalised input (residual_out, or x). */
+typedef struct ss_rmsnorm_bwd_args {
+  int rows, dim, io_dtype, unit_offset;
+  const void* h;         int64_t h_row_stride;
+  const float* weight;                                       /* (dim) fp32                    */
+  const float* rstd;                                         /* (rows) fp32 from the forward  */
+  const void* dy;        int64_t dy_row_stride;
+  const void* dh_in;     int64_t dh_in_row_stride;          /* nullable                      */
+  void* dh;              int64_t dh_row_stride;
+  float* dweight;                                            /* (dim) fp32, overwritten       */
+} ss_rmsnorm_bwd_args;
+
 /* Number of fp32 elements of the forward-to-backward state buffer. */
 SS_API size_t ss_ckpt_elems(int batch, int dim, int seqlen, int dstate);
 
@@ -207,6 +240,12 @@ SS_API int ss_conv_bwd(const ss_conv_bwd_args* args, void* stream);
 /* One decode step of the convolution (see ss_conv_step_args). */
 SS_API int ss_conv_step(const ss_conv_step_args* args, void* stream);
 
+/* Residual add + RMSNorm (see ss_rmsnorm_args). */
+SS_API int ss_rmsnorm_fwd(const ss_rmsnorm_args* args, void* stream);
+
+/* Its backward (see ss_rmsnorm_bwd_args). */
+SS_API int ss_rmsnorm_bwd(const ss_rmsnorm_bwd_args* args, void* stream);
+
 /* Static description of a status code. */
 SS_API const char* ss_status_string(int status);
 
@@ -223,7 +262,7 @@ SS_API int ss_abi_version(void);
 
 /* sizeof the argument structs as compiled into the library (0: ss_fwd_args,
  * 1: ss_bwd_args, 2: ss_step_args, 3: ss_conv_args, 4: ss_conv_bwd_args,
- * 5: ss_conv_step_args; 0 for other values) — lets an FFI binding check its own struct
+ * 5: ss_conv_step_args, 6: ss_rmsnorm_args, 7: ss_rmsnorm_bwd_args; 0 for other values) — lets an FFI binding check its own struct
  * layout against the library's. */
 SS_API size_t ss_struct_size(int which);
 

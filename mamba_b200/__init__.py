@@ -7,10 +7,16 @@ Public operators (all CUDA-only, backed by libmamba_b200_ss.so):
   mamba_inner_fn, MambaInnerFn         the whole Mamba block from the input projection's output
                                        (conv + SiLU, projections, scan + gate, output projection)
   mamba_simple_forward                 a MambaSimple module's forward through mamba_inner_fn
+  rms_norm_fn, rms_norm                residual add + RMSNorm in one kernel (forward / backward)
+  causal_lm_forward                    a CausalLM's forward through the fused block and norm
+  generate, Decoder                    prefill + cached single-token decode (CUDA-graph step)
 """
+from .decode import Decoder, generate
 from .inner import MambaInnerFn, mamba_inner_fn, mamba_simple_forward
+from .lm import causal_lm_forward
+from .norm import rms_norm, rms_norm_fn
 from .selective_scan_interface import SelectiveScanFn, selective_scan_fn, selective_state_update
 
 __all__ = ["SelectiveScanFn", "selective_scan_fn", "selective_state_update", "MambaInnerFn", "mamba_inner_fn",
-           "mamba_simple_forward"]
+           "mamba_simple_forward", "rms_norm_fn", "rms_norm", "causal_lm_forward", "generate", "Decoder"]
 __version__ = "0.1.0"

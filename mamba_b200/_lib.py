@@ -100,13 +100,38 @@ class ConvStepArgs(ctypes.Structure):
     ]
 
 
-STRUCTS = (FwdArgs, BwdArgs, StepArgs, ConvArgs, ConvBwdArgs, ConvStepArgs)  # ss_struct_size index order
-ABI_VERSION = 3
+class RmsNormArgs(ctypes.Structure):
+    _fields_ = [
+        ("rows", c_int), ("dim", c_int), ("io_dtype", c_int), ("unit_offset", c_int), ("eps", ctypes.c_float),
+        ("x", c_vp), ("x_row_stride", c_i64),
+        ("residual", c_vp), ("residual_row_stride", c_i64),
+        ("weight", c_vp),
+        ("y", c_vp), ("y_row_stride", c_i64),
+        ("residual_out", c_vp), ("residual_out_row_stride", c_i64),
+        ("rstd", c_vp),
+    ]
+
+
+class RmsNormBwdArgs(ctypes.Structure):
+    _fields_ = [
+        ("rows", c_int), ("dim", c_int), ("io_dtype", c_int), ("unit_offset", c_int),
+        ("h", c_vp), ("h_row_stride", c_i64),
+        ("weight", c_vp), ("rstd", c_vp),
+        ("dy", c_vp), ("dy_row_stride", c_i64),
+        ("dh_in", c_vp), ("dh_in_row_stride", c_i64),
+        ("dh", c_vp), ("dh_row_stride", c_i64),
+        ("dweight", c_vp),
+    ]
+
+
+# ss_struct_size index order
+STRUCTS = (FwdArgs, BwdArgs, StepArgs, ConvArgs, ConvBwdArgs, ConvStepArgs, RmsNormArgs, RmsNormBwdArgs)
+ABI_VERSION = 4
 MAX_CONV_WIDTH = 4
 
 EXPORTS = ("ss_fwd", "ss_bwd", "ss_step", "ss_ckpt_elems", "ss_status_string",
            "ss_last_cuda_error", "ss_abi_version", "ss_struct_size", "ss_device_status",
-           "ss_bwd_noalloc", "ss_conv_fwd", "ss_conv_bwd", "ss_conv_step")
+           "ss_bwd_noalloc", "ss_conv_fwd", "ss_conv_bwd", "ss_conv_step", "ss_rmsnorm_fwd", "ss_rmsnorm_bwd")
 NOALLOC_MAX_CKPT_ELEMS = 4194304  # SS_NOALLOC_MAX_CKPT_ELEMS
 
 _lib = None
@@ -132,8 +157,10 @@ def lib():
                 L.ss_conv_fwd.argtypes = [ctypes.POINTER(ConvArgs), c_vp]
                 L.ss_conv_bwd.argtypes = [ctypes.POINTER(ConvBwdArgs), c_vp]
                 L.ss_conv_step.argtypes = [ctypes.POINTER(ConvStepArgs), c_vp]
+                L.ss_rmsnorm_fwd.argtypes = [ctypes.POINTER(RmsNormArgs), c_vp]
+                L.ss_rmsnorm_bwd.argtypes = [ctypes.POINTER(RmsNormBwdArgs), c_vp]
                 for f in ("ss_fwd", "ss_bwd", "ss_step", "ss_last_cuda_error", "ss_abi_version",
-                          "ss_conv_fwd", "ss_conv_bwd", "ss_conv_step"):
+                          "ss_conv_fwd", "ss_conv_bwd", "ss_conv_step", "ss_rmsnorm_fwd", "ss_rmsnorm_bwd"):
                     getattr(L, f).restype = c_int
                 L.ss_ckpt_elems.argtypes = [c_int, c_int, c_int, c_int]
                 L.ss_ckpt_elems.restype = ctypes.c_size_t

@@ -280,6 +280,8 @@ size_t ss_struct_size(int which) {
     case 3: return sizeof(ss_conv_args);
     case 4: return sizeof(ss_conv_bwd_args);
     case 5: return sizeof(ss_conv_step_args);
+    case 6: return sizeof(ss_rmsnorm_args);
+    case 7: return sizeof(ss_rmsnorm_bwd_args);
     default: return 0;
   }
 }

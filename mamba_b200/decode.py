@@ -1,0 +1,167 @@
+"""Decoding for MambaSimple models: a prompt prefill that leaves per-layer states, single-token
+steps that continue from them, and ``generate`` for CausalLM-shaped models.
+
+The reference has no decode path: ``CausalLM.generate`` is a stub (models/causal_lm.py:61-62)
+and ``MambaSimple`` has no step, so continuing a sequence there means re-running the whole
+forward over it for every new token.  Here a block keeps two states per sequence:
+
+* conv state (batch, d_inner, K-1) fp32 — the last K-1 inputs of its causal convolution;
+* SSM state  (batch, d_inner, d_state) fp32 — h of the selective scan,
+
+and a new token costs one step of each (``ss_conv_step``, ``ss_step`` with the SiLU(z) gate
+fused) plus the block's small projections.  The prefill runs the fused block path
+(``mamba_inner_prefill``: conv kernel, batched GEMMs, scan with ``return_last_state``); each
+block's residual add is fused with the next RMSNorm (``rms_norm(..., prenorm=True)``); and the
+per-token model step of ``Decoder`` is captured once in a CUDA graph and replayed, so a decode
+step is one graph launch rather than a dozen kernel launches per layer from Python.
+
+Models are duck-typed on the reference's structure (models/causal_lm.py:20-58): ``embedding``,
+``layers`` (each with ``norm``, ``mamba``), ``norm``, ``lm_head``; each ``mamba`` has
+MambaSimple's parameter names (modules/mamba_simple.py:33-85).  Dropout is not applied
+(inference).
+"""
+from __future__ import annotations
+
+import torch
+
+from .inner import conv_step, mamba_inner_prefill
+from .norm import rms_norm
+from .selective_scan_interface import selective_state_update
+
+
+class _BlockParams:
+    """A MambaSimple block's parameters in the form the step kernels take, computed once."""
+
+    def __init__(self, blk):
+        self.blk = blk
+        self.d = blk.D.shape[0]
+        self.n = blk.log_A.shape[1]
+        self.R = blk.delta_proj.weight.shape[1]
+        self.A = (-torch.exp(blk.log_A.detach().float())).contiguous()
+        self.D = blk.D.detach().float().contiguous()
+        self.dt_bias = blk.delta_proj.bias.detach().float().contiguous()
+        w = blk.short_conv.weight.detach()
+        self.conv_w = w.reshape(w.shape[0], -1).float().contiguous()
+        self.conv_b = None if blk.short_conv.bias is None else blk.short_conv.bias.detach().float().contiguous()
+        self.K = self.conv_w.shape[1]
+
+
+@torch.no_grad()
+def mamba_simple_prefill(block, hidden_states, params: _BlockParams | None = None):
+    """Block forward over a prompt (batch, L, d_model) from zero states.  Returns
+    (output (batch, L, d_model), conv_state, ssm_state)."""
+    p = params or _BlockParams(block)
+    xz = block.input_proj(hidden_states)
+    return mamba_inner_prefill(xz, p.conv_w, p.conv_b, block.ssm_param_proj.weight, block.delta_proj.weight,
+                               block.delta_proj.bias, block.output_proj.weight, block.output_proj.bias, p.A, p.D,
+                               True)
+
+
+@torch.no_grad()
+def mamba_simple_step(block, hidden, conv_state, ssm_state, params: _BlockParams | None = None):
+    """One token (batch, d_model) through a block; updates both states in place."""
+    p = params or _BlockParams(block)
+    xz = block.input_proj(hidden)                                    # (b, 2 d)
+    x, z = xz[:, :p.d], xz[:, p.d:]
+    u = conv_step(conv_state, x, p.conv_w, p.conv_b)                 # (b, d)
+    dbl = torch.nn.functional.linear(u, block.ssm_param_proj.weight)  # (b, R + 2N)
+    dt = torch.nn.functional.linear(dbl[:, :p.R], block.delta_proj.weight)
+    B, C = dbl[:, p.R:p.R + p.n], dbl[:, p.R + p.n:]
+    y = selective_state_update(ssm_state, u, dt, p.A, B, C, p.D, z=z, dt_bias=p.dt_bias, dt_softplus=True)
+    return block.output_proj(y)
+
+
+class Decoder:
+    """Incremental decoding of a CausalLM-shaped model for a fixed batch size.
+
+    ``prefill(input_ids)`` runs the prompt and returns the last position's logits;
+    ``step(token_ids)`` feeds one token per sequence and returns the next logits (fp32).
+    With ``cuda_graph`` the step is captured on first use and replayed afterwards."""
+
+    def __init__(self, model, batch: int, cuda_graph: bool = True):
+        self.model = model
+        self.batch = batch
+        self.params = [_BlockParams(layer.mamba) for layer in model.layers]
+        dev = model.lm_head.weight.device
+        self.conv_states = [torch.zeros(batch, p.d, p.K - 1, device=dev) for p in self.params]
+        self.ssm_states = [torch.zeros(batch, p.d, p.n, device=dev) for p in self.params]
+        self.cuda_graph = cuda_graph
+        self.graph = None
+        self.tok = torch.zeros(batch, dtype=torch.long, device=dev)
+        self.logits = None
+
+    @torch.no_grad()
+    def prefill(self, input_ids):
+        if input_ids.shape[0] != self.batch:
+            raise ValueError(f"batch {input_ids.shape[0]} != decoder batch {self.batch}")
+        m = self.model
+        h = m.embedding(input_ids)
+        res = y = None
+        for i, layer in enumerate(m.layers):
+            # the residual add of the previous block fused with this block's RMSNorm
+            x, res = rms_norm(layer.norm, h if res is None else y, residual=res, prenorm=True)
+            y, cs, ss = mamba_simple_prefill(layer.mamba, x, self.params[i])
+            self.conv_states[i].copy_(cs)
+            self.ssm_states[i].copy_(ss)
+        return m.lm_head(rms_norm(m.norm, y[:, -1], residual=res[:, -1])).float()
+
+    def _step_eager(self, tok):
+        m = self.model
+        h = m.embedding(tok)
+        res = y = None
+        for i, layer in enumerate(m.layers):
+            x, res = rms_norm(layer.norm, h if res is None else y, residual=res, prenorm=True)
+            y = mamba_simple_step(layer.mamba, x, self.conv_states[i], self.ssm_states[i], self.params[i])
+        return m.lm_head(rms_norm(m.norm, y, residual=res)).float()
+
+    @torch.no_grad()
+    def step(self, token_ids):
+        if not self.cuda_graph:
+            return self._step_eager(token_ids)
+        self.tok.copy_(token_ids)
+        if self.graph is None:
+            self._capture()
+        self.graph.replay()
+        return self.logits
+
+    def _capture(self):
+        # warm-up on a side stream (library handles, cuBLAS workspaces), states saved around it
+        saved = [t.clone() for t in self.conv_states + self.ssm_states]
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            for _ in range(2):
+                self._step_eager(self.tok)
+        torch.cuda.current_stream().wait_stream(s)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            self.logits = self._step_eager(self.tok)
+        for t, v in zip(self.conv_states + self.ssm_states, saved):
+            t.copy_(v)
+
+
+def _sample(logits, temperature, top_k, generator):
+    if temperature == 0:
+        return logits.argmax(-1)
+    logits = logits / temperature
+    if top_k is not None:
+        kth = torch.topk(logits, top_k, dim=-1).values[:, -1:]
+        logits = logits.masked_fill(logits < kth, float("-inf"))
+    return torch.multinomial(torch.softmax(logits, -1), 1, generator=generator).squeeze(-1)
+
+
+@torch.no_grad()
+def generate(model, input_ids, max_new_tokens: int = 50, temperature: float = 1.0, top_k: int | None = None,
+             cuda_graph: bool = True, generator: torch.Generator | None = None):
+    """Continue every sequence of ``input_ids`` (batch, L) by ``max_new_tokens`` tokens —
+    the signature of the reference's stub CausalLM.generate (models/causal_lm.py:61), with
+    ``temperature = 0`` meaning greedy.  Returns (batch, L + max_new_tokens) token ids."""
+    dec = Decoder(model, input_ids.shape[0], cuda_graph=cuda_graph)
+    out = [input_ids]
+    logits = dec.prefill(input_ids)
+    for i in range(max_new_tokens):
+        tok = _sample(logits, temperature, top_k, generator)
+        out.append(tok[:, None])
+        if i + 1 < max_new_tokens:
+            logits = dec.step(tok)
+    return torch.cat(out, 1)

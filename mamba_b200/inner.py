@@ -148,6 +148,37 @@ def _wmm(W, X):
     return torch.bmm(W.unsqueeze(0).expand(X.shape[0], -1, -1), X)
 
 
+def _block_forward(xz, conv_weight, conv_bias, x_proj_weight, delta_proj_weight, delta_proj_bias, out_proj_weight,
+                   out_proj_bias, A, D, delta_softplus, *, train, want_states):
+    """Forward of the fused block.  Returns (result (b, L, dm), tensors the backward needs when
+    train, conv state (b, d, K-1) and final SSM state (b, d, N) when want_states)."""
+    _cuda_device(xz, conv_weight, x_proj_weight, delta_proj_weight, out_proj_weight, A)
+    xz = _bld(xz, "xz")
+    b, l, d2 = xz.shape
+    d = d2 // 2
+    if d2 != 2 * d:
+        raise ValueError("xz must have an even last dimension (x and z halves)")
+    io = xz.dtype
+    n = A.shape[1]
+    R = delta_proj_weight.shape[1]
+    if x_proj_weight.shape != (R + 2 * n, d):
+        raise ValueError(f"x_proj_weight must be {(R + 2 * n, d)}, got {tuple(x_proj_weight.shape)}")
+    x, z = xz[..., :d], xz[..., d:]
+    u, zt, conv_state = conv_forward(x, conv_weight, conv_bias, z, want_state=want_states)
+    Wx, Wdt, Wo = _w(x_proj_weight, io), _w(delta_proj_weight, io), _w(out_proj_weight, io)
+    # every GEMM below reads and writes (batch, rows, seqlen) or transposed views in place
+    dblT = _wmm(Wx, u)                                                 # (b, R + 2N, L)
+    delta = _wmm(Wdt, dblT[:, :R])                                     # (b, d, L)
+    B, C = dblT[:, R:R + n].unsqueeze(1), dblT[:, R + n:].unsqueeze(1)  # (b, 1, N, L)
+    p = _Prepared(u, delta, A, B, C, D, zt, delta_proj_bias, delta_softplus)
+    out, ckpt, last, y = scan_forward(p, train, want_states)           # gated (b, d, L)
+    res = torch.bmm(out.transpose(1, 2), Wo.t().expand(b, d, Wo.shape[0]))  # (b, L, dm)
+    if out_proj_bias is not None:
+        res = res + out_proj_bias.to(io)
+    saved = (u, zt, dblT, out, ckpt, y) if train else None
+    return res, saved, conv_state, last
+
+
 class MambaInnerFn(torch.autograd.Function):
     """Autograd op for the Mamba block between the input and output projections' GEMMs
     (inclusive of the output projection); see the module docstring."""
@@ -155,31 +186,13 @@ class MambaInnerFn(torch.autograd.Function):
     @staticmethod
     def forward(ctx, xz, conv_weight, conv_bias, x_proj_weight, delta_proj_weight, delta_proj_bias,
                 out_proj_weight, out_proj_bias, A, D=None, delta_softplus=True):
-        _cuda_device(xz, conv_weight, x_proj_weight, delta_proj_weight, out_proj_weight, A)
-        xz = _bld(xz, "xz")
-        b, l, d2 = xz.shape
-        d = d2 // 2
-        if d2 != 2 * d:
-            raise ValueError("xz must have an even last dimension (x and z halves)")
-        io = xz.dtype
-        n = A.shape[1]
-        R = delta_proj_weight.shape[1]
-        if x_proj_weight.shape != (R + 2 * n, d):
-            raise ValueError(f"x_proj_weight must be {(R + 2 * n, d)}, got {tuple(x_proj_weight.shape)}")
-        x, z = xz[..., :d], xz[..., d:]
-        u, zt, _ = conv_forward(x, conv_weight, conv_bias, z)
-        Wx, Wdt, Wo = _w(x_proj_weight, io), _w(delta_proj_weight, io), _w(out_proj_weight, io)
-        # every GEMM below reads and writes (batch, rows, seqlen) or transposed views in place
-        dblT = _wmm(Wx, u)                                         # (b, R + 2N, L)
-        delta = _wmm(Wdt, dblT[:, :R])                                    # (b, d, L)
-        B, C = dblT[:, R:R + n].unsqueeze(1), dblT[:, R + n:].unsqueeze(1)  # (b, 1, N, L)
-        p = _Prepared(u, delta, A, B, C, D, zt, delta_proj_bias, delta_softplus)
-        out, ckpt, _, y = scan_forward(p, True, False)                     # gated (b, d, L)
-        res = torch.bmm(out.transpose(1, 2), Wo.t().expand(b, d, Wo.shape[0]))  # (b, L, dm)
-        if out_proj_bias is not None:
-            res = res + out_proj_bias.to(io)
-        ctx.save_for_backward(xz, conv_weight, conv_bias, x_proj_weight, delta_proj_weight, delta_proj_bias,
-                              out_proj_weight, out_proj_bias, A, D, u, zt, dblT, out, ckpt, y)
+        train = any(ctx.needs_input_grad)  # inference keeps no checkpoints
+        res, saved, _, _ = _block_forward(xz, conv_weight, conv_bias, x_proj_weight, delta_proj_weight,
+                                          delta_proj_bias, out_proj_weight, out_proj_bias, A, D, delta_softplus,
+                                          train=train, want_states=False)
+        if train:
+            ctx.save_for_backward(xz, conv_weight, conv_bias, x_proj_weight, delta_proj_weight, delta_proj_bias,
+                                  out_proj_weight, out_proj_bias, A, D, *saved)
         ctx.softplus = bool(delta_softplus)
         return res
 
@@ -229,6 +242,18 @@ def mamba_inner_fn(xz, conv1d_weight, conv1d_bias, x_proj_weight, delta_proj_wei
     out_proj_bias of output_proj, A (dim, N) = -exp(log_A), D (dim)."""
     return MambaInnerFn.apply(xz, conv1d_weight, conv1d_bias, x_proj_weight, delta_proj_weight, delta_proj_bias,
                               out_proj_weight, out_proj_bias, A, D, delta_softplus)
+
+
+@torch.no_grad()
+def mamba_inner_prefill(xz, conv1d_weight, conv1d_bias, x_proj_weight, delta_proj_weight, delta_proj_bias,
+                        out_proj_weight, out_proj_bias, A, D=None, delta_softplus=True):
+    """Inference forward of mamba_inner_fn over a prompt that also returns the states a decode
+    continues from: (result (b, L, dm), conv_state (b, d, K-1) fp32, ssm_state (b, d, N) fp32).
+    Nothing is kept for a backward."""
+    res, _, conv_state, last = _block_forward(xz, conv1d_weight, conv1d_bias, x_proj_weight, delta_proj_weight,
+                                              delta_proj_bias, out_proj_weight, out_proj_bias, A, D, delta_softplus,
+                                              train=False, want_states=True)
+    return res, conv_state, last
 
 
 def mamba_simple_forward(block, hidden_states):

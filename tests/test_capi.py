@@ -33,7 +33,7 @@ def test_library_exports_every_declared_symbol():
 
 def test_abi_version_and_struct_layout():
     lib = L.lib()
-    assert lib.ss_abi_version() == 3
+    assert lib.ss_abi_version() == 4
     for i, st in enumerate(L.STRUCTS):
         assert lib.ss_struct_size(i) == ctypes.sizeof(st)
     assert lib.ss_struct_size(len(L.STRUCTS)) == 0
@@ -167,3 +167,21 @@ def test_conv_bwd_and_step_validation():
     assert lib.ss_conv_step(ctypes.byref(s), None) == L.SS_ERR_INVALID
     s.width = 8
     assert lib.ss_conv_step(ctypes.byref(s), None) == L.SS_ERR_UNSUPPORTED
+
+
+def test_rmsnorm_validation():
+    lib = L.lib()
+    a = L.RmsNormArgs()
+    a.rows, a.dim, a.io_dtype, a.unit_offset, a.eps = 4, 4096, L.SS_BF16, 1, 1e-6
+    assert lib.ss_rmsnorm_fwd(ctypes.byref(a), None) == L.SS_ERR_UNSUPPORTED  # row too long
+    a.dim = 768
+    assert lib.ss_rmsnorm_fwd(ctypes.byref(a), None) == L.SS_ERR_INVALID      # no pointers
+    a.rows = 0
+    assert lib.ss_rmsnorm_fwd(ctypes.byref(a), None) == L.SS_OK               # empty: nothing to do
+    a.rows, a.eps = 4, -1.0
+    assert lib.ss_rmsnorm_fwd(ctypes.byref(a), None) == L.SS_ERR_INVALID
+    b = L.RmsNormBwdArgs()
+    b.rows, b.dim, b.io_dtype = 4, 768, L.SS_F32
+    assert lib.ss_rmsnorm_bwd(ctypes.byref(b), None) == L.SS_ERR_INVALID      # no weight / dweight
+    assert lib.ss_rmsnorm_fwd(None, None) == L.SS_ERR_INVALID
+    assert lib.ss_rmsnorm_bwd(None, None) == L.SS_ERR_INVALID

@@ -111,3 +111,24 @@ def test_mamba_simple_restatement_matches_reference_module(ref_pkg):
     y_mine.backward(g)
     for (name, p), q in zip(ref.named_parameters(), mine.parameters()):
         np.testing.assert_allclose(q.grad.numpy(), p.grad.numpy(), rtol=1e-3, atol=1e-4, err_msg=name)
+
+
+def test_causal_lm_restatement_matches_reference_model(ref_pkg):
+    """Pins tests/torch_ref.CausalLMRef (used by the GPU decode tests) to the reference's
+    CausalLM: identical state_dict keys and logits."""
+    from torch_ref import CausalLMRef
+
+    lm = importlib.import_module("reference.models.causal_lm")
+    torch.manual_seed(2)
+    cfg = lm.CausalLMConfig(vocab_size=50, model_dim=16, state_dim=4, num_layers=2, dropout_rate=0.0)
+    ref = lm.CausalLM(cfg).eval()
+    mine = CausalLMRef(50, 16, state_dim=4, num_layers=2).eval()
+    assert set(ref.state_dict()) == set(mine.state_dict())
+    sd = ref.state_dict()
+    for k in sd:
+        if k.endswith("norm.weight"):  # move the norms off their zero init
+            sd[k] = torch.randn_like(sd[k]) * 0.1
+    ref.load_state_dict(sd)
+    mine.load_state_dict(sd)
+    ids = torch.randint(0, 50, (2, 12))
+    np.testing.assert_allclose(mine(ids).detach().numpy(), ref(ids).detach().numpy(), rtol=1e-4, atol=1e-4)

@@ -89,3 +89,52 @@ class MambaSimpleRef(torch.nn.Module):
         y, _ = scan_autograd(u, delta, A, B.transpose(1, 2).unsqueeze(1), C.transpose(1, 2).unsqueeze(1),
                              self.D.to(u.dtype), None, self.delta_proj.bias.to(u.dtype), True)
         return self.output_proj(y.transpose(1, 2) * F.silu(z))
+
+
+class RMSNormRef(torch.nn.Module):
+    """The reference's RMSNorm (modules/rms_norm.py:4-30): x / rms(x) * (1 + weight) in fp32,
+    cast back; weight starts at zero."""
+
+    def __init__(self, dim, eps=1e-6):
+        super().__init__()
+        self.eps = eps
+        self.weight = torch.nn.Parameter(torch.zeros(dim))
+
+    def forward(self, x):
+        xf = x.float()
+        y = xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + self.eps) * (1.0 + self.weight.float())
+        return y.type_as(x)
+
+
+class _BlockRef(torch.nn.Module):
+    def __init__(self, model_dim, state_dim, conv_kernel, expansion_factor, dropout):
+        super().__init__()
+        self.norm = RMSNormRef(model_dim)
+        self.mamba = MambaSimpleRef(model_dim, state_dim, conv_kernel, expansion_factor)
+        self.dropout = torch.nn.Dropout(dropout)
+
+
+class CausalLMRef(torch.nn.Module):
+    """The reference's CausalLM (models/causal_lm.py:7-58) restated with the same module tree
+    and parameter names, so state_dicts interchange.  ``block_forward(mamba, x)`` replaces each
+    block's mixer call (default: the mixer module itself), which lets a test run the same
+    weights through the fused GPU path."""
+
+    def __init__(self, vocab_size=64, model_dim=32, state_dim=16, conv_kernel=4, expansion_factor=2,
+                 dropout_rate=0.0, num_layers=2, tie_embeddings=True):
+        super().__init__()
+        self.embedding = torch.nn.Embedding(vocab_size, model_dim)
+        self.layers = torch.nn.ModuleList(
+            [_BlockRef(model_dim, state_dim, conv_kernel, expansion_factor, dropout_rate) for _ in range(num_layers)])
+        self.norm = RMSNormRef(model_dim)
+        self.lm_head = torch.nn.Linear(model_dim, vocab_size, bias=False)
+        if tie_embeddings:
+            self.lm_head.weight = self.embedding.weight
+
+    def forward(self, input_ids, block_forward=None):
+        h = self.embedding(input_ids)
+        for layer in self.layers:
+            x = layer.norm(h)
+            y = layer.mamba(x) if block_forward is None else block_forward(layer.mamba, x)
+            h = h + layer.dropout(y)
+        return self.lm_head(self.norm(h))
