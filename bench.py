@@ -46,11 +46,11 @@ def args_():
     ap.add_argument("--e2e-steps", type=int, default=5)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="CPU-baseline sample budget")
-    ap.add_argument("--workload", default="scan", choices=["scan", "block", "decode"],
+    ap.add_argument("--workload", default="scan", choices=["scan", "block", "decode", "norm"],
                     help="scan: the north-star selective scan (default); block: one MambaSimple block "
                          "(d_model 768) fwd+bwd, fused mamba_inner_fn against the reference's op sequence; "
                          "decode: a 24-layer CausalLM (d_model 768) decoding 256 tokens after a 128-token prompt "
-                         "at batch 64")
+                         "at batch 64; norm: residual add + RMSNorm fwd+bwd over 16384 x 768 bf16 rows")
     ap.add_argument("--block-path", default="both", choices=["both", "fused", "unfused"],
                     help="block workload: time both paths, or only one (for a launch list of one path)")
     return ap.parse_args()
@@ -388,6 +388,68 @@ def decode_bench(a):
     return 0
 
 
+def norm_bench(a):
+    """Residual add + RMSNorm (the reference's Block add, models/causal_lm.py:37, and RMSNorm,
+    modules/rms_norm.py:21-30) over the rows of one training step of the 24-layer config
+    (batch 8 x seqlen 2048 = 16384 rows of d_model 768, bf16), forward + backward: the fused
+    kernels against the reference's PyTorch ops.  Algorithmic bytes per row: forward reads x and
+    the residual and writes y and the sum (4 x 2 B x 768); backward reads the sum, dy and the
+    incoming residual gradient and writes dh (4 x 2 B x 768)."""
+    import torch
+
+    from mamba_b200.norm import rms_norm_fn
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    rows, dim = 16384, 768
+    g = torch.Generator().manual_seed(0)
+    x = torch.randn(rows, dim, generator=g).to(dev, torch.bfloat16).requires_grad_()
+    r = torch.randn(rows, dim, generator=g).to(dev, torch.bfloat16).requires_grad_()
+    w = (0.1 * torch.randn(dim, generator=g)).to(dev).requires_grad_()
+    dy = torch.randn(rows, dim, generator=g).to(dev, torch.bfloat16)
+    dh = torch.randn(rows, dim, generator=g).to(dev, torch.bfloat16)
+
+    def clear():  # fresh .grad every step: no accumulation kernels in either path
+        x.grad = r.grad = w.grad = None
+
+    def ref():
+        clear()
+        h = x + r
+        hf = h.float()
+        y = (hf * torch.rsqrt(hf.pow(2).mean(-1, keepdim=True) + 1e-6) * (1.0 + w.float())).type_as(h)
+        torch.autograd.backward([y, h], [dy, dh])
+
+    def fused():
+        clear()
+        y, h = rms_norm_fn(x, w, r, 1e-6, True, True)
+        torch.autograd.backward([y, h], [dy, dh])
+
+    def timed(fn):
+        for _ in range(a.warmup):
+            fn()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(a.steps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / a.steps
+
+    ms_ref, ms_f = timed(ref), timed(fused)
+    nbytes = rows * dim * 2 * 8
+    peak = load_peaks()[0]
+    line = {"workload": "norm", "metric": "residual add + RMSNorm fwd+bwd rows/s (16384 x 768, bf16)",
+            "value": rows / (ms_f / 1e3), "unit": "rows/s", "ms_per_step": ms_f,
+            "reference_ops_ms_per_step": ms_ref, "speedup_vs_reference_ops": ms_ref / ms_f,
+            "roofline": {"bound": "hbm", "algorithmic_bytes": nbytes, "achieved": nbytes / (ms_f / 1e3) / 1e9,
+                         "peak": peak, "unit": "GB/s", "frac": nbytes / (ms_f / 1e3) / 1e9 / peak,
+                         "note": "fwd + bwd kernels and the autograd glue between them, timed together"},
+            "n_gpus": 1, "higher_is_better": True, "dtype": "bf16", "data": "synthetic"}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 def _lm_hidden(model, ids, block_forward):
     h = model.embedding(ids)
     for layer in model.layers:
@@ -490,6 +552,8 @@ def main():
         return block_bench(a) if rank == 0 else 0
     if a.workload == "decode":
         return decode_bench(a) if rank == 0 else 0
+    if a.workload == "norm":
+        return norm_bench(a) if rank == 0 else 0
 
     import torch
     import torch.distributed as dist

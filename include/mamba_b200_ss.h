@@ -50,7 +50,7 @@
 extern "C" {
 #endif
 
-#define SS_ABI_VERSION 4
+#define SS_ABI_VERSION 5
 #define SS_MAX_DSTATE 16
 #define SS_MAX_CONV_WIDTH 4
 /* capacity (floats) of the library-held state array used by ss_bwd_noalloc: 16 MiB */
@@ -113,18 +113,23 @@ typedef struct ss_bwd_args {
 typedef struct ss_step_args {
   int batch, dim, dstate, ngroups;
   int dt_softplus;
-  int io_dtype;             /* dtype of x, dt, z, out                                     */
+  int io_dtype;             /* dtype of x, dt, z, out, dt_proj                            */
   int bc_dtype;             /* dtype of B, C: SS_F32 or io_dtype                          */
   float* state;      int64_t state_batch_stride;  /* (batch, dim, dstate) fp32, in/out    */
   const void* x;     int64_t x_batch_stride;      /* (batch, dim)                         */
-  const void* dt;    int64_t dt_batch_stride;     /* (batch, dim)                         */
+  const void* dt;    int64_t dt_batch_stride;     /* (batch, dim); (batch, dt_rank) with dt_proj */
   const float* A;                                 /* (dim, dstate)                        */
-  const void* B;                                  /* (batch, ngroups, dstate) contiguous  */
-  const void* C;
+  const void* B;     int64_t B_batch_stride;      /* (batch, ngroups, dstate), groups and
+                                                     states packed; batch stride in
+                                                     elements, 0 = packed                 */
+  const void* C;     int64_t C_batch_stride;
   const float* D;                                 /* nullable                             */
   const void* z;     int64_t z_batch_stride;      /* nullable                             */
   const float* dt_bias;                           /* nullable                             */
   void* out;         int64_t out_batch_stride;    /* (batch, dim)                         */
+  const void* dt_proj; int dt_rank;               /* nullable: dt = dt_in . dt_proj[c, :], dt_proj
+                                                     (dim, dt_rank) row-major, dt_rank <= 1024
+                                                     (the delta projection, fused)          */
 } ss_step_args;
 
 /* Causal depthwise convolution (+ SiLU) of the (batch, seqlen, dim) input x into the scan's
@@ -228,7 +233,9 @@ SS_API int ss_bwd(const ss_bwd_args* args, void* stream);
  * not alias an input; args->y is ignored. */
 SS_API int ss_bwd_noalloc(const ss_bwd_args* args, void* stream);
 
-/* One decode step: state <- exp(dt'*A) state + dt'*x*B; out = (C.state + D x) [* silu(z)]. */
+/* One decode step: state <- exp(dt'*A) state + dt'*x*B; out = (C.state + D x) [* silu(z)],
+ * dt' = softplus(dt + dt_bias) when dt_softplus; with dt_proj, dt is first projected from the
+ * dt_rank inputs (the reference block's delta_proj, modules/mamba_simple.py:56-60, :114). */
 SS_API int ss_step(const ss_step_args* args, void* stream);
 
 /* Convolution + SiLU on the input side of a Mamba block (see ss_conv_args). */

@@ -60,10 +60,12 @@ class StepArgs(ctypes.Structure):
         ("state", c_vp), ("state_batch_stride", c_i64),
         ("x", c_vp), ("x_batch_stride", c_i64),
         ("dt", c_vp), ("dt_batch_stride", c_i64),
-        ("A", c_vp), ("B", c_vp), ("C", c_vp), ("D", c_vp),
+        ("A", c_vp), ("B", c_vp), ("B_batch_stride", c_i64), ("C", c_vp), ("C_batch_stride", c_i64),
+        ("D", c_vp),
         ("z", c_vp), ("z_batch_stride", c_i64),
         ("dt_bias", c_vp),
         ("out", c_vp), ("out_batch_stride", c_i64),
+        ("dt_proj", c_vp), ("dt_rank", c_int),
     ]
 
 
@@ -126,7 +128,7 @@ class RmsNormBwdArgs(ctypes.Structure):
 
 # ss_struct_size index order
 STRUCTS = (FwdArgs, BwdArgs, StepArgs, ConvArgs, ConvBwdArgs, ConvStepArgs, RmsNormArgs, RmsNormBwdArgs)
-ABI_VERSION = 4
+ABI_VERSION = 5
 MAX_CONV_WIDTH = 4
 
 EXPORTS = ("ss_fwd", "ss_bwd", "ss_step", "ss_ckpt_elems", "ss_status_string",

@@ -14,11 +14,12 @@ bool aligned_rows(const void* p, int64_t stride, size_t es) {
   return p == nullptr || ((reinterpret_cast<uintptr_t>(p) & 15) == 0 && ((stride * (int64_t)es) & 15) == 0);
 }
 
-// vectors per lane: the smallest of 1, 2, 4, 8 covering the row; 0 when the row is too long
+// vectors per lane: the smallest of 1, 2, 3, 4, 6, 8 covering the row (3 fits d_model 768 in
+// bf16 exactly); 0 when the row is too long
 int vectors_per_lane(int dim, size_t es) {
   const int vw = (int)(16 / es);
   const int need = (dim + 32 * vw - 1) / (32 * vw);
-  for (int nv = 1; nv <= 8; nv <<= 1)
+  for (int nv : {1, 2, 3, 4, 6, 8})
     if (need <= nv) return nv;
   return 0;
 }
@@ -39,7 +40,9 @@ int by_dtype(int io, F&& f) {
   switch (nv) {                                                                           \
     case 1: KERNEL<IT, 1><<<grid, 32 * kNormWarps, 0, st>>>(P); break;                    \
     case 2: KERNEL<IT, 2><<<grid, 32 * kNormWarps, 0, st>>>(P); break;                    \
+    case 3: KERNEL<IT, 3><<<grid, 32 * kNormWarps, 0, st>>>(P); break;                    \
     case 4: KERNEL<IT, 4><<<grid, 32 * kNormWarps, 0, st>>>(P); break;                    \
+    case 6: KERNEL<IT, 6><<<grid, 32 * kNormWarps, 0, st>>>(P); break;                    \
     default: KERNEL<IT, 8><<<grid, 32 * kNormWarps, 0, st>>>(P); break;                   \
   }                                                                                       \
   return cudaGetLastError();

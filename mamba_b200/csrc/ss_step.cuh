@@ -1,6 +1,7 @@
 // Single-token decode step (no counterpart in the reference, whose generate() is a stub,
 // models/causal_lm.py:61-62): one step of the forward recurrence from a stored state,
-//   dt'      = softplus(dt + dt_bias)   (threshold 20, as forward_kernel.cu:216-221)
+//   dt'      = softplus(dt + dt_bias)   (threshold 20, as forward_kernel.cu:216-221), where dt
+//              is optionally the delta projection dt_in . dt_proj[c, :] computed here
 //   state[n] = exp(dt' A[c,n]) state[n] + dt' x B[n]
 //   out      = (sum_n C[n] state[n] + D x) [* silu(z)]
 // Bandwidth-bound on the fp32 state (read + write 8 B per (b, c, n)).  TPC threads per
@@ -25,15 +26,25 @@ __global__ void __launch_bounds__(128) ss_step_kernel(const __grid_constant__ ss
   const bool bc_f32 = a.bc_dtype == SS_F32;
 
   float xv = 0.f, dv = 0.f, zv = 0.f;
+  if (a.dt_proj != nullptr) {
+    // fused delta projection: the channel's TPC lanes split the dt_rank-long dot product
+    const IT* din = (const IT*)a.dt + (int64_t)b * a.dt_batch_stride;
+    const IT* wrow = (const IT*)a.dt_proj + (int64_t)cc * a.dt_rank;
+    for (int r = q; r < a.dt_rank; r += TPC) dv = fmaf(to_f<IT>(din[r]), to_f<IT>(wrow[r]), dv);
+#pragma unroll
+    for (int o = 1; o < TPC; o <<= 1) dv += __shfl_xor_sync(0xffffffffu, dv, o);
+  }
   if (ok) {
     xv = to_f<IT>(((const IT*)a.x)[(int64_t)b * a.x_batch_stride + c]);
-    dv = to_f<IT>(((const IT*)a.dt)[(int64_t)b * a.dt_batch_stride + c]);
+    if (a.dt_proj == nullptr) dv = to_f<IT>(((const IT*)a.dt)[(int64_t)b * a.dt_batch_stride + c]);
     if (a.dt_bias != nullptr) dv += a.dt_bias[c];
     if (a.z != nullptr) zv = to_f<IT>(((const IT*)a.z)[(int64_t)b * a.z_batch_stride + c]);
   }
   const float dt = a.dt_softplus ? softplus_thr(dv) : dv;
   float* st = a.state + (int64_t)b * a.state_batch_stride + (int64_t)cc * N;
-  const int64_t bco = ((int64_t)b * a.ngroups + g) * N;
+  const int64_t bsb = a.B_batch_stride ? a.B_batch_stride : (int64_t)a.ngroups * N;
+  const int64_t bsc = a.C_batch_stride ? a.C_batch_stride : (int64_t)a.ngroups * N;
+  const int64_t bob = (int64_t)b * bsb + (int64_t)g * N, boc = (int64_t)b * bsc + (int64_t)g * N;
 
   float y = 0.f;
   if (ok) {
@@ -50,8 +61,8 @@ __global__ void __launch_bounds__(128) ss_step_kernel(const __grid_constant__ ss
     for (int j = 0; j < kSPW; ++j) {
       const int n = 4 * q + j;
       if (n < N) {
-        const float Bn = bc_f32 ? ((const float*)a.B)[bco + n] : to_f<IT>(((const IT*)a.B)[bco + n]);
-        const float Cn = bc_f32 ? ((const float*)a.C)[bco + n] : to_f<IT>(((const IT*)a.C)[bco + n]);
+        const float Bn = bc_f32 ? ((const float*)a.B)[bob + n] : to_f<IT>(((const IT*)a.B)[bob + n]);
+        const float Cn = bc_f32 ? ((const float*)a.C)[boc + n] : to_f<IT>(((const IT*)a.C)[boc + n]);
         s[j] = fmaf(exp_fast(dt * a.A[(int64_t)c * N + n]), s[j], dt * xv * Bn);
         y = fmaf(Cn, s[j], y);
       }

@@ -65,9 +65,9 @@ def mamba_simple_step(block, hidden, conv_state, ssm_state, params: _BlockParams
     x, z = xz[:, :p.d], xz[:, p.d:]
     u = conv_step(conv_state, x, p.conv_w, p.conv_b)                 # (b, d)
     dbl = torch.nn.functional.linear(u, block.ssm_param_proj.weight)  # (b, R + 2N)
-    dt = torch.nn.functional.linear(dbl[:, :p.R], block.delta_proj.weight)
-    B, C = dbl[:, p.R:p.R + p.n], dbl[:, p.R + p.n:]
-    y = selective_state_update(ssm_state, u, dt, p.A, B, C, p.D, z=z, dt_bias=p.dt_bias, dt_softplus=True)
+    # B, C read in place from dbl; the delta projection runs inside the step kernel
+    y = selective_state_update(ssm_state, u, dbl[:, :p.R], p.A, dbl[:, p.R:p.R + p.n], dbl[:, p.R + p.n:], p.D,
+                               z=z, dt_bias=p.dt_bias, dt_softplus=True, dt_proj_weight=block.delta_proj.weight)
     return block.output_proj(y)
 
 

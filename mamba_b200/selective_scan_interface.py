@@ -221,14 +221,17 @@ def selective_scan_fn(u, delta, A, B, C, D=None, z=None, delta_bias=None, delta_
 
 
 # ----------------------------------------------------------------------------- decode
-def selective_state_update(state, x, dt, A, B, C, D=None, z=None, dt_bias=None, dt_softplus=False):
+def selective_state_update(state, x, dt, A, B, C, D=None, z=None, dt_bias=None, dt_softplus=False,
+                           dt_proj_weight=None):
     """One decode step; updates ``state`` (batch, dim, dstate) fp32 in place.
 
-    x, dt, z: (batch, dim); A: (dim, dstate); B, C: (batch, dstate) or (batch, ngroups, dstate);
-    D, dt_bias: (dim,).  Returns out (batch, dim) in x's dtype:
+    x, dt, z: (batch, dim); A: (dim, dstate); B, C: (batch, dstate) or (batch, ngroups, dstate)
+    (any batch stride; groups and states packed); D, dt_bias: (dim,).  With ``dt_proj_weight``
+    (dim, dt_rank), dt is (batch, dt_rank) and is projected inside the kernel (the block's
+    delta_proj without its bias, which is dt_bias).  Returns out (batch, dim) in x's dtype:
     out = (C . state' + D x) [* silu(z)], state' = exp(dt' A) state + dt' x B.
     """
-    dev = _cuda_device(state, x, dt, A, B, C, D, z, dt_bias)
+    dev = _cuda_device(state, x, dt, A, B, C, D, z, dt_bias, dt_proj_weight)
     if state.dtype != torch.float32 or state.stride(-1) != 1 or state.stride(-2) != state.shape[-1]:
         raise ValueError("state must be float32 with contiguous (dim, dstate) rows")
     b, d, n = state.shape
@@ -239,6 +242,13 @@ def selective_state_update(state, x, dt, A, B, C, D=None, z=None, dt_bias=None, 
     zs = None if z is None else (z if z.dtype == io else z.to(io))
     if zs is not None and zs.stride(-1) != 1:
         zs = zs.contiguous()
+    W, rank = None, 0
+    if dt_proj_weight is not None:
+        W = dt_proj_weight if dt_proj_weight.dtype == io else dt_proj_weight.to(io)
+        W = W.contiguous()
+        rank = W.shape[1]
+        if W.shape[0] != d or dts.shape[-1] != rank:
+            raise ValueError(f"dt_proj_weight must be (dim, dt_rank) and dt (batch, dt_rank)")
     if B.dim() == 2:
         B, C = B.unsqueeze(1), C.unsqueeze(1)
     ng = B.shape[1]
@@ -246,14 +256,19 @@ def selective_state_update(state, x, dt, A, B, C, D=None, z=None, dt_bias=None, 
         bc = L.dtype_code(io)
     else:
         B, C, bc = B.float(), C.float(), L.SS_F32
-    B, C = B.contiguous(), C.contiguous()
+
+    def packed_rows(M):  # groups and states contiguous within a batch row; any batch stride
+        return M if (M.stride(2) == 1 and M.stride(1) == n) else M.contiguous()
+
+    B, C = packed_rows(B), packed_rows(C)
     Af, Df, bf = _f32(A), _f32(D), _f32(dt_bias)
     out = torch.empty((b, d), dtype=io, device=dev)
     args = L.StepArgs(b, d, n, ng, int(bool(dt_softplus)), L.dtype_code(io), bc,
                       state.data_ptr(), state.stride(0), xs.data_ptr(), xs.stride(0),
-                      dts.data_ptr(), dts.stride(0), Af.data_ptr(), B.data_ptr(), C.data_ptr(),
+                      dts.data_ptr(), dts.stride(0), Af.data_ptr(), B.data_ptr(), B.stride(0),
+                      C.data_ptr(), C.stride(0),
                       L.ptr(Df), L.ptr(zs), zs.stride(0) if zs is not None else 0, L.ptr(bf),
-                      out.data_ptr(), out.stride(0))
+                      out.data_ptr(), out.stride(0), L.ptr(W), rank)
     with torch.cuda.device(dev):
         L.check(L.lib().ss_step(args, L.stream_of(dev)), "ss_step")
     return out

@@ -67,3 +67,32 @@ def test_prompt_then_steps_equals_full_forward(dtype):
     rtol, atol = TOL[dtype]
     assert_close("stepped outputs", stepped, full[..., P:], rtol, atol)
     assert_close("final state", state, full_last, 1e-4, 1e-5)
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("n,rank", [(16, 48), (8, 5), (4, 33)])
+def test_step_fused_dt_projection_and_strided_bc(dtype, n, rank):
+    """dt_proj_weight projects dt inside the kernel, and B / C may be column slices of one
+    (batch, rank + 2N) projection output: the same step as projecting first with a GEMM and
+    passing packed B / C (which rounds dt to the I/O dtype first, hence the I/O tolerance)."""
+    import mamba_b200
+
+    g = torch.Generator().manual_seed(n + rank)
+    b, d = 5, 72
+    st0 = torch.randn(b, d, n, generator=g).cuda()
+    x = torch.randn(b, d, generator=g).to(dtype).cuda()
+    z = torch.randn(b, d, generator=g).to(dtype).cuda()
+    dbl = torch.randn(b, rank + 2 * n, generator=g).to(dtype).cuda()
+    W = (0.3 * torch.randn(d, rank, generator=g)).to(dtype).cuda()
+    A = (-torch.rand(d, n, generator=g) - 0.5).cuda()
+    D = torch.randn(d, generator=g).cuda()
+    bias = (torch.randn(d, generator=g) - 2).cuda()
+    dt_full = (dbl[:, :rank].float() @ W.float().t())  # fp32, as the kernel accumulates
+    s1, s2 = st0.clone(), st0.clone()
+    y1 = mamba_b200.selective_state_update(s1, x, dt_full, A, dbl[:, rank:rank + n].contiguous(),
+                                           dbl[:, rank + n:].contiguous(), D, z=z, dt_bias=bias, dt_softplus=True)
+    y2 = mamba_b200.selective_state_update(s2, x, dbl[:, :rank], A, dbl[:, rank:rank + n], dbl[:, rank + n:], D,
+                                           z=z, dt_bias=bias, dt_softplus=True, dt_proj_weight=W)
+    rtol, atol = TOL[dtype]
+    assert_close("state", s2, s1, rtol, atol)
+    assert_close("out", y2, y1, rtol, atol)
