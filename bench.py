@@ -51,6 +51,9 @@ def args_():
                          "(d_model 768) fwd+bwd, fused mamba_inner_fn against the reference's op sequence; "
                          "decode: a 24-layer CausalLM (d_model 768) decoding 256 tokens after a 128-token prompt "
                          "at batch 64; norm: residual add + RMSNorm fwd+bwd over 16384 x 768 bf16 rows")
+    ap.add_argument("--decode-tokens", type=int, default=256, help="decode workload: new tokens per sequence")
+    ap.add_argument("--decode-no-cache-tokens", type=int, default=8,
+                    help="decode workload: tokens timed for the no-cache alternative (0 skips it)")
     ap.add_argument("--block-path", default="both", choices=["both", "fused", "unfused"],
                     help="block workload: time both paths, or only one (for a launch list of one path)")
     return ap.parse_args()
@@ -323,7 +326,7 @@ def decode_bench(a):
 
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
-    vocab, dm, layers, b, L0, T = 32000, 768, 24, 64, 128, 256
+    vocab, dm, layers, b, L0, T = 32000, 768, 24, 64, 128, a.decode_tokens
     torch.manual_seed(0)
     model = _causal_lm(vocab, dm, layers).to(dev, torch.bfloat16).eval()
     prompt = torch.randint(0, vocab, (b, L0), generator=torch.Generator().manual_seed(1)).to(dev)
@@ -337,8 +340,7 @@ def decode_bench(a):
         tok = logits.argmax(-1)
         for _ in range(a.warmup):  # warm-up steps (the graph is captured on the first)
             tok = dec.step(tok).argmax(-1)
-        dec = Decoder(model, b, cuda_graph=cuda_graph)
-        torch.cuda.synchronize()
+        torch.cuda.synchronize()  # the timed run reuses this decoder: prefill overwrites its states
         e0, e1, e2 = ev(), ev(), ev()
         with ClockSampler(dev.index) as clk:
             e0.record()
@@ -354,18 +356,21 @@ def decode_bench(a):
     with torch.no_grad():
         pre_g, dec_g, clocks = run(True)
         _, dec_e, _ = run(False)
-        ids = torch.cat([prompt, prompt[:, :8]], 1)
-        fwd = lambda L: model.lm_head(_lm_hidden(model, ids[:, :L], mamba_simple_forward)[:, -1])
-        for _ in range(2):
-            fwd(L0 + 1)
-        torch.cuda.synchronize()
-        e0, e1 = ev(), ev()
-        e0.record()
-        for i in range(8):
-            fwd(L0 + 1 + i).argmax(-1)
-        e1.record()
-        torch.cuda.synchronize()
-        naive_ms = e0.elapsed_time(e1) / 8
+        nc = a.decode_no_cache_tokens
+        naive_ms = float("nan")
+        if nc > 0:
+            ids = torch.cat([prompt, prompt[:, :nc]], 1)
+            fwd = lambda L: model.lm_head(_lm_hidden(model, ids[:, :L], mamba_simple_forward)[:, -1])
+            for _ in range(2):
+                fwd(L0 + 1)
+            torch.cuda.synchronize()
+            e0, e1 = ev(), ev()
+            e0.record()
+            for i in range(nc):
+                fwd(L0 + 1 + i).argmax(-1)
+            e1.record()
+            torch.cuda.synchronize()
+            naive_ms = e0.elapsed_time(e1) / nc
     n_params = sum(p.numel() for p in model.parameters())
     d, n = 2 * dm, 16
     step_bytes = 2 * n_params + layers * b * d * (n + 3) * 4 * 2  # weights once + SSM / conv states in and out

@@ -93,6 +93,8 @@ __global__ void __launch_bounds__(32 * kNormWarps) rmsnorm_fwd_kernel(const __gr
   const int row = blockIdx.x * kNormWarps + (threadIdx.x >> 5);
   if (row >= a.rows) return;
   const int dim = a.dim;
+  float w[NV][VW];  // issued first: its latency overlaps the row loads
+  load_weight<NV, VW>(w, a.weight, dim, lane, a.unit_offset != 0);
   float h[NV][VW];
   row_load<IT, NV>(h, (const IT*)a.x + (int64_t)row * a.x_row_stride, dim, lane, P.vec);
   if (a.residual != nullptr) {
@@ -111,8 +113,6 @@ __global__ void __launch_bounds__(32 * kNormWarps) rmsnorm_fwd_kernel(const __gr
 #pragma unroll
     for (int k = 0; k < VW; ++k) ss = fmaf(h[j][k], h[j][k], ss);
   const float rstd = rsqrtf(warp_sum(ss) / (float)dim + a.eps);
-  float w[NV][VW];
-  load_weight<NV, VW>(w, a.weight, dim, lane, a.unit_offset != 0);
 #pragma unroll
   for (int j = 0; j < NV; ++j)
 #pragma unroll

@@ -26,11 +26,31 @@ __global__ void __launch_bounds__(128) ss_step_kernel(const __grid_constant__ ss
   const bool bc_f32 = a.bc_dtype == SS_F32;
 
   float xv = 0.f, dv = 0.f, zv = 0.f;
+  float* st = a.state + (int64_t)b * a.state_batch_stride + (int64_t)cc * N;
+  // issue the state load before the dt work, so its DRAM latency overlaps it
+  const bool vec = (N % 4) == 0 && ((reinterpret_cast<uintptr_t>(st) & 15) == 0);
+  float s[kSPW];
+  if (ok && vec && 4 * q < N) {
+    const float4 v = *reinterpret_cast<const float4*>(st + 4 * q);
+    s[0] = v.x; s[1] = v.y; s[2] = v.z; s[3] = v.w;
+  } else {
+#pragma unroll
+    for (int j = 0; j < kSPW; ++j) s[j] = (ok && 4 * q + j < N) ? st[4 * q + j] : 0.f;
+  }
   if (a.dt_proj != nullptr) {
-    // fused delta projection: the channel's TPC lanes split the dt_rank-long dot product
+    // fused delta projection: the channel's TPC lanes split the dt_rank-long dot product,
+    // two independent accumulators per lane
     const IT* din = (const IT*)a.dt + (int64_t)b * a.dt_batch_stride;
     const IT* wrow = (const IT*)a.dt_proj + (int64_t)cc * a.dt_rank;
-    for (int r = q; r < a.dt_rank; r += TPC) dv = fmaf(to_f<IT>(din[r]), to_f<IT>(wrow[r]), dv);
+    float d1 = 0.f;
+    int r = q;
+#pragma unroll 4
+    for (; r + TPC < a.dt_rank; r += 2 * TPC) {
+      dv = fmaf(to_f<IT>(din[r]), to_f<IT>(wrow[r]), dv);
+      d1 = fmaf(to_f<IT>(din[r + TPC]), to_f<IT>(wrow[r + TPC]), d1);
+    }
+    if (r < a.dt_rank) dv = fmaf(to_f<IT>(din[r]), to_f<IT>(wrow[r]), dv);
+    dv += d1;
 #pragma unroll
     for (int o = 1; o < TPC; o <<= 1) dv += __shfl_xor_sync(0xffffffffu, dv, o);
   }
@@ -41,22 +61,12 @@ __global__ void __launch_bounds__(128) ss_step_kernel(const __grid_constant__ ss
     if (a.z != nullptr) zv = to_f<IT>(((const IT*)a.z)[(int64_t)b * a.z_batch_stride + c]);
   }
   const float dt = a.dt_softplus ? softplus_thr(dv) : dv;
-  float* st = a.state + (int64_t)b * a.state_batch_stride + (int64_t)cc * N;
   const int64_t bsb = a.B_batch_stride ? a.B_batch_stride : (int64_t)a.ngroups * N;
   const int64_t bsc = a.C_batch_stride ? a.C_batch_stride : (int64_t)a.ngroups * N;
   const int64_t bob = (int64_t)b * bsb + (int64_t)g * N, boc = (int64_t)b * bsc + (int64_t)g * N;
 
   float y = 0.f;
   if (ok) {
-    float s[kSPW];
-    const bool vec = (N % 4) == 0 && ((reinterpret_cast<uintptr_t>(st) & 15) == 0);
-    if (vec && 4 * q < N) {
-      const float4 v = *reinterpret_cast<const float4*>(st + 4 * q);
-      s[0] = v.x; s[1] = v.y; s[2] = v.z; s[3] = v.w;
-    } else {
-#pragma unroll
-      for (int j = 0; j < kSPW; ++j) s[j] = (4 * q + j < N) ? st[4 * q + j] : 0.f;
-    }
 #pragma unroll
     for (int j = 0; j < kSPW; ++j) {
       const int n = 4 * q + j;

@@ -25,7 +25,7 @@ from __future__ import annotations
 import torch
 
 from .inner import conv_step, mamba_inner_prefill
-from .norm import rms_norm
+from .norm import rms_norm_fn
 from .selective_scan_interface import selective_state_update
 
 
@@ -82,6 +82,9 @@ class Decoder:
         self.model = model
         self.batch = batch
         self.params = [_BlockParams(layer.mamba) for layer in model.layers]
+        # fp32 norm weights, cast once (a per-call cast would be one more kernel per layer and step)
+        self.norms = [(layer.norm.weight.detach().float().contiguous(), layer.norm.eps) for layer in model.layers]
+        self.final_norm = (model.norm.weight.detach().float().contiguous(), model.norm.eps)
         dev = model.lm_head.weight.device
         self.conv_states = [torch.zeros(batch, p.d, p.K - 1, device=dev) for p in self.params]
         self.ssm_states = [torch.zeros(batch, p.d, p.n, device=dev) for p in self.params]
@@ -99,20 +102,26 @@ class Decoder:
         res = y = None
         for i, layer in enumerate(m.layers):
             # the residual add of the previous block fused with this block's RMSNorm
-            x, res = rms_norm(layer.norm, h if res is None else y, residual=res, prenorm=True)
+            x, res = self._norm(i, h if res is None else y, res)
             y, cs, ss = mamba_simple_prefill(layer.mamba, x, self.params[i])
             self.conv_states[i].copy_(cs)
             self.ssm_states[i].copy_(ss)
-        return m.lm_head(rms_norm(m.norm, y[:, -1], residual=res[:, -1])).float()
+        w, eps = self.final_norm
+        return m.lm_head(rms_norm_fn(y[:, -1], w, res[:, -1], eps)).float()
+
+    def _norm(self, i, x, res):
+        w, eps = self.norms[i]
+        return rms_norm_fn(x, w, res, eps, True, True)
 
     def _step_eager(self, tok):
         m = self.model
         h = m.embedding(tok)
         res = y = None
         for i, layer in enumerate(m.layers):
-            x, res = rms_norm(layer.norm, h if res is None else y, residual=res, prenorm=True)
+            x, res = self._norm(i, h if res is None else y, res)
             y = mamba_simple_step(layer.mamba, x, self.conv_states[i], self.ssm_states[i], self.params[i])
-        return m.lm_head(rms_norm(m.norm, y, residual=res)).float()
+        w, eps = self.final_norm
+        return m.lm_head(rms_norm_fn(y, w, res, eps)).float()
 
     @torch.no_grad()
     def step(self, token_ids):
