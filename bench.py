@@ -43,7 +43,7 @@ def args_():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="mamba_b200", choices=["mamba_b200", "reference"])
-    ap.add_argument("--e2e-steps", type=int, default=5)
+    ap.add_argument("--e2e-steps", type=int, default=10)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="CPU-baseline sample budget")
     ap.add_argument("--workload", default="scan", choices=["scan", "block", "decode", "norm"],
@@ -625,32 +625,64 @@ def main():
     tokens_job = b * L * world
     value = tokens_job / (ms_step / 1e3)
 
-    # ---- end to end: pinned host inputs in, every result out, through the public operator
+    # ---- end to end: pinned host inputs in, every result out, through the public operator.
+    # Steps are independent, so the loop is pipelined over three streams: step i+1's inputs are
+    # copied in while step i computes, and step i's results are copied out while step i+1
+    # computes (the host link is full duplex).  Every step still moves all of its bytes both
+    # ways; inputs alternate between two device buffer sets.
+    names = ("u", "delta", "z", "B", "C", "dout", "A", "D", "delta_bias")
     pin = {k: v.pin_memory() for k, v in host.items()}
-    dbuf = {k: torch.empty_like(v, device=dev) for k, v in host.items()}
-    outs_host = None
+    bufs = [{k: torch.empty_like(v, device=dev) for k, v in host.items()} for _ in range(2)]
+    s_in, s_cmp, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev), torch.cuda.Stream(dev)
     E = max(1, a.e2e_steps)
-    h2d = sum(v.numel() * v.element_size() for k, v in pin.items() if k in ("u", "delta", "z", "B", "C", "dout"))
+    h2d = sum(pin[k].numel() * pin[k].element_size() for k in names)
+    outs_host = []
+
+    def e2e_run(nsteps, t_start=None, t_end=None):
+        in_done, cmp_done = [None] * nsteps, [None] * nsteps
+
+        def copy_in(i):
+            with torch.cuda.stream(s_in):
+                if i >= 2:
+                    s_in.wait_event(cmp_done[i - 2])  # step i-2 has finished reading this buffer set
+                for k in names:
+                    bufs[i % 2][k].copy_(pin[k], non_blocking=True)
+                in_done[i] = torch.cuda.Event()
+                in_done[i].record(s_in)
+
+        if t_start is not None:
+            t_start.record(s_in)
+        copy_in(0)
+        nbytes = 0
+        for i in range(nsteps):
+            if i + 1 < nsteps:
+                copy_in(i + 1)
+            with torch.cuda.stream(s_cmp):
+                s_cmp.wait_event(in_done[i])
+                t = {k: bufs[i % 2][k].detach().requires_grad_(k in leaves) for k in names}
+                out = step(t)
+                out.backward(t["dout"])
+                res = [out.detach()] + [t[k].grad for k in leaves]
+                cmp_done[i] = torch.cuda.Event()
+                cmp_done[i].record(s_cmp)
+            if not outs_host:
+                outs_host.extend(torch.empty(r.shape, dtype=r.dtype, pin_memory=True) for r in res)
+            with torch.cuda.stream(s_out):
+                s_out.wait_event(cmp_done[i])
+                for hbuf, r in zip(outs_host, res):
+                    hbuf.copy_(r, non_blocking=True)
+                    r.record_stream(s_out)  # allocated on the compute stream, read here
+            nbytes = sum(r.numel() * r.element_size() for r in res)
+        if t_end is not None:
+            t_end.record(s_out)  # s_out's last copy waited on the last compute, which waited on its inputs
+        return nbytes
+
+    e2e_run(2)  # warm-up: pinned output buffers, stream pools
+    torch.cuda.synchronize()
     barrier()
     torch.cuda.synchronize()
     s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    d2h = 0
-    for i in range(E + 1):  # first iteration warms the pinned output buffers
-        if i == 1:
-            torch.cuda.synchronize()
-            s0.record()
-        for k in ("u", "delta", "z", "B", "C", "dout", "A", "D", "delta_bias"):
-            dbuf[k].copy_(pin[k], non_blocking=True)
-        t = {k: dbuf[k].detach().requires_grad_(k in leaves) for k in dbuf}
-        out = step(t)
-        out.backward(t["dout"])
-        res = [out.detach()] + [t[k].grad for k in leaves]
-        if outs_host is None:
-            outs_host = [torch.empty(r.shape, dtype=r.dtype, pin_memory=True) for r in res]
-        for hbuf, r in zip(outs_host, res):
-            hbuf.copy_(r, non_blocking=True)
-        d2h = sum(r.numel() * r.element_size() for r in res)
-    s1.record()
+    d2h = e2e_run(E, s0, s1)
     torch.cuda.synchronize()
     e2e_ms = s0.elapsed_time(s1) / E
     if world > 1:
@@ -679,6 +711,7 @@ def main():
                      "frac": achieved / peak, "peak_source": peak_kind,
                      "algorithmic_bytes_per_launch": dom_bytes, "traffic": profile_traffic()},
         "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                "pipeline": "copy-in, compute and copy-out of consecutive steps on three streams",
                 "ms_per_step": e2e_ms},
         "gpu_launches": 2 * K,
         "clocks": clk.summary(),
