@@ -46,11 +46,12 @@ def args_():
     ap.add_argument("--e2e-steps", type=int, default=10)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="CPU-baseline sample budget")
-    ap.add_argument("--workload", default="scan", choices=["scan", "block", "decode", "norm"],
+    ap.add_argument("--workload", default="scan", choices=["scan", "block", "decode", "norm", "model"],
                     help="scan: the north-star selective scan (default); block: one MambaSimple block "
                          "(d_model 768) fwd+bwd, fused mamba_inner_fn against the reference's op sequence; "
                          "decode: a 24-layer CausalLM (d_model 768) decoding 256 tokens after a 128-token prompt "
-                         "at batch 64; norm: residual add + RMSNorm fwd+bwd over 16384 x 768 bf16 rows")
+                         "at batch 64; norm: residual add + RMSNorm fwd+bwd over 16384 x 768 bf16 rows; "
+                         "model: one training step (fwd+bwd, cross-entropy) of the 24-layer CausalLM")
     ap.add_argument("--decode-tokens", type=int, default=256, help="decode workload: new tokens per sequence")
     ap.add_argument("--decode-no-cache-tokens", type=int, default=8,
                     help="decode workload: tokens timed for the no-cache alternative (0 skips it)")
@@ -455,6 +456,86 @@ def norm_bench(a):
     return 0
 
 
+def model_bench(a):
+    """One training step (forward, cross-entropy over the vocabulary, backward; no optimizer)
+    of the 24-layer CausalLM config (d_model 768, d_inner 1536, N 16, vocab 32000) at batch 8 x
+    seqlen 2048, bf16 parameters, two ways on the same model and tokens:
+      fused:     mamba_b200.causal_lm_forward (fused blocks; residual add fused with RMSNorm);
+      reference: the reference CausalLM's own forward structure (models/causal_lm.py:30-58: torch
+                 RMSNorm, MambaSimple's op sequence with its permute copies,
+                 modules/mamba_simple.py:87-151) with mamba_b200's scan as its SelectiveScanFn —
+                 what the reference runs after the drop-in alone."""
+    import torch
+    import torch.nn.functional as F
+
+    import mamba_b200
+    from mamba_b200 import causal_lm_forward
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    vocab, dm, layers, b, L = 32000, 768, 24, 8, 2048
+    d, n, K = 2 * dm, 16, 4
+    R = math.ceil(dm / 16)
+    torch.manual_seed(0)
+    model = _causal_lm(vocab, dm, layers).to(dev, torch.bfloat16).train()
+    ids = torch.randint(0, vocab, (b, L + 1), generator=torch.Generator().manual_seed(1)).to(dev)
+    inp, tgt = ids[:, :-1], ids[:, 1:]
+
+    def mamba_ref(blk, x):  # modules/mamba_simple.py:87-151
+        xs, zs = torch.chunk(blk.input_proj(x).permute(0, 2, 1).contiguous(), 2, dim=1)
+        xs = F.silu(blk.short_conv(xs)[..., :L])
+        dbl = blk.ssm_param_proj(xs.permute(0, 2, 1).contiguous().view(b * L, d))
+        dr, B, C = torch.split(dbl, [R, n, n], dim=-1)
+        delta = (blk.delta_proj.weight @ dr.t()).view(d, b, L).permute(1, 0, 2).contiguous()
+        B = B.view(b, L, n).permute(0, 2, 1).contiguous().unsqueeze(1)
+        C = C.view(b, L, n).permute(0, 2, 1).contiguous().unsqueeze(1)
+        y = mamba_b200.selective_scan_fn(xs, delta, -torch.exp(blk.log_A.float()), B, C, blk.D.float(), None,
+                                         blk.delta_proj.bias.float(), True)
+        hs = y.permute(0, 2, 1).contiguous()
+        hs = hs * F.silu(zs.permute(0, 2, 1).contiguous())
+        return blk.output_proj(hs)
+
+    def ref_forward(x_ids):  # models/causal_lm.py:30-58
+        h = model.embedding(x_ids)
+        for layer in model.layers:
+            r = h
+            h = mamba_ref(layer.mamba, layer.norm(h)) + r
+        return model.lm_head(model.norm(h))
+
+    def timed(fwd):
+        def step():
+            loss = F.cross_entropy(fwd(inp).float().view(-1, vocab), tgt.reshape(-1))
+            loss.backward()
+            for p_ in model.parameters():
+                p_.grad = None
+        for _ in range(a.warmup):
+            step()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with ClockSampler(dev.index) as clk:
+            e0.record()
+            for _ in range(a.steps):
+                step()
+            e1.record()
+            torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / a.steps, clk.summary()
+
+    ms_ref, _ = timed(ref_forward)
+    ms_f, clocks = timed(lambda x: causal_lm_forward(model, x))
+    tokens = b * L
+    line = {"workload": "model", "metric": "24-layer CausalLM training step tokens/s (fwd + bwd, batch 8 x 2048)",
+            "value": tokens / (ms_f / 1e3), "unit": "tokens/s", "ms_per_step": ms_f,
+            "reference_structure_value": tokens / (ms_ref / 1e3), "reference_structure_ms_per_step": ms_ref,
+            "speedup_vs_reference_structure": ms_ref / ms_f, "n_gpus": 1, "steps": a.steps, "warmup": a.warmup,
+            "higher_is_better": True, "dtype": "bf16", "data": "synthetic (random weights and tokens)",
+            "config": {"workload": "CausalLM 24 layers, d_model 768, d_inner 1536, d_state 16, vocab 32000 (tied), "
+                                   "batch 8, seqlen 2048, bf16 parameters, cross-entropy loss, no optimizer step",
+                       "params": sum(p_.numel() for p_ in model.parameters())},
+            "clocks": clocks}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 def _lm_hidden(model, ids, block_forward):
     h = model.embedding(ids)
     for layer in model.layers:
@@ -559,6 +640,8 @@ def main():
         return decode_bench(a) if rank == 0 else 0
     if a.workload == "norm":
         return norm_bench(a) if rank == 0 else 0
+    if a.workload == "model":
+        return model_bench(a) if rank == 0 else 0
 
     import torch
     import torch.distributed as dist
