@@ -63,10 +63,14 @@ struct BwdSmem {
   alignas(16) float4 sig_s[kCh][4];
   alignas(16) float4 gz_s[kHasZ ? kCh : 1][4];
   alignas(16) float B_s[kVarB ? kTile : 1][NS];
+  float bc_pad[16];  // puts C_s rows on the other half of the banks from B_s rows
   alignas(16) float C_s[kVarC ? kTile : 1][NS];
   alignas(16) float s12_s[kNW][kTile][kS12Row];                        // (S1, S2) per channel
   alignas(16) float fold[(kVarB || kVarC) ? kNW : 1][16 * 64];         // 4 steps x 2 pairs x B|C
-  alignas(16) float fout[(kVarB || kVarC) ? kNW : 1][2][kSPW][kTile];  // [B|C][j][t] sums
+  // per-warp channel sums of the tile: row k = (2 * pair + h) * 2 + (B|C), step t stored at
+  // t ^ (4 * (k >> 1)), which makes the fold's scattered writes conflict-free while every
+  // aligned group of 4 steps stays contiguous for the 16-byte reads
+  alignas(16) float fout[(kVarB || kVarC) ? kNW : 1][2 * kSPW][kTile];
   alignas(8) uint64_t full[kStagesBwd<IT>];
 };
 
@@ -175,8 +179,7 @@ __global__ void __launch_bounds__(32 * kNW, 3) ss_bwd_kernel(const __grid_consta
     float2 hp[kTile + 1][2];
     if constexpr (kTMA) {
       failed = !mbar_wait_bounded(&sm.full[stg], (it / kStagesBwd<IT>) & 1);
-      if constexpr (kVarB) widen_bc<IT, NT, NS>(sm.B_s, reinterpret_cast<const float*>(sm.Braw[stg]), false);
-      if constexpr (kVarC) widen_bc<IT, NT, NS>(sm.C_s, reinterpret_cast<const float*>(sm.Craw[stg]), false);
+      if (w == 0) widen_bc_warp<IT, NS, kVarB, kVarC>(sm.B_s, sm.C_s, sm.Braw[stg], sm.Craw[stg], false, lane);
 #pragma unroll
       for (int p = 0; p < 2; ++p)
         hp[0][p] = (k > 0) ? make_float2(sm.hck[stg][kSPW * w + 2 * p][lane], sm.hck[stg][kSPW * w + 2 * p + 1][lane])
@@ -366,7 +369,8 @@ __global__ void __launch_bounds__(32 * kNW, 3) ss_bwd_kernel(const __grid_consta
         acc.x += __shfl_xor_sync(0xffffffffu, acc.x, 1);
         acc.y += __shfl_xor_sync(0xffffffffu, acc.y, 1);
         const int st = r >> 2, p = (r >> 1) & 1;
-        sm.fout[w][type][2 * p + h][4 * i4 + st] = h ? acc.y : acc.x;
+        const int k = (2 * p + h) * 2 + type;
+        sm.fout[w][k][(4 * i4 + st) ^ (4 * (k >> 1))] = h ? acc.y : acc.x;
         __syncwarp();
       }
     }
@@ -377,7 +381,8 @@ __global__ void __launch_bounds__(32 * kNW, 3) ss_bwd_kernel(const __grid_consta
       const int n = kSPW * w + j;
       const bool want = (type == 0) ? kVarB : kVarC;
       if (want && n < N) {
-        const float4 v = *reinterpret_cast<const float4*>(&sm.fout[w][type][j][tt]);
+        const int k = j * 2 + type;
+        const float4 v = *reinterpret_cast<const float4*>(&sm.fout[w][k][tt ^ (4 * (k >> 1))]);
         float* dst = (type == 0 ? a.dB : a.dC) + bc_off + (int64_t)n * L + t0 + tt;
         if (P.vec_dbc && tt + 4 <= tlen) {
           red_add_v4(dst, v.x, v.y, v.z, v.w);

@@ -37,18 +37,47 @@ struct FwdSmem {
   alignas(16) float4 dt_s[kCh][4];
   alignas(16) float4 dtu_s[kCh][4];
   alignas(16) float B_s[kVarB ? kTile : 1][NS];
+  float bc_pad[16];  // puts C_s rows on the other half of the banks from B_s rows
   alignas(16) float C_s[kVarC ? kTile : 1][NS];
   float y_s[kNW][kTile][kPad];
   alignas(8) uint64_t full[kStages];
 };
 
-// widen a TMA'd [n][t] tile of B or C (dtype IT or fp32) into fp32 [t][n]
-template <typename IT, int NT, int NS>
-__device__ __forceinline__ void widen_bc(float (*dst)[NS], const float* raw, bool f32) {
-  for (int i = threadIdx.x; i < NS * kTile; i += NT) {
-    const int n = i / kTile, t = i % kTile;
-    dst[t][n] = f32 ? raw[i] : to_f<IT>(reinterpret_cast<const IT*>(raw)[i]);
+// B and C tiles arrive from TMA as raw[n][t] (NS rows of kTile steps, in the I/O dtype, or fp32
+// when f32) and the scans read them as fp32 [t][n].  One warp transposes both: lane l < 16
+// owns row l of B, lane l >= 16 row l - 16 of C; it reads its row with 16-byte loads and
+// writes one column, so each store instruction covers 16 consecutive floats of a B row and 16
+// of a C row (on different bank halves: C_s is laid out 16 floats off B_s's banks).  A
+// thread-per-element mapping made every store an 8-way bank conflict.
+template <typename IT, int NS, bool kB, bool kC>
+__device__ __forceinline__ void widen_bc_warp(float (*Bd)[NS], float (*Cd)[NS], const void* Braw, const void* Craw,
+                                              bool f32, int lane) {
+  const bool isC = lane >= 16;
+  const int n = lane & 15;
+  if (n >= NS || (isC ? !kC : !kB)) return;
+  float (*dst)[NS] = isC ? Cd : Bd;
+  const void* raw = isC ? Craw : Braw;
+  float v[kTile];
+  if (f32) {
+    const float4* r = reinterpret_cast<const float4*>(static_cast<const float*>(raw) + n * kTile);
+#pragma unroll
+    for (int q = 0; q < kTile / 4; ++q) {
+      const float4 x = r[q];
+      v[4 * q] = x.x; v[4 * q + 1] = x.y; v[4 * q + 2] = x.z; v[4 * q + 3] = x.w;
+    }
+  } else {
+    constexpr int VW = 16 / sizeof(IT);
+    const uint4* r = reinterpret_cast<const uint4*>(static_cast<const IT*>(raw) + n * kTile);
+#pragma unroll
+    for (int q = 0; q < kTile / VW; ++q) {
+      const uint4 x = r[q];
+      const IT* e = reinterpret_cast<const IT*>(&x);
+#pragma unroll
+      for (int j = 0; j < VW; ++j) v[q * VW + j] = to_f<IT>(e[j]);
+    }
   }
+#pragma unroll
+  for (int t = 0; t < kTile; ++t) dst[t][n] = v[t];
 }
 
 template <typename IT, int kNW, bool kVarB, bool kVarC, bool kHasZ, bool kTMA>
@@ -141,8 +170,7 @@ __global__ void __launch_bounds__(32 * kNW, 4) ss_fwd_kernel(const __grid_consta
     bool failed = false;
     if constexpr (kTMA) {
       failed = !mbar_wait_bounded(&sm.full[stg], (k / kStages) & 1);
-      if constexpr (kVarB) widen_bc<IT, NT, NS>(sm.B_s, sm.Braw[stg], bc_f32);
-      if constexpr (kVarC) widen_bc<IT, NT, NS>(sm.C_s, sm.Craw[stg], bc_f32);
+      if (w == 0) widen_bc_warp<IT, NS, kVarB, kVarC>(sm.B_s, sm.C_s, sm.Braw[stg], sm.Craw[stg], bc_f32, lane);
     } else {
       load_tile<IT, NT>(sm.u[0], ub + t0, a.u_dim_stride, nvalid, tlen, P.vec_u);
       load_tile<IT, NT>(sm.d[0], db + t0, a.delta_dim_stride, nvalid, tlen, P.vec_d);
