@@ -23,6 +23,9 @@
  *              directly and writes the scan's (batch, dim, seqlen) layout.
  *   ss_conv_step <- no counterpart (no decode in the reference): the same convolution for
  *              one new input from a rolling state of the previous width-1 inputs.
+ *   ss_mamba_step <- no counterpart: one decode step of a MambaSimple block's mixer (conv step,
+ *              x projection, delta projection, SSM step, gate; modules/mamba_simple.py:93-146
+ *              for one token) in one kernel.
  *   ss_rmsnorm_fwd / ss_rmsnorm_bwd <- the reference's RMSNorm.forward (modules/rms_norm.py:
  *              21-30) fused with its Block's residual add (models/causal_lm.py:30-37), which
  *              the reference runs as a chain of PyTorch elementwise and reduction kernels.
@@ -50,7 +53,7 @@
 extern "C" {
 #endif
 
-#define SS_ABI_VERSION 5
+#define SS_ABI_VERSION 6
 #define SS_MAX_DSTATE 16
 #define SS_MAX_CONV_WIDTH 4
 /* capacity (floats) of the library-held state array used by ss_bwd_noalloc: 16 MiB */
@@ -211,6 +214,28 @@ typedef struct ss_rmsnorm_bwd_args {
   float* dweight;                                            /* (dim) fp32, overwritten       */
 } ss_rmsnorm_bwd_args;
 
+/* One decode step of a Mamba block's mixer, between its input and output projections:
+ *   x, z = xz[b, :dim], xz[b, dim:]
+ *   u    = silu(conv_bias + conv_weight . [conv_state, x]);  conv_state rolls in
+ *   dbl  = x_proj u  (dt_rank + 2 dstate values: dt_in, B, C)
+ *   dt   = dt_proj dt_in + dt_bias  (softplus'd when dt_softplus)
+ *   ssm_state = exp(dt A) ssm_state + dt u B;   y = (C . ssm_state + D u) * silu(z)
+ * u and dbl are rounded to the I/O dtype (as the stored activations of the prompt path). */
+typedef struct ss_mamba_step_args {
+  int batch, dim, dstate, width, dt_rank, io_dtype, dt_softplus;
+  const void* xz;        int64_t xz_batch_stride;   /* (batch, 2 dim), unit stride along dim  */
+  float* conv_state;                                 /* (batch, dim, width-1) fp32, packed     */
+  const float* conv_weight;                          /* (dim, width) fp32                      */
+  const float* conv_bias;                            /* (dim) fp32, nullable                   */
+  const void* x_proj;                                /* (dt_rank + 2 dstate, dim) row-major    */
+  const void* dt_proj;                               /* (dim, dt_rank) row-major               */
+  const float* dt_bias;                              /* (dim) fp32, nullable                   */
+  const float* A;                                    /* (dim, dstate) fp32                     */
+  const float* D;                                    /* (dim) fp32, nullable                   */
+  float* ssm_state;                                  /* (batch, dim, dstate) fp32, packed      */
+  void* y;               int64_t y_batch_stride;    /* (batch, dim): the gated output         */
+} ss_mamba_step_args;
+
 /* Number of fp32 elements of the forward-to-backward state buffer. */
 SS_API size_t ss_ckpt_elems(int batch, int dim, int seqlen, int dstate);
 
@@ -247,6 +272,9 @@ SS_API int ss_conv_bwd(const ss_conv_bwd_args* args, void* stream);
 /* One decode step of the convolution (see ss_conv_step_args). */
 SS_API int ss_conv_step(const ss_conv_step_args* args, void* stream);
 
+/* One decode step of a block's mixer (see ss_mamba_step_args). */
+SS_API int ss_mamba_step(const ss_mamba_step_args* args, void* stream);
+
 /* Residual add + RMSNorm (see ss_rmsnorm_args). */
 SS_API int ss_rmsnorm_fwd(const ss_rmsnorm_args* args, void* stream);
 
@@ -269,7 +297,8 @@ SS_API int ss_abi_version(void);
 
 /* sizeof the argument structs as compiled into the library (0: ss_fwd_args,
  * 1: ss_bwd_args, 2: ss_step_args, 3: ss_conv_args, 4: ss_conv_bwd_args,
- * 5: ss_conv_step_args, 6: ss_rmsnorm_args, 7: ss_rmsnorm_bwd_args; 0 for other values) — lets an FFI binding check its own struct
+ * 5: ss_conv_step_args, 6: ss_rmsnorm_args, 7: ss_rmsnorm_bwd_args, 8: ss_mamba_step_args;
+ * 0 for other values) — lets an FFI binding check its own struct
  * layout against the library's. */
 SS_API size_t ss_struct_size(int which);
 

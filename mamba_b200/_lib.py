@@ -126,14 +126,28 @@ class RmsNormBwdArgs(ctypes.Structure):
     ]
 
 
+class MambaStepArgs(ctypes.Structure):
+    _fields_ = [
+        ("batch", c_int), ("dim", c_int), ("dstate", c_int), ("width", c_int), ("dt_rank", c_int),
+        ("io_dtype", c_int), ("dt_softplus", c_int),
+        ("xz", c_vp), ("xz_batch_stride", c_i64),
+        ("conv_state", c_vp), ("conv_weight", c_vp), ("conv_bias", c_vp),
+        ("x_proj", c_vp), ("dt_proj", c_vp), ("dt_bias", c_vp), ("A", c_vp), ("D", c_vp),
+        ("ssm_state", c_vp),
+        ("y", c_vp), ("y_batch_stride", c_i64),
+    ]
+
+
 # ss_struct_size index order
-STRUCTS = (FwdArgs, BwdArgs, StepArgs, ConvArgs, ConvBwdArgs, ConvStepArgs, RmsNormArgs, RmsNormBwdArgs)
-ABI_VERSION = 5
+STRUCTS = (FwdArgs, BwdArgs, StepArgs, ConvArgs, ConvBwdArgs, ConvStepArgs, RmsNormArgs, RmsNormBwdArgs,
+           MambaStepArgs)
+ABI_VERSION = 6
 MAX_CONV_WIDTH = 4
 
 EXPORTS = ("ss_fwd", "ss_bwd", "ss_step", "ss_ckpt_elems", "ss_status_string",
            "ss_last_cuda_error", "ss_abi_version", "ss_struct_size", "ss_device_status",
-           "ss_bwd_noalloc", "ss_conv_fwd", "ss_conv_bwd", "ss_conv_step", "ss_rmsnorm_fwd", "ss_rmsnorm_bwd")
+           "ss_bwd_noalloc", "ss_conv_fwd", "ss_conv_bwd", "ss_conv_step", "ss_rmsnorm_fwd", "ss_rmsnorm_bwd",
+           "ss_mamba_step")
 NOALLOC_MAX_CKPT_ELEMS = 4194304  # SS_NOALLOC_MAX_CKPT_ELEMS
 
 _lib = None
@@ -161,8 +175,10 @@ def lib():
                 L.ss_conv_step.argtypes = [ctypes.POINTER(ConvStepArgs), c_vp]
                 L.ss_rmsnorm_fwd.argtypes = [ctypes.POINTER(RmsNormArgs), c_vp]
                 L.ss_rmsnorm_bwd.argtypes = [ctypes.POINTER(RmsNormBwdArgs), c_vp]
+                L.ss_mamba_step.argtypes = [ctypes.POINTER(MambaStepArgs), c_vp]
                 for f in ("ss_fwd", "ss_bwd", "ss_step", "ss_last_cuda_error", "ss_abi_version",
-                          "ss_conv_fwd", "ss_conv_bwd", "ss_conv_step", "ss_rmsnorm_fwd", "ss_rmsnorm_bwd"):
+                          "ss_conv_fwd", "ss_conv_bwd", "ss_conv_step", "ss_rmsnorm_fwd", "ss_rmsnorm_bwd",
+           "ss_mamba_step"):
                     getattr(L, f).restype = c_int
                 L.ss_ckpt_elems.argtypes = [c_int, c_int, c_int, c_int]
                 L.ss_ckpt_elems.restype = ctypes.c_size_t

@@ -284,6 +284,7 @@ size_t ss_struct_size(int which) {
     case 5: return sizeof(ss_conv_step_args);
     case 6: return sizeof(ss_rmsnorm_args);
     case 7: return sizeof(ss_rmsnorm_bwd_args);
+    case 8: return sizeof(ss_mamba_step_args);
     default: return 0;
   }
 }

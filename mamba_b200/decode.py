@@ -8,8 +8,9 @@ forward over it for every new token.  Here a block keeps two states per sequence
 * conv state (batch, d_inner, K-1) fp32 — the last K-1 inputs of its causal convolution;
 * SSM state  (batch, d_inner, d_state) fp32 — h of the selective scan,
 
-and a new token costs one step of each (``ss_conv_step``, ``ss_step`` with the SiLU(z) gate
-fused) plus the block's small projections.  The prefill runs the fused block path
+and a new token costs the block's input and output projections plus one fused mixer kernel
+(``ss_mamba_step``: the conv step, the x and delta projections, the SSM step and the SiLU(z)
+gate).  The prefill runs the fused block path
 (``mamba_inner_prefill``: conv kernel, batched GEMMs, scan with ``return_last_state``); each
 block's residual add is fused with the next RMSNorm (``rms_norm(..., prenorm=True)``); and the
 per-token model step of ``Decoder`` is captured once in a CUDA graph and replayed, so a decode
@@ -24,9 +25,10 @@ from __future__ import annotations
 
 import torch
 
-from .inner import conv_step, mamba_inner_prefill
+from . import _lib as L
+from .inner import mamba_inner_prefill
 from .norm import rms_norm_fn
-from .selective_scan_interface import selective_state_update
+from .selective_scan_interface import _cuda_device
 
 
 class _BlockParams:
@@ -57,17 +59,38 @@ def mamba_simple_prefill(block, hidden_states, params: _BlockParams | None = Non
                                True)
 
 
+def mamba_mixer_step(xz, conv_state, ssm_state, p: _BlockParams, x_proj_weight, delta_proj_weight):
+    """The mixer of one decode step (conv step, x projection, delta projection, SSM step, gate)
+    in one kernel (``ss_mamba_step``): xz (batch, 2 d) -> y (batch, d); both states update in
+    place."""
+    _cuda_device(xz, conv_state, ssm_state, x_proj_weight, delta_proj_weight)
+    b = xz.shape[0]
+    io = xz.dtype
+    if xz.stride(-1) != 1:
+        xz = xz.contiguous()
+    Wx = x_proj_weight if x_proj_weight.dtype == io else x_proj_weight.to(io)
+    Wdt = delta_proj_weight if delta_proj_weight.dtype == io else delta_proj_weight.to(io)
+    Wx, Wdt = Wx.contiguous(), Wdt.contiguous()
+    for t, shape in ((conv_state, (b, p.d, p.K - 1)), (ssm_state, (b, p.d, p.n))):
+        if t.dtype != torch.float32 or tuple(t.shape) != shape or not t.is_contiguous():
+            raise ValueError(f"state must be a contiguous fp32 {shape} tensor")
+    y = torch.empty((b, p.d), dtype=io, device=xz.device)
+    args = L.MambaStepArgs(b, p.d, p.n, p.K, p.R, L.dtype_code(io), 1, xz.data_ptr(), xz.stride(0),
+                           L.ptr(conv_state) if p.K > 1 else None, p.conv_w.data_ptr(), L.ptr(p.conv_b),
+                           Wx.data_ptr(), Wdt.data_ptr(), p.dt_bias.data_ptr(), p.A.data_ptr(), p.D.data_ptr(),
+                           ssm_state.data_ptr(), y.data_ptr(), y.stride(0))
+    with torch.cuda.device(xz.device):
+        L.check(L.lib().ss_mamba_step(args, L.stream_of(xz.device)), "ss_mamba_step")
+    return y
+
+
 @torch.no_grad()
 def mamba_simple_step(block, hidden, conv_state, ssm_state, params: _BlockParams | None = None):
-    """One token (batch, d_model) through a block; updates both states in place."""
+    """One token (batch, d_model) through a block; updates both states in place.  Three kernels:
+    the input projection (GEMM), the fused mixer step, the output projection (GEMM)."""
     p = params or _BlockParams(block)
     xz = block.input_proj(hidden)                                    # (b, 2 d)
-    x, z = xz[:, :p.d], xz[:, p.d:]
-    u = conv_step(conv_state, x, p.conv_w, p.conv_b)                 # (b, d)
-    dbl = torch.nn.functional.linear(u, block.ssm_param_proj.weight)  # (b, R + 2N)
-    # B, C read in place from dbl; the delta projection runs inside the step kernel
-    y = selective_state_update(ssm_state, u, dbl[:, :p.R], p.A, dbl[:, p.R:p.R + p.n], dbl[:, p.R + p.n:], p.D,
-                               z=z, dt_bias=p.dt_bias, dt_softplus=True, dt_proj_weight=block.delta_proj.weight)
+    y = mamba_mixer_step(xz, conv_state, ssm_state, p, block.ssm_param_proj.weight, block.delta_proj.weight)
     return block.output_proj(y)
 
 

@@ -33,7 +33,7 @@ def test_library_exports_every_declared_symbol():
 
 def test_abi_version_and_struct_layout():
     lib = L.lib()
-    assert lib.ss_abi_version() == 5
+    assert lib.ss_abi_version() == 6
     for i, st in enumerate(L.STRUCTS):
         assert lib.ss_struct_size(i) == ctypes.sizeof(st)
     assert lib.ss_struct_size(len(L.STRUCTS)) == 0

@@ -117,3 +117,37 @@ def test_sampled_generate_is_reproducible():
     a = generate(model, prompt, 8, temperature=0.8, top_k=20, generator=torch.Generator("cuda").manual_seed(1))
     b = generate(model, prompt, 8, temperature=0.8, top_k=20, generator=torch.Generator("cuda").manual_seed(1))
     assert torch.equal(a, b) and a.shape == (2, 13)
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("batch,dm,N", [(3, 64, 16), (64, 32, 16), (1, 48, 8), (5, 40, 4)])
+def test_fused_mixer_step_matches_separate_kernels(dtype, batch, dm, N):
+    """ss_mamba_step against the composition it replaces: the conv-step kernel, the x projection
+    as a GEMM, and the SSM-step kernel (with its fused delta projection) — several tokens in a
+    row, both states compared after each."""
+    import torch.nn.functional as F
+
+    from mamba_b200.decode import _BlockParams, mamba_mixer_step
+    from mamba_b200.inner import conv_step
+    from mamba_b200.selective_scan_interface import selective_state_update
+
+    torch.manual_seed(batch + dm)
+    blk = MambaSimpleRef(dm, state_dim=N, conv_bias=True).to(dtype).cuda()
+    with torch.no_grad():
+        blk.log_A.add_(0.1 * torch.randn_like(blk.log_A))
+    p = _BlockParams(blk)
+    cs1 = torch.randn(batch, p.d, p.K - 1, device="cuda").to(dtype).float()
+    ss1 = torch.randn(batch, p.d, p.n, device="cuda")
+    cs2, ss2 = cs1.clone(), ss1.clone()
+    rtol, atol = TOL[dtype]
+    for t in range(4):
+        xz = torch.randn(batch, 2 * p.d, device="cuda").to(dtype)
+        y1 = mamba_mixer_step(xz, cs1, ss1, p, blk.ssm_param_proj.weight, blk.delta_proj.weight)
+        u = conv_step(cs2, xz[:, :p.d], p.conv_w, p.conv_b)
+        dbl = F.linear(u, blk.ssm_param_proj.weight)
+        y2 = selective_state_update(ss2, u, dbl[:, :p.R], p.A, dbl[:, p.R:p.R + p.n], dbl[:, p.R + p.n:], p.D,
+                                    z=xz[:, p.d:], dt_bias=p.dt_bias, dt_softplus=True,
+                                    dt_proj_weight=blk.delta_proj.weight)
+        assert torch.equal(cs1, cs2), t
+        assert_close(f"ssm state {t}", ss1, ss2, rtol, atol)
+        assert_close(f"y {t}", y1, y2, rtol, max(atol, rtol * float(y2.abs().max())))
