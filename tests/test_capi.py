@@ -185,3 +185,24 @@ def test_rmsnorm_validation():
     assert lib.ss_rmsnorm_bwd(ctypes.byref(b), None) == L.SS_ERR_INVALID      # no weight / dweight
     assert lib.ss_rmsnorm_fwd(None, None) == L.SS_ERR_INVALID
     assert lib.ss_rmsnorm_bwd(None, None) == L.SS_ERR_INVALID
+
+
+def test_mamba_step_validation():
+    lib = L.lib()
+    a = L.MambaStepArgs()
+    a.batch, a.dim, a.dstate, a.width, a.dt_rank, a.io_dtype, a.dt_softplus = 2, 64, 16, 4, 4, L.SS_BF16, 1
+    assert lib.ss_mamba_step(ctypes.byref(a), None) == L.SS_ERR_INVALID      # no pointers
+    for f in ("xz", "conv_state", "conv_weight", "x_proj", "dt_proj", "A", "ssm_state", "y"):
+        setattr(a, f, 0x1000)
+    a.xz_batch_stride, a.y_batch_stride = 100, 64
+    assert lib.ss_mamba_step(ctypes.byref(a), None) == L.SS_ERR_INVALID      # xz rows shorter than 2 dim
+    a.xz_batch_stride = 128
+    a.dstate = 17
+    assert lib.ss_mamba_step(ctypes.byref(a), None) == L.SS_ERR_UNSUPPORTED
+    a.dstate, a.width = 16, 5
+    assert lib.ss_mamba_step(ctypes.byref(a), None) == L.SS_ERR_UNSUPPORTED
+    a.width, a.dt_rank = 4, 0
+    assert lib.ss_mamba_step(ctypes.byref(a), None) == L.SS_ERR_INVALID
+    a.dt_rank, a.batch = 4, 0
+    assert lib.ss_mamba_step(ctypes.byref(a), None) == L.SS_OK               # empty batch: nothing to do
+    assert lib.ss_mamba_step(None, None) == L.SS_ERR_INVALID
