@@ -7,7 +7,7 @@ position, the token the full forward ranks first.
 The full forward used as the reference here is the fused block path (mamba_simple_forward,
 itself checked against the float64 restatement in test_inner_gpu).  Tolerances: fp32
 rtol 1e-4 with atol scaled to the largest magnitude (the step and the scan sum the states in
-different orders); bf16 rtol 2e-2 / atol 5e-2.
+different orders); bf16 and fp16 rtol 2e-2 / atol 5e-2.
 """
 import pytest
 import torch
@@ -26,7 +26,7 @@ def _block(dtype, dm=64, N=16, seed=0):
     return blk.to(dtype).cuda().eval()
 
 
-@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16, torch.float16])
 def test_block_prefill_then_steps_match_full_forward(dtype):
     from mamba_b200 import mamba_simple_forward
     from mamba_b200.decode import mamba_simple_prefill, mamba_simple_step
@@ -91,7 +91,7 @@ def test_cuda_graph_step_equals_eager_step():
         assert torch.equal(a.step(tok), g.step(tok)), t
 
 
-@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16, torch.float16])
 def test_greedy_generate_agrees_with_full_forward(dtype):
     from mamba_b200.decode import generate
 
@@ -119,7 +119,7 @@ def test_sampled_generate_is_reproducible():
     assert torch.equal(a, b) and a.shape == (2, 13)
 
 
-@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16, torch.float16])
 @pytest.mark.parametrize("batch,dm,N", [(3, 64, 16), (64, 32, 16), (1, 48, 8), (5, 40, 4)])
 def test_fused_mixer_step_matches_separate_kernels(dtype, batch, dm, N):
     """ss_mamba_step against the composition it replaces: the conv-step kernel, the x projection

@@ -4,7 +4,7 @@ and of the fused block mamba_inner_fn, against plain-torch float64 references
 the reference's MambaSimple).
 
 Tolerances: fp32 I/O rtol 1e-4 / atol 1e-5 for the convolution, and for the whole block (GEMMs
-included) rtol 1e-4 with atol scaled to the tensor's largest magnitude; bf16 I/O rtol 2e-2 /
+included) rtol 1e-4 with atol scaled to the tensor's largest magnitude; bf16 and fp16 I/O rtol 2e-2 /
 atol 5e-2 (whole-block gradients: atol = rtol x max|ref|), as for the scan.
 """
 import pytest
@@ -26,7 +26,7 @@ def _conv_inputs(b, L, d, K, dtype, seed, bias=True, with_z=True, state=False):
     return xz, w, bs, st
 
 
-@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16, torch.float16])
 @pytest.mark.parametrize("b,L,d,K,bias,state", [
     (2, 128, 64, 4, True, False),     # whole tiles
     (2, 100, 96, 4, False, True),     # ragged tile in L and in channels, an initial state
@@ -52,7 +52,7 @@ def test_conv_forward_matches_torch(dtype, b, L, d, K, bias, state):
     assert torch.equal(st_out, full[..., full.shape[-1] - (K - 1):])
 
 
-@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16, torch.float16])
 @pytest.mark.parametrize("b,L,d,K,bias,state", [
     (2, 128, 64, 4, True, False),
     (2, 100, 96, 4, True, True),
@@ -104,7 +104,7 @@ def _block(dtype, seed=0, conv_bias=True, bias=True, dm=64, N=16):
     return blk.to(dtype).cuda()
 
 
-@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16, torch.float16])
 @pytest.mark.parametrize("L,conv_bias,bias", [(100, True, True), (64, False, False)])
 def test_mamba_inner_fn_matches_block_reference(dtype, L, conv_bias, bias):
     from mamba_b200.inner import mamba_simple_forward

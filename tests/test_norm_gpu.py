@@ -2,7 +2,7 @@
 mamba_b200.norm) against the reference's RMSNorm restated in torch (tests/torch_ref.RMSNormRef,
 modules/rms_norm.py:21-30) with the residual add of its Block done first in the I/O dtype, and
 of causal_lm_forward against the restated CausalLM.  Gradients are checked against float64
-autograd.  Tolerances: fp32 rtol 1e-4 / atol 1e-5; bf16 rtol 2e-2 / atol 5e-2 (sums over rows
+autograd.  Tolerances: fp32 rtol 1e-4 / atol 1e-5; bf16 and fp16 rtol 2e-2 / atol 5e-2 (sums over rows
 such as dweight: atol scaled to the largest magnitude)."""
 import pytest
 import torch
@@ -19,7 +19,7 @@ def _ref(x, w, res, eps):
     return (hd * torch.rsqrt(hd.pow(2).mean(-1, keepdim=True) + eps) * (1 + w.double())), h
 
 
-@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16, torch.float16])
 @pytest.mark.parametrize("shape,with_res", [((4, 33, 768), True), ((7, 768), False), ((5, 100), True),
                                            ((3, 2048), True), ((2, 9, 32), False), ((0, 64), True)])
 def test_rms_norm_forward_backward(dtype, shape, with_res):
@@ -76,7 +76,7 @@ def test_rms_norm_rejects_long_rows():
         rms_norm_fn(torch.randn(2, 4096, device="cuda", dtype=torch.bfloat16), torch.zeros(4096, device="cuda"))
 
 
-@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16, torch.float16])
 def test_causal_lm_forward_matches_reference_structure(dtype):
     from mamba_b200 import causal_lm_forward, mamba_simple_forward
 
