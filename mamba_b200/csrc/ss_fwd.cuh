@@ -39,7 +39,7 @@ struct FwdSmem {
   alignas(16) float B_s[kVarB ? kTile : 1][NS];
   float bc_pad[16];  // puts C_s rows on the other half of the banks from B_s rows
   alignas(16) float C_s[kVarC ? kTile : 1][NS];
-  float y_s[kNW][kTile][kPad];
+  float y_s[2][kNW][kTile][kPad];  // per-warp partial outputs, double-buffered across tiles
   alignas(8) uint64_t full[kStages];
 };
 
@@ -209,15 +209,20 @@ __global__ void __launch_bounds__(32 * kNW, 4) ss_fwd_kernel(const __grid_consta
         sm.dtu_s[pc][ch] = make_float4(dtuv[4 * q], dtuv[4 * q + 1], dtuv[4 * q + 2], dtuv[4 * q + 3]);
       }
     }
-    if (__syncthreads_or(failed)) {
+    if (__syncthreads_or(failed)) {  // (every thread has also finished the previous tile's epilogue)
       // a TMA stage never completed: report, let the copies in flight land, and leave
       if (tid == 0) {
         if (P.status != nullptr) atomicOr(P.status, kStatusTimeout);
-        for (int j = k + 1; j < ntiles && j < k + kStages; ++j)
+        const int issued_end = max(kStages, k + kStages - 1);  // tiles issued before this point
+        for (int j = k + 1; j < ntiles && j < issued_end; ++j)
           mbar_wait_bounded(&sm.full[j % kStages], (j / kStages) & 1);
       }
       __syncthreads();
       return;
+    }
+    // ---- refill the slot the previous tile used (every thread is past its epilogue)
+    if constexpr (kTMA) {
+      if (tid == 0 && k >= 1 && k - 1 + kStages < ntiles) issue(k - 1 + kStages, (k - 1) % kStages);
     }
 
     // ---- 2. the recurrence, 4 states per lane, 16 steps.  All 64 decays of the tile are
@@ -263,7 +268,7 @@ __global__ void __launch_bounds__(32 * kNW, 4) ss_fwd_kernel(const __grid_consta
 #pragma unroll
         for (int p = 0; p < 2; ++p) h[p] = fma2(da[t][p], h[p], mul2(f2(dus[st]), Bv[p]));
         const float2 y2 = fma2(Cv[1], h[1], mul2(Cv[0], h[0]));
-        sm.y_s[w][t][lane] = y2.x + y2.y;
+        sm.y_s[k & 1][w][t][lane] = y2.x + y2.y;
       }
     }
     if (a.ckpt != nullptr && lane_ok) {
@@ -287,7 +292,7 @@ __global__ void __launch_bounds__(32 * kNW, 4) ss_fwd_kernel(const __grid_consta
         const int t = pq * S + i;
         float y = Dv * uo[i];
 #pragma unroll
-        for (int g = 0; g < kNW; ++g) y += sm.y_s[g][t][pc];
+        for (int g = 0; g < kNW; ++g) y += sm.y_s[k & 1][g][t][pc];
         yu[i] = y;
         if constexpr (kHasZ) {
           y *= zo[i] * sigmoid_fast(zo[i]);
@@ -298,11 +303,11 @@ __global__ void __launch_bounds__(32 * kNW, 4) ss_fwd_kernel(const __grid_consta
       store_run<IT, S>(orow + t0 + pq * S, yv, nv, P.vec_out);
       if (kHasZ && yrow != nullptr) store_run<IT, S>(yrow + t0 + pq * S, yu, nv, P.vec_y);
     }
-    __syncthreads();
-    // ---- 4. refill the freed slot
-    if constexpr (kTMA) {
-      if (tid == 0 && k + kStages < ntiles) issue(k + kStages, stg);
-    }
+    // With TMA there is no barrier here: the next tile's recurrence writes the other y_s buffer,
+    // and the slot this epilogue read is refilled only after the next tile's first barrier,
+    // which every thread reaches after finishing this epilogue.  The synchronous path reloads
+    // its single slot at the top of the next tile, so it waits here.
+    if constexpr (!kTMA) __syncthreads();
   }
 
   if (a.last_state != nullptr && lane_ok) {
