@@ -55,6 +55,8 @@ def args_():
     ap.add_argument("--decode-tokens", type=int, default=256, help="decode workload: new tokens per sequence")
     ap.add_argument("--decode-no-cache-tokens", type=int, default=8,
                     help="decode workload: tokens timed for the no-cache alternative (0 skips it)")
+    ap.add_argument("--model-path", default="both", choices=["both", "fused", "reference"],
+                    help="model workload: time both paths, or only one (for a launch list of one path)")
     ap.add_argument("--block-path", default="both", choices=["both", "fused", "unfused"],
                     help="block workload: time both paths, or only one (for a launch list of one path)")
     return ap.parse_args()
@@ -520,8 +522,12 @@ def model_bench(a):
             torch.cuda.synchronize()
         return e0.elapsed_time(e1) / a.steps, clk.summary()
 
-    ms_ref, _ = timed(ref_forward)
-    ms_f, clocks = timed(lambda x: causal_lm_forward(model, x))
+    ms_ref = ms_f = float("nan")
+    clocks = None
+    if a.model_path in ("both", "reference"):
+        ms_ref, clocks = timed(ref_forward)
+    if a.model_path in ("both", "fused"):
+        ms_f, clocks = timed(lambda x: causal_lm_forward(model, x))
     tokens = b * L
     line = {"workload": "model", "metric": "24-layer CausalLM training step tokens/s (fwd + bwd, batch 8 x 2048)",
             "value": tokens / (ms_f / 1e3), "unit": "tokens/s", "ms_per_step": ms_f,
