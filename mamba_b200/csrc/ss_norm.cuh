@@ -136,9 +136,12 @@ __global__ void __launch_bounds__(32 * kNormWarps) rmsnorm_bwd_kernel(const __gr
     for (int k = 0; k < VW; ++k) dw[j][k] = 0.f;
   const float inv_dim = 1.f / (float)dim;
   for (int row = blockIdx.x * kNormWarps + wid; row < a.rows; row += gridDim.x * kNormWarps) {
-    float h[NV][VW], g[NV][VW];
+    float h[NV][VW], g[NV][VW], gin[NV][VW];
+    // all of the row's loads are issued before any is consumed: one memory round trip per row
     row_load<IT, NV>(h, (const IT*)a.h + (int64_t)row * a.h_row_stride, dim, lane, P.vec);
     row_load<IT, NV>(g, (const IT*)a.dy + (int64_t)row * a.dy_row_stride, dim, lane, P.vec);
+    if (a.dh_in != nullptr)
+      row_load<IT, NV>(gin, (const IT*)a.dh_in + (int64_t)row * a.dh_in_row_stride, dim, lane, P.vec);
     const float rstd = a.rstd[row];
     float dot = 0.f;
 #pragma unroll
@@ -157,11 +160,10 @@ __global__ void __launch_bounds__(32 * kNormWarps) rmsnorm_bwd_kernel(const __gr
 #pragma unroll
       for (int k = 0; k < VW; ++k) g[j][k] = rstd * (g[j][k] - h[j][k] * c);
     if (a.dh_in != nullptr) {
-      row_load<IT, NV>(h, (const IT*)a.dh_in + (int64_t)row * a.dh_in_row_stride, dim, lane, P.vec);
 #pragma unroll
       for (int j = 0; j < NV; ++j)
 #pragma unroll
-        for (int k = 0; k < VW; ++k) g[j][k] += h[j][k];
+        for (int k = 0; k < VW; ++k) g[j][k] += gin[j][k];
     }
     row_store<IT, NV>((IT*)a.dh + (int64_t)row * a.dh_row_stride, g, dim, lane, P.vec);
   }
