@@ -73,6 +73,23 @@ def algorithmic_bytes(b, d, L, n, es=2):
     return fwd, bwd
 
 
+def compute_floor(b, d, L, n, ms_step, sm_mhz):
+    """The step's MUFU (ex2 / lg2 / rcp) work, counted from the kernels' arithmetic, against the
+    B200's 148 SMs x 16 MUFU lanes per clock at the sampled SM clock: the compute floor that
+    keeps this path far from its HBM roofline.  Per element: forward 1 ex2 per state + 4
+    (softplus: ex2, lg2; SiLU gate: ex2, rcp); backward 2 ex2 per state (the tile's forward
+    recompute and the reverse step) + 5 (softplus and its slope: ex2, lg2, rcp; gate: ex2, rcp)."""
+    elems = b * d * L
+    mufu = elems * ((n + 4) + (2 * n + 5))
+    mhz = sm_mhz or 1965.0
+    peak = 148 * 16 * mhz * 1e6
+    floor_ms = mufu / peak * 1e3
+    return {"mufu_ops_per_step": mufu, "mufu_peak_ops_per_s": peak, "mufu_floor_ms": floor_ms,
+            "mufu_frac": floor_ms / ms_step,
+            "note": "MUFU floor of the step at the sampled SM clock; the scan kernels issue at ~45 % of "
+                    "peak with latency stalls on shared-memory and MUFU results (ncu summaries)"}
+
+
 def load_peaks():
     p = os.path.join(HERE, "MEASURED_PEAKS.json")
     try:
@@ -805,6 +822,7 @@ def main():
         "gpu_launches": 2 * K,
         "clocks": clk.summary(),
     }
+    line["compute"] = compute_floor(b, d, L, n, ms_step, line["clocks"].get("sm_mhz"))
     if world == 1 and not a.no_cpu_baseline:
         try:
             v, thr, sample, _ = cpu_sample_rate(b * d * L, b * L, a.cpu_seconds)
