@@ -10,7 +10,9 @@ north-star point of BASELINE.json: per GPU batch 8, d_inner 1536, seqlen 2048, d
 bf16 u / delta / z / B / C, fp32 A / D / delta_bias, softplus on, SiLU(z) gate.  Inputs per
 step (u, delta, z, dout: 4 x 50 MB) exceed the 126 MB L2, so no flush is needed between
 steps.  N GPUs run N batch shards of a global batch 8N (weak scaling; the scan has no
-exchange, so no collective runs inside the timed region).
+exchange, so no collective runs inside the timed region).  ``--workload scan-c4`` runs the
+same step at BASELINE config 4 (d_inner 5120, a global batch of 64 split over the N GPUs:
+strong scaling).
 
 Rank 0 prints one JSON line.  ``value`` is tokens/s of the whole job (inputs resident in
 HBM); ``e2e`` is the same metric with pinned-host inputs copied in and all results copied
@@ -34,7 +36,30 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, HERE)
 
 METRIC = "selective-scan fwd+bwd tokens/s and HBM GB/s (% of ~8 TB/s peak) at 1/2/4/8 B200"
-PER_GPU = dict(b=8, d=1536, L=2048, n=16)
+# scan workloads: "scan" is the north-star point (per-GPU batch fixed, weak scaling); "scan-c4"
+# is BASELINE config 4, a Mamba-2.8B-shaped layer whose global batch of 64 is split over the GPUs
+# (strong scaling)
+SCAN_WORKLOADS = {
+    "scan": dict(b=8, d=1536, L=2048, n=16, scaling="weak",
+                 label="selective_scan fwd+bwd, batch 8 per GPU, d_inner 1536, seqlen 2048, d_state 16, "
+                       "bf16 I/O + fp32 state, z gate, softplus (north-star point)"),
+    "scan-c4": dict(b=64, d=5120, L=2048, n=16, scaling="strong",
+                    label="selective_scan fwd+bwd, global batch 64 split over the GPUs, d_inner 5120, seqlen 2048, "
+                          "d_state 16, bf16 I/O + fp32 state, z gate, softplus (config 4, Mamba-2.8B-shaped layer)"),
+}
+PER_GPU = {k: SCAN_WORKLOADS["scan"][k] for k in ("b", "d", "L", "n")}
+
+
+def scan_shape(workload, world):
+    """Per-GPU batch b, the job's global batch, d, L, n and the scaling kind of a scan workload."""
+    s = dict(SCAN_WORKLOADS[workload])
+    if s["scaling"] == "weak":
+        s["global_b"] = s["b"] * world
+    else:
+        if s["b"] % world:
+            raise SystemExit(f"{workload}: the global batch {s['b']} does not split over {world} GPUs")
+        s["global_b"], s["b"] = s["b"], s["b"] // world
+    return s
 
 
 def args_():
@@ -46,8 +71,9 @@ def args_():
     ap.add_argument("--e2e-steps", type=int, default=20)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="CPU-baseline sample budget")
-    ap.add_argument("--workload", default="scan", choices=["scan", "block", "decode", "norm", "model"],
-                    help="scan: the north-star selective scan (default); block: one MambaSimple block "
+    ap.add_argument("--workload", default="scan", choices=["scan", "scan-c4", "block", "decode", "norm", "model"],
+                    help="scan: the north-star selective scan (default); scan-c4: the scan at config 4 "
+                         "(global batch 64 over the GPUs, d_inner 5120); block: one MambaSimple block "
                          "(d_model 768) fwd+bwd, fused mamba_inner_fn against the reference's op sequence; "
                          "decode: a 24-layer CausalLM (d_model 768) decoding 256 tokens after a 128-token prompt "
                          "at batch 64; norm: residual add + RMSNorm fwd+bwd over 16384 x 768 bf16 rows; "
@@ -191,28 +217,33 @@ class ClockSampler:
 
 
 # ----------------------------------------------------------------------------- inputs
-def make_inputs(b, d, L, n, seed, device):
+def make_inputs(b, d, L, n, seed, device="cpu"):
+    """Seeded inputs with the configs' distributions, generated on `device` (the CPU for the
+    north-star point; the GPU for config 4, whose 671M-element tensors take minutes to draw on
+    one host thread)."""
     import torch
 
-    g = torch.Generator().manual_seed(seed)
-    rn = lambda *s: torch.randn(*s, generator=g, dtype=torch.float32)
-    dt = torch.exp(torch.rand(d, generator=g) * (math.log(0.1) - math.log(1e-3)) + math.log(1e-3)).clamp(min=1e-4)
-    host = dict(
-        u=rn(b, d, L).bfloat16(), delta=(0.5 * rn(b, d, L)).bfloat16(), z=rn(b, d, L).bfloat16(),
-        B=rn(b, 1, n, L).bfloat16(), C=rn(b, 1, n, L).bfloat16(), dout=rn(b, d, L).bfloat16(),
-        A=-torch.arange(1, n + 1, dtype=torch.float32).repeat(d, 1), D=torch.ones(d),
-        delta_bias=dt + torch.log(-torch.expm1(-dt)))
-    return host
+    g = torch.Generator(device=device).manual_seed(seed)
+    rn = lambda *s: torch.randn(*s, generator=g, dtype=torch.float32, device=device)
+    dt = torch.exp(torch.rand(d, generator=g, device=device) * (math.log(0.1) - math.log(1e-3))
+                   + math.log(1e-3)).clamp(min=1e-4)
+    bf = lambda t: t.bfloat16()
+    x = dict(u=bf(rn(b, d, L)), delta=bf(0.5 * rn(b, d, L)), z=bf(rn(b, d, L)),
+             B=bf(rn(b, 1, n, L)), C=bf(rn(b, 1, n, L)), dout=bf(rn(b, d, L)),
+             A=-torch.arange(1, n + 1, dtype=torch.float32, device=device).repeat(d, 1),
+             D=torch.ones(d, device=device), delta_bias=dt + torch.log(-torch.expm1(-dt)))
+    return x
 
 
 # ----------------------------------------------------------------------------- cpu legs
-def cpu_sample_rate(n_full_elems, tokens_full, budget_s, seed=0):
+def cpu_sample_rate(n_full_elems, tokens_full, budget_s, seed=0, shape=None):
     """Time the fp32 CPU oracle port (fwd + bwd, all host threads) on a slice of the
     workload sized to ~budget_s, and extrapolate to tokens/s of the full workload."""
     import torch
     from oracle import oracle as O
 
-    d_full, L, n = PER_GPU["d"], PER_GPU["L"], PER_GPU["n"]
+    shape = shape or PER_GPU
+    d_full, L, n = shape["d"], shape["L"], shape["n"]
 
     def run(rows):
         bsl, dsl = (1, rows) if rows <= d_full else (rows // d_full, d_full)
@@ -229,7 +260,7 @@ def cpu_sample_rate(n_full_elems, tokens_full, budget_s, seed=0):
     # then whole batch rows) towards ~budget_s, never past the per-GPU workload
     cal = max(8, 8 * threads)
     t_cal = run(cal)
-    rows = int(min(n_full_elems // L, PER_GPU["b"] * d_full, max(cal, cal * budget_s / max(t_cal, 1e-3))))
+    rows = int(min(n_full_elems // L, shape["b"] * d_full, max(cal, cal * budget_s / max(t_cal, 1e-3))))
     rows = max(8, rows - rows % 8) if rows <= d_full else rows - rows % d_full
     t, reps = run(rows), 1
     while t < budget_s and reps < 64:  # the whole slice was fast: repeat it to fill the budget
@@ -245,21 +276,22 @@ def cpu_sample_rate(n_full_elems, tokens_full, budget_s, seed=0):
 def reference_arm(a, world, rank):
     if rank != 0:
         return 0
-    b, d, L, n = PER_GPU["b"] * world, PER_GPU["d"], PER_GPU["L"], PER_GPU["n"]
+    shape = scan_shape(a.workload if a.workload in SCAN_WORKLOADS else "scan", world)
+    b, d, L, n = shape["global_b"], shape["d"], shape["L"], shape["n"]
     elems, tokens = b * d * L, b * L
     per_step_budget = max(1.0, 120.0 / max(1, a.steps + a.warmup))
     vals = []
     sample = threads = None
     for i in range(a.warmup + a.steps):
-        v, threads, sample, _ = cpu_sample_rate(elems, tokens, per_step_budget, seed=i)
+        v, threads, sample, _ = cpu_sample_rate(elems, tokens, per_step_budget, seed=i, shape=shape)
         if i >= a.warmup:
             vals.append(v)
     value = statistics.median(vals)
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
         "steps": a.steps, "warmup": a.warmup, "ms_per_step": 1e3 * tokens / value, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": config_dict(world),
+        "scaling": shape["scaling"], "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": config_dict(world, shape),
         "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "port",
                          "sample": f"per step: {sample}; extrapolated to the workload's elements"},
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -270,13 +302,13 @@ def reference_arm(a, world, rank):
     return 0
 
 
-def config_dict(world):
-    b = PER_GPU["b"]
-    return {"workload": "selective_scan fwd+bwd, batch 8 per GPU, d_inner 1536, seqlen 2048, d_state 16, "
-                        "bf16 I/O + fp32 state, z gate, softplus (north-star point)",
-            "global_batch": b * world, "per_gpu_batch": b, "d_inner": PER_GPU["d"], "seq_len": PER_GPU["L"],
-            "d_state": PER_GPU["n"], "parallelism": f"batch-sharded x{world}, no collective in the path",
-            "l2": "inputs larger than L2 (200 MB per step of u/delta/z/dout)"}
+def config_dict(world, shape):
+    b, d, L = shape["b"], shape["d"], shape["L"]
+    step_mb = 4 * b * d * L * 2 / 1e6
+    return {"workload": shape["label"],
+            "global_batch": shape["global_b"], "per_gpu_batch": b, "d_inner": d, "seq_len": L,
+            "d_state": shape["n"], "parallelism": f"batch-sharded x{world}, no collective in the path",
+            "l2": f"inputs larger than L2 ({step_mb:.0f} MB per GPU per step of u/delta/z/dout)"}
 
 
 # ----------------------------------------------------------------------------- gpu arm
@@ -677,9 +709,14 @@ def main():
         from datetime import timedelta
         dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=180))
 
-    b, d, L, n = PER_GPU["b"], PER_GPU["d"], PER_GPU["L"], PER_GPU["n"]
-    host = make_inputs(b, d, L, n, seed=1000 + rank, device="cpu")
-    x = {k: v.to(dev) for k, v in host.items()}
+    shape = scan_shape(a.workload, world)
+    b, d, L, n = shape["b"], shape["d"], shape["L"], shape["n"]
+    if a.workload == "scan":
+        host = make_inputs(b, d, L, n, seed=1000 + rank, device="cpu")
+        x = {k: v.to(dev) for k, v in host.items()}
+    else:
+        x = make_inputs(b, d, L, n, seed=1000 + rank, device=dev)
+        host = {k: v.cpu() for k, v in x.items()}
     leaves = ["u", "delta", "A", "B", "C", "D", "z", "delta_bias"]
     for k in leaves:
         x[k].requires_grad_(True)
@@ -809,13 +846,14 @@ def main():
     step_gbs = (fwd_bytes + bwd_bytes) / (ms_step / 1e3) / 1e9
     line = {
         "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": K, "warmup": a.warmup,
-        "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-        "dtype": "bf16", "data": "synthetic", "config": config_dict(world),
+        "ms_per_step": ms_step, "higher_is_better": True, "scaling": shape["scaling"], "vs_baseline": None,
+        "dtype": "bf16", "data": "synthetic", "config": config_dict(world, shape),
         "hbm_gbs_step": step_gbs, "hbm_frac_step": step_gbs / peak, "hbm_frac_step_nominal_8tbs": step_gbs / 8000.0,
         "kernels_ms": {"fwd": fwd_ms, "bwd": bwd_ms},
         "roofline": {"kernel": dom, "bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                      "frac": achieved / peak, "peak_source": peak_kind,
-                     "algorithmic_bytes_per_launch": dom_bytes, "traffic": profile_traffic()},
+                     "algorithmic_bytes_per_launch": dom_bytes,
+                     "traffic": profile_traffic() if a.workload == "scan" else None},
         "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "pipeline": "copy-in, compute and copy-out of consecutive steps on three streams",
                 "ms_per_step": e2e_ms},
@@ -825,7 +863,7 @@ def main():
     line["compute"] = compute_floor(b, d, L, n, ms_step, line["clocks"].get("sm_mhz"))
     if world == 1 and not a.no_cpu_baseline:
         try:
-            v, thr, sample, _ = cpu_sample_rate(b * d * L, b * L, a.cpu_seconds)
+            v, thr, sample, _ = cpu_sample_rate(b * d * L, b * L, a.cpu_seconds, shape=shape)
             line["cpu_baseline"] = {"value": v, "unit": "tokens/s", "cores": thr, "kind": "port", "sample": sample}
         except Exception as e:  # the baseline is reported, never required
             line["cpu_baseline"] = {"value": None, "unit": "tokens/s", "cores": None, "kind": "port",

@@ -170,3 +170,65 @@ def test_config2_long_sequence_last_state():
     assert_close("out", out[:, sl], ref_out, rtol, atol)
     assert_close("last_state", last[:, sl], ref_last, rtol, atol)
     assert torch.isfinite(out).all()
+
+
+@pytest.mark.slow
+def test_config4_full_size_fwd_bwd():
+    """Config 4 (Mamba-2.8B-shaped layer): b64 d5120 L2048 N16, bf16 u / delta / z / B / C,
+    fp32 A / D / delta_bias, fwd + bwd at full size (671M elements per tensor).
+
+    Batch rows are independent, so three whole rows (all 5120 channels, all 2048 steps) are
+    checked against the oracle: out, last state, du, ddelta, dz, and the row's dB / dC (sums
+    over every channel).  The gradients summed over the 64 rows (dA, dD, ddelta_bias) are checked
+    by linearity — the full run equals the sum of four 16-row runs of the same inputs (fp32
+    summation order only) — and the same three rows run alone match the oracle's sums."""
+    import math
+
+    import mamba_b200
+
+    b, d, L, n = 64, 5120, 2048, 16
+    g = torch.Generator(device="cuda").manual_seed(4)
+    rn = lambda *s: torch.randn(*s, generator=g, device="cuda")
+    x = dict(u=rn(b, d, L).bfloat16(), delta=(0.5 * rn(b, d, L)).bfloat16(), z=rn(b, d, L).bfloat16(),
+             B=rn(b, 1, n, L).bfloat16(), C=rn(b, 1, n, L).bfloat16())
+    dout = rn(b, d, L).bfloat16()
+    gc = torch.Generator().manual_seed(4)
+    dt = torch.exp(torch.rand(d, generator=gc) * (math.log(0.1) - math.log(1e-3)) + math.log(1e-3)).clamp(min=1e-4)
+    x.update(A=-torch.arange(1, n + 1, dtype=torch.float32).repeat(d, 1).cuda(), D=torch.ones(d, device="cuda"),
+             delta_bias=(dt + torch.log(-torch.expm1(-dt))).cuda())
+    keys = ("u", "delta", "A", "B", "C", "D", "z", "delta_bias")
+
+    def run(rows):
+        t = {k: (x[k][rows] if k in ("u", "delta", "z", "B", "C") else x[k]).detach().requires_grad_() for k in keys}
+        out, last = mamba_b200.selective_scan_fn(t["u"], t["delta"], t["A"], t["B"], t["C"], t["D"], t["z"],
+                                                 t["delta_bias"], True, return_last_state=True)
+        out.backward(dout[rows])
+        res = {"out": out.detach(), "last_state": last}
+        res.update({"d" + k: t[k].grad for k in keys})
+        return res
+
+    full = run(slice(None))
+    torch.cuda.synchronize()
+    assert all(torch.isfinite(v).all() for v in full.values())
+    for k in ("dA", "dD", "ddelta_bias"):
+        full[k] = full[k].clone()
+
+    # linearity over batch rows of the summed parameter gradients, at full size
+    parts = {k: torch.zeros_like(full[k]) for k in ("dA", "dD", "ddelta_bias")}
+    for r0 in range(0, b, 16):
+        part = run(slice(r0, r0 + 16))
+        for k in parts:
+            parts[k] += part[k]
+        del part
+    for k in parts:
+        assert_close(f"{k} (64 rows vs 4 x 16 rows)", full[k], parts[k], 1e-4, 1e-4 * float(parts[k].abs().max()))
+
+    # three whole rows against the oracle
+    rows = [0, 37, 63]
+    sub = run(rows)
+    cpu = {k: (x[k][rows] if k in ("u", "delta", "z", "B", "C") else x[k]).cpu() for k in keys}
+    cpu.update(softplus=True, dout=dout[rows].cpu())
+    want = oracle_case(cpu)
+    got_rows = {k: full[k][rows] for k in ("out", "last_state", "du", "ddelta", "dz", "dB", "dC")}
+    compare(got_rows, want, torch.bfloat16, keys=("out", "last_state", "du", "ddelta", "dz", "dB", "dC"))
+    compare(sub, want, torch.bfloat16, keys=("dA", "dD", "ddelta_bias"))
