@@ -335,14 +335,19 @@ def _mamba_block(dm, n=16, K=4):
     return blk
 
 
-def _causal_lm(vocab, dm, layers, n=16, K=4):
+# Mamba-130M-shaped CausalLM (24 layers, d_model 768, vocab 50280 with tied
+# embeddings, RMSNorm eps 1e-5)
+LM_VOCAB, LM_EPS = 50280, 1e-5
+
+
+def _causal_lm(vocab, dm, layers, n=16, K=4, eps=LM_EPS):
     """A model with the reference CausalLM's module tree (models/causal_lm.py:20-58): embedding,
     layers of (RMSNorm, MambaSimple block), final RMSNorm, lm_head tied to the embedding."""
     import torch
     import torch.nn as nn
 
     class RMSNorm(nn.Module):  # modules/rms_norm.py:4-30
-        def __init__(self, dim, eps=1e-6):
+        def __init__(self, dim, eps):
             super().__init__()
             self.eps, self.weight = eps, nn.Parameter(torch.zeros(dim))
 
@@ -356,9 +361,9 @@ def _causal_lm(vocab, dm, layers, n=16, K=4):
     m.layers = nn.ModuleList()
     for _ in range(layers):
         layer = nn.Module()
-        layer.norm, layer.mamba = RMSNorm(dm), _mamba_block(dm, n, K)
+        layer.norm, layer.mamba = RMSNorm(dm, eps), _mamba_block(dm, n, K)
         m.layers.append(layer)
-    m.norm = RMSNorm(dm)
+    m.norm = RMSNorm(dm, eps)
     m.lm_head = nn.Linear(dm, vocab, bias=False)
     m.lm_head.weight = m.embedding.weight
     return m
@@ -366,7 +371,7 @@ def _causal_lm(vocab, dm, layers, n=16, K=4):
 
 def decode_bench(a):
     """Decoding with a 24-layer CausalLM-shaped model (d_model 768, d_inner 1536, N 16, vocab
-    32000; the decode of the 24-layer model config): batch 64, a 128-token prompt, then 256 new
+    50280; the decode of the 24-layer model config): batch 64, a 128-token prompt, then 256 new
     tokens (greedy), bf16.  Reports new tokens per second over the decode loop (prompt prefill
     timed separately) for the CUDA-graph step and the eager step, and — as the reference's
     alternative, since its generate() is a stub and MambaSimple has no step — the cost of one
@@ -378,7 +383,7 @@ def decode_bench(a):
 
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
-    vocab, dm, layers, b, L0, T = 32000, 768, 24, 64, 128, a.decode_tokens
+    vocab, dm, layers, b, L0, T = LM_VOCAB, 768, 24, 64, 128, a.decode_tokens
     torch.manual_seed(0)
     model = _causal_lm(vocab, dm, layers).to(dev, torch.bfloat16).eval()
     prompt = torch.randint(0, vocab, (b, L0), generator=torch.Generator().manual_seed(1)).to(dev)
@@ -437,7 +442,7 @@ def decode_bench(a):
                      "peak": load_peaks()[0], "unit": "GB/s",
                      "frac": step_bytes / (step_ms / 1e3) / 1e9 / load_peaks()[0]},
         "n_gpus": 1, "higher_is_better": True, "dtype": "bf16", "data": "synthetic (random weights, random prompt)",
-        "config": {"workload": "24-layer CausalLM, d_model 768, d_inner 1536, d_state 16, vocab 32000, batch 64, "
+        "config": {"workload": "24-layer CausalLM, d_model 768, d_inner 1536, d_state 16, vocab 50280, batch 64, "
                                "prompt 128, 256 new tokens, greedy", "params": n_params},
         "clocks": clocks,
     }
@@ -509,7 +514,7 @@ def norm_bench(a):
 
 def model_bench(a):
     """One training step (forward, cross-entropy over the vocabulary, backward; no optimizer)
-    of the 24-layer CausalLM config (d_model 768, d_inner 1536, N 16, vocab 32000) at batch 8 x
+    of the 24-layer CausalLM config (d_model 768, d_inner 1536, N 16, vocab 50280) at batch 8 x
     seqlen 2048, bf16 parameters, two ways on the same model and tokens:
       fused:     mamba_b200.causal_lm_forward (fused blocks; residual add fused with RMSNorm);
       reference: the reference CausalLM's own forward structure (models/causal_lm.py:30-58: torch
@@ -524,7 +529,7 @@ def model_bench(a):
 
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
-    vocab, dm, layers, b, L = 32000, 768, 24, 8, 2048
+    vocab, dm, layers, b, L = LM_VOCAB, 768, 24, 8, 2048
     d, n, K = 2 * dm, 16, 4
     R = math.ceil(dm / 16)
     torch.manual_seed(0)
@@ -583,7 +588,7 @@ def model_bench(a):
             "reference_structure_value": tokens / (ms_ref / 1e3), "reference_structure_ms_per_step": ms_ref,
             "speedup_vs_reference_structure": ms_ref / ms_f, "n_gpus": 1, "steps": a.steps, "warmup": a.warmup,
             "higher_is_better": True, "dtype": "bf16", "data": "synthetic (random weights and tokens)",
-            "config": {"workload": "CausalLM 24 layers, d_model 768, d_inner 1536, d_state 16, vocab 32000 (tied), "
+            "config": {"workload": "CausalLM 24 layers, d_model 768, d_inner 1536, d_state 16, vocab 50280 (tied), RMSNorm eps 1e-5, "
                                    "batch 8, seqlen 2048, bf16 parameters, cross-entropy loss, no optimizer step",
                        "params": sum(p_.numel() for p_ in model.parameters())},
             "clocks": clocks}

@@ -175,7 +175,9 @@ def _block_forward(xz, conv_weight, conv_bias, x_proj_weight, delta_proj_weight,
     res = torch.bmm(out.transpose(1, 2), Wo.t().expand(b, d, Wo.shape[0]))  # (b, L, dm)
     if out_proj_bias is not None:
         res = res + out_proj_bias.to(io)
-    saved = (u, zt, dblT, out, ckpt, y) if train else None
+    # the scan operands as the native call took them (B / C contiguous, fp32 bias): the backward
+    # reuses them instead of preparing them again
+    saved = (u, zt, dblT, out, ckpt, y, p.A, p.B, p.C, p.D, p.delta_bias) if train else None
     return res, saved, conv_state, last
 
 
@@ -198,7 +200,8 @@ class MambaInnerFn(torch.autograd.Function):
 
     @staticmethod
     def backward(ctx, dres):
-        (xz, conv_w, conv_b, Wx0, Wdt0, dt_b, Wo0, bo, A, D, u, zt, dblT, out, ckpt, y) = ctx.saved_tensors
+        (xz, conv_w, conv_b, Wx0, Wdt0, dt_b, Wo0, bo, A, D, u, zt, dblT, out, ckpt, y,
+         A32, B, C, D32, bias32) = ctx.saved_tensors
         io = xz.dtype
         b, l, d2 = xz.shape
         d = d2 // 2
@@ -208,20 +211,21 @@ class MambaInnerFn(torch.autograd.Function):
         dres = dres.to(io)
         # output projection
         dout = _wmm(Wo.t(), dres.transpose(1, 2))                         # (b, d, L)
-        dWo = torch.bmm(dres.transpose(1, 2), out.transpose(1, 2)).sum(0, dtype=torch.float32)  # (dm, d)
+        # weight gradients: per-row GEMMs summed over the batch (fp32 accumulation) straight into
+        # the parameter's dtype
+        dWo = torch.bmm(dres.transpose(1, 2), out.transpose(1, 2)).sum(0, dtype=Wo0.dtype)  # (dm, d)
         dbo = dres.sum((0, 1), dtype=torch.float32) if bo is not None else None
         # scan
-        B, C = dblT[:, R:R + n].unsqueeze(1), dblT[:, R + n:].unsqueeze(1)
         delta = _wmm(Wdt, dblT[:, :R])
-        p = _Prepared(u, delta, A, B, C, D, zt, dt_b, ctx.softplus)
+        p = _Prepared(u, delta, A32, B, C, D32, zt, bias32, ctx.softplus)
         du, ddelta, dA, dB, dC, dD, dzt, ddt_b = scan_backward(p, dout, ckpt, y)
         # delta and x projections
         d_dblT = torch.empty((b, R + 2 * n, l), dtype=io, device=xz.device)
-        d_dblT[:, :R] = _wmm(Wdt.t(), ddelta)
+        torch.bmm(Wdt.t().unsqueeze(0).expand(b, -1, -1), ddelta, out=d_dblT[:, :R])
         d_dblT[:, R:R + n] = dB[:, 0]
         d_dblT[:, R + n:] = dC[:, 0]
-        dWdt = torch.bmm(ddelta, dblT[:, :R].transpose(1, 2)).sum(0, dtype=torch.float32)  # (d, R)
-        dWx = torch.bmm(d_dblT, u.transpose(1, 2)).sum(0, dtype=torch.float32)            # (R + 2N, d)
+        dWdt = torch.bmm(ddelta, dblT[:, :R].transpose(1, 2)).sum(0, dtype=Wdt0.dtype)  # (d, R)
+        dWx = torch.bmm(d_dblT, u.transpose(1, 2)).sum(0, dtype=Wx0.dtype)            # (R + 2N, d)
         du_total = torch.baddbmm(du, Wx.t().unsqueeze(0).expand(b, -1, -1), d_dblT)  # (b, d, L)
         # convolution (+ the gate half's gradient), written into d(xz)
         dxz = torch.empty_like(xz)
