@@ -53,8 +53,9 @@
 extern "C" {
 #endif
 
-#define SS_ABI_VERSION 6
-#define SS_MAX_DSTATE 16
+#define SS_ABI_VERSION 7
+/* the reference's kernels dispatch dstate up to 256 (csrc/selective_scan/static_switch.h:15-35) */
+#define SS_MAX_DSTATE 256
 #define SS_MAX_CONV_WIDTH 4
 /* capacity (floats) of the library-held state array used by ss_bwd_noalloc: 16 MiB */
 #define SS_NOALLOC_MAX_CKPT_ELEMS 4194304
@@ -70,7 +71,7 @@ typedef enum ss_dtype { SS_F32 = 0, SS_BF16 = 1, SS_F16 = 2 } ss_dtype;
 typedef enum ss_status {
   SS_OK = 0,
   SS_ERR_INVALID = 1,     /* null pointer, bad size, bad stride, dim % ngroups != 0 */
-  SS_ERR_UNSUPPORTED = 2, /* dtype combination or dstate > SS_MAX_DSTATE */
+  SS_ERR_UNSUPPORTED = 2, /* dtype combination, dstate > SS_MAX_DSTATE or a size the grid cannot hold */
   SS_ERR_CUDA = 3         /* a CUDA runtime call or kernel launch failed */
 } ss_status;
 
@@ -94,6 +95,11 @@ typedef struct ss_fwd_args {
   void* out_y;       int64_t out_y_batch_stride, out_y_dim_stride;
                             /* nullable: the ungated y (D*u + C.h), which ss_bwd needs when
                                z is given; written only when z is given                   */
+  float* work;              /* 16-byte aligned fp32 scratch of ss_work_elems(batch, dim,
+                               seqlen, dstate) floats, required when that is > 0 (dstate > 16: the states
+                               are scanned in groups of 16 whose per-element sums meet
+                               here); ss_fwd and ss_bwd overwrite it; contents are not
+                               needed between calls.  Nullable when dstate <= 16.          */
 } ss_fwd_args;
 
 typedef struct ss_bwd_args {
@@ -238,6 +244,10 @@ typedef struct ss_mamba_step_args {
 
 /* Number of fp32 elements of the forward-to-backward state buffer. */
 SS_API size_t ss_ckpt_elems(int batch, int dim, int seqlen, int dstate);
+
+/* Number of fp32 elements of the scratch ss_fwd_args.work must hold: 0 for dstate <= 16,
+ * else 2 * batch * dim * seqlen (ss_fwd uses the first half, ss_bwd all of it). */
+SS_API size_t ss_work_elems(int batch, int dim, int seqlen, int dstate);
 
 /* Forward scan: out = (D*u + sum_n C*h) [* silu(z)], h_t = exp(delta'*A) h_{t-1} + delta'*u*B. */
 SS_API int ss_fwd(const ss_fwd_args* args, void* stream);

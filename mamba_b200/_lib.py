@@ -17,7 +17,7 @@ LIB_PATH = os.path.join(_PKG, "libmamba_b200_ss.so")
 
 SS_F32, SS_BF16, SS_F16 = 0, 1, 2
 SS_OK, SS_ERR_INVALID, SS_ERR_UNSUPPORTED, SS_ERR_CUDA = 0, 1, 2, 3
-SS_MAX_DSTATE = 16
+SS_MAX_DSTATE = 256
 TILE = 16  # time steps between checkpoints (kTile in csrc/ss_common.cuh)
 
 _DTYPES = {torch.float32: SS_F32, torch.bfloat16: SS_BF16, torch.float16: SS_F16}
@@ -38,6 +38,7 @@ class FwdArgs(ctypes.Structure):
         ("out", c_vp), ("out_batch_stride", c_i64), ("out_dim_stride", c_i64),
         ("ckpt", c_vp), ("last_state", c_vp),
         ("out_y", c_vp), ("out_y_batch_stride", c_i64), ("out_y_dim_stride", c_i64),
+        ("work", c_vp),
     ]
 
 
@@ -141,10 +142,10 @@ class MambaStepArgs(ctypes.Structure):
 # ss_struct_size index order
 STRUCTS = (FwdArgs, BwdArgs, StepArgs, ConvArgs, ConvBwdArgs, ConvStepArgs, RmsNormArgs, RmsNormBwdArgs,
            MambaStepArgs)
-ABI_VERSION = 6
+ABI_VERSION = 7
 MAX_CONV_WIDTH = 4
 
-EXPORTS = ("ss_fwd", "ss_bwd", "ss_step", "ss_ckpt_elems", "ss_status_string",
+EXPORTS = ("ss_fwd", "ss_bwd", "ss_step", "ss_ckpt_elems", "ss_work_elems", "ss_status_string",
            "ss_last_cuda_error", "ss_abi_version", "ss_struct_size", "ss_device_status",
            "ss_bwd_noalloc", "ss_conv_fwd", "ss_conv_bwd", "ss_conv_step", "ss_rmsnorm_fwd", "ss_rmsnorm_bwd",
            "ss_mamba_step")
@@ -182,6 +183,8 @@ def lib():
                     getattr(L, f).restype = c_int
                 L.ss_ckpt_elems.argtypes = [c_int, c_int, c_int, c_int]
                 L.ss_ckpt_elems.restype = ctypes.c_size_t
+                L.ss_work_elems.argtypes = [c_int, c_int, c_int, c_int]
+                L.ss_work_elems.restype = ctypes.c_size_t
                 L.ss_status_string.argtypes = [c_int]
                 L.ss_status_string.restype = ctypes.c_char_p
                 L.ss_device_status.argtypes = [c_int, c_vp]
@@ -237,3 +240,8 @@ def device_status(device, reset: bool = True) -> int:
 
 def ckpt_elems(batch, dim, seqlen, dstate) -> int:
     return int(lib().ss_ckpt_elems(batch, dim, seqlen, dstate))
+
+
+def work_elems(batch, dim, seqlen, dstate) -> int:
+    """fp32 scratch a scan call needs (0 for dstate <= 16)."""
+    return int(lib().ss_work_elems(batch, dim, seqlen, dstate))

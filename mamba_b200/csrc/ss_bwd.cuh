@@ -29,6 +29,11 @@
 // Inputs (u, delta, dout, z, y, the B / C tiles and the checkpointed states) stream through
 // a TMA ring of kStagesBwd tiles; kTMA = false loads each tile synchronously.  Shared memory
 // is kept under ~72 KB (bf16) so that three CTAs fit on an SM next to their registers.
+//
+// dstate > 16: one CTA per (32 channels, group of 16 states), as in the forward.  Every state's
+// reverse recurrence, its dA and its dB / dC rows belong to one CTA, but (S1, S2) sum over all
+// states: with kMulti each CTA adds its partial pair per element into an fp32 workspace
+// ([b][c][t][2]) and bwd_finish_kernel then forms du, ddelta, dz, dD and ddelta_bias.
 #pragma once
 #include "ss_common.cuh"
 #include "ss_fwd.cuh"  // widen_bc
@@ -74,7 +79,7 @@ struct BwdSmem {
   alignas(8) uint64_t full[kStagesBwd<IT>];
 };
 
-template <typename IT, int kNW, bool kVarB, bool kVarC, bool kHasZ, bool kTMA>
+template <typename IT, int kNW, bool kVarB, bool kVarC, bool kHasZ, bool kTMA, bool kMulti = false>
 __global__ void __launch_bounds__(32 * kNW, 3) ss_bwd_kernel(const __grid_constant__ BwdK P) {
   constexpr int NT = 32 * kNW;
   constexpr int NS = kSPW * kNW;
@@ -87,11 +92,15 @@ __global__ void __launch_bounds__(32 * kNW, 3) ss_bwd_kernel(const __grid_consta
   const ss_fwd_args& f = a.f;
 
   const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
-  const int grp = blockIdx.x / P.tpg;
-  const int cl0 = (blockIdx.x % P.tpg) * kCh;
+  const int ctile = blockIdx.x % P.nct;
+  const int bsg = blockIdx.x / P.nct;
+  const int sg = bsg % P.nsg;            // state group: states n0 .. n0 + 15
+  const int b = bsg / P.nsg;
+  const int grp = ctile / P.tpg;
+  const int cl0 = (ctile % P.tpg) * kCh;
   const int c0 = grp * P.dpg + cl0;
   const int nvalid = min(kCh, P.dpg - cl0);
-  const int b = blockIdx.y;
+  const int n0 = sg * NS;
   const int N = f.dstate, L = f.seqlen;
   const bool bc_f32 = f.bc_dtype == SS_F32;
 
@@ -104,7 +113,7 @@ __global__ void __launch_bounds__(32 * kNW, 3) ss_bwd_kernel(const __grid_consta
     float av[2], bv[2], cv[2];
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
-      const int n = kSPW * w + 2 * p + h;
+      const int n = n0 + kSPW * w + 2 * p + h;
       const bool ok = lane_ok && n < N;
       const int64_t ia = (int64_t)c * N + n;
       av[h] = ok ? f.A[ia] : 0.f;
@@ -135,7 +144,7 @@ __global__ void __launch_bounds__(32 * kNW, 3) ss_bwd_kernel(const __grid_consta
   IT* du_row = (IT*)a.du + (int64_t)b * a.du_batch_stride + (int64_t)(c0 + pc) * a.du_dim_stride;
   IT* dd_row = (IT*)a.ddelta + (int64_t)b * a.ddelta_batch_stride + (int64_t)(c0 + pc) * a.ddelta_dim_stride;
   IT* dz_row = kHasZ ? (IT*)a.dz + (int64_t)b * a.dz_batch_stride + (int64_t)(c0 + pc) * a.dz_dim_stride : nullptr;
-  const int64_t bc_off = ((int64_t)b * f.ngroups + grp) * N * (int64_t)L;
+  const int64_t bc_off = (((int64_t)b * f.ngroups + grp) * N + n0) * (int64_t)L;  // row n0 of this group
 
   const int ntiles = P.ntiles;
   const uint32_t io_bytes = kCh * kTile * (uint32_t)sizeof(IT);
@@ -145,8 +154,8 @@ __global__ void __launch_bounds__(32 * kNW, 3) ss_bwd_kernel(const __grid_consta
   auto issue = [&](int i, int s) {
     const int k = ntiles - 1 - i;
     uint64_t* bar = &sm.full[s];
-    const uint32_t bytes = (3 + (kHasZ ? 2 : 0)) * io_bytes + ((kVarB ? 1 : 0) + (kVarC ? 1 : 0)) * bc_bytes +
-                           (k > 0 ? h_bytes : 0u);
+    const uint32_t bytes = (3 + (kHasZ ? (kMulti ? 1 : 2) : 0)) * io_bytes +
+                           ((kVarB ? 1 : 0) + (kVarC ? 1 : 0)) * bc_bytes + (k > 0 ? h_bytes : 0u);
     mbar_expect_tx(bar, bytes);
     const int t0 = k * kTile;
     tma_load_3d(&sm.u[s][0][0], &P.tm_u, t0, c0, b, bar);
@@ -154,11 +163,11 @@ __global__ void __launch_bounds__(32 * kNW, 3) ss_bwd_kernel(const __grid_consta
     tma_load_3d(&sm.g[s][0][0], &P.tm_g, t0, c0, b, bar);
     if constexpr (kHasZ) {
       tma_load_3d(&sm.z[s][0][0], &P.tm_z, t0, c0, b, bar);
-      tma_load_3d(&sm.y[s][0][0], &P.tm_y, t0, c0, b, bar);
+      if constexpr (!kMulti) tma_load_3d(&sm.y[s][0][0], &P.tm_y, t0, c0, b, bar);
     }
-    if constexpr (kVarB) tma_load_3d(&sm.Braw[s][0], &P.tm_B, t0, 0, b * f.ngroups + grp, bar);
-    if constexpr (kVarC) tma_load_3d(&sm.Craw[s][0], &P.tm_C, t0, 0, b * f.ngroups + grp, bar);
-    if (k > 0) tma_load_3d(&sm.hck[s][0][0], &P.tm_h, c0, 0, b * ntiles + (k - 1), bar);
+    if constexpr (kVarB) tma_load_3d(&sm.Braw[s][0], &P.tm_B, t0, n0, b * f.ngroups + grp, bar);
+    if constexpr (kVarC) tma_load_3d(&sm.Craw[s][0], &P.tm_C, t0, n0, b * f.ngroups + grp, bar);
+    if (k > 0) tma_load_3d(&sm.hck[s][0][0], &P.tm_h, c0, n0, b * ntiles + (k - 1), bar);
   };
   if constexpr (kTMA) {
     if (tid == 0) {
@@ -190,15 +199,15 @@ __global__ void __launch_bounds__(32 * kNW, 3) ss_bwd_kernel(const __grid_consta
       load_tile<IT, NT>(sm.g[0], gb + t0, a.dout_dim_stride, nvalid, tlen, P.vec_dout);
       if constexpr (kHasZ) {
         load_tile<IT, NT>(sm.z[0], zb + t0, f.z_dim_stride, nvalid, tlen, P.vec_z);
-        load_tile<IT, NT>(sm.y[0], yb + t0, a.y_dim_stride, nvalid, tlen, P.vec_y);
+        if constexpr (!kMulti) load_tile<IT, NT>(sm.y[0], yb + t0, a.y_dim_stride, nvalid, tlen, P.vec_y);
       }
       if constexpr (kVarB) {
-        if (bc_f32) load_bc_tile<float, NT, NS>(sm.B_s, (const float*)f.B + bc_off + t0, L, N, tlen);
-        else load_bc_tile<IT, NT, NS>(sm.B_s, (const IT*)f.B + bc_off + t0, L, N, tlen);
+        if (bc_f32) load_bc_tile<float, NT, NS>(sm.B_s, (const float*)f.B + bc_off + t0, L, N - n0, tlen);
+        else load_bc_tile<IT, NT, NS>(sm.B_s, (const IT*)f.B + bc_off + t0, L, N - n0, tlen);
       }
       if constexpr (kVarC) {
-        if (bc_f32) load_bc_tile<float, NT, NS>(sm.C_s, (const float*)f.C + bc_off + t0, L, N, tlen);
-        else load_bc_tile<IT, NT, NS>(sm.C_s, (const IT*)f.C + bc_off + t0, L, N, tlen);
+        if (bc_f32) load_bc_tile<float, NT, NS>(sm.C_s, (const float*)f.C + bc_off + t0, L, N - n0, tlen);
+        else load_bc_tile<IT, NT, NS>(sm.C_s, (const IT*)f.C + bc_off + t0, L, N - n0, tlen);
       }
       // states at the tile start (end of the previous tile), from the forward's checkpoints
 #pragma unroll
@@ -206,7 +215,7 @@ __global__ void __launch_bounds__(32 * kNW, 3) ss_bwd_kernel(const __grid_consta
         float hv[2];
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
-          const int n = kSPW * w + 2 * p + h;
+          const int n = n0 + kSPW * w + 2 * p + h;
           hv[h] = (k > 0 && lane_ok && n < N) ? f.ckpt[(((int64_t)b * ntiles + (k - 1)) * N + n) * f.dim + c] : 0.f;
         }
         hp[0][p] = make_float2(hv[0], hv[1]);
@@ -378,9 +387,9 @@ __global__ void __launch_bounds__(32 * kNW, 3) ss_bwd_kernel(const __grid_consta
     // ---- dB / dC of this tile: 4 consecutive steps of one (B|C, n) row per lane
     if constexpr (kFold) {
       const int type = lane >> 4, j = (lane >> 2) & 3, tt = 4 * (lane & 3);
-      const int n = kSPW * w + j;
+      const int n = kSPW * w + j;  // within the group: dst rows start at bc_off (row n0)
       const bool want = (type == 0) ? kVarB : kVarC;
-      if (want && n < N) {
+      if (want && n0 + n < N) {
         const int k = j * 2 + type;
         const float4 v = *reinterpret_cast<const float4*>(&sm.fout[w][k][tt ^ (4 * (k >> 1))]);
         float* dst = (type == 0 ? a.dB : a.dC) + bc_off + (int64_t)n * L + t0 + tt;
@@ -398,7 +407,20 @@ __global__ void __launch_bounds__(32 * kNW, 3) ss_bwd_kernel(const __grid_consta
     __syncthreads();
 
     // ---- element phase 2: du, ddelta, dz
-    {
+    if constexpr (kMulti) {
+      // state groups: this CTA's (S1, S2) over its states go to the workspace; the finish
+      // kernel forms the element gradients from the sums over every group
+      const int nv = pc_ok ? max(0, min(S, tlen - pq * S)) : 0;
+      float* wrow = f.work + (((int64_t)b * f.dim + c0 + pc) * L + t0 + pq * S) * 2;
+#pragma unroll
+      for (int i = 0; i < S; ++i) {
+        const int t = pq * S + i;
+        float2 S12 = make_float2(0.f, 0.f);
+#pragma unroll
+        for (int g = 0; g < kNW; ++g) S12 = add2(S12, *reinterpret_cast<const float2*>(&sm.s12_s[g][t][2 * pc]));
+        if (i < nv) red_add_v2(wrow + 2 * i, S12.x, S12.y);
+      }
+    } else {
       float uv[S], yv[S];
       lds_run<IT, S>(&sm.u[stg][pc][pq * S], uv);
       if constexpr (kHasZ) lds_run<IT, S>(&sm.y[stg][pc][pq * S], yv);
@@ -444,7 +466,7 @@ __global__ void __launch_bounds__(32 * kNW, 3) ss_bwd_kernel(const __grid_consta
     const float dAv[2] = {dA2[p].x, dA2[p].y}, dBv[2] = {dBc[p].x, dBc[p].y}, dCv[2] = {dCc[p].x, dCc[p].y};
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
-      const int n = kSPW * w + 2 * p + h;
+      const int n = n0 + kSPW * w + 2 * p + h;
       if (lane_ok && n < N) {
         const int64_t ia = (int64_t)c * N + n;
         red_add(a.dA + ia, dAv[h]);
@@ -453,15 +475,80 @@ __global__ void __launch_bounds__(32 * kNW, 3) ss_bwd_kernel(const __grid_consta
       }
     }
   }
-  // the kNW element-role threads of a channel are adjacent lanes
+  if constexpr (!kMulti) {  // (state groups: bwd_finish_kernel accumulates dD and ddelta_bias)
+    // the kNW element-role threads of a channel are adjacent lanes
 #pragma unroll
-  for (int o = 1; o < kNW; o <<= 1) {
-    dD_acc += __shfl_xor_sync(0xffffffffu, dD_acc, o);
-    db_acc += __shfl_xor_sync(0xffffffffu, db_acc, o);
+    for (int o = 1; o < kNW; o <<= 1) {
+      dD_acc += __shfl_xor_sync(0xffffffffu, dD_acc, o);
+      db_acc += __shfl_xor_sync(0xffffffffu, db_acc, o);
+    }
+    if (pq == 0 && pc_ok) {
+      if (a.dD != nullptr) red_add(a.dD + c0 + pc, dD_acc);
+      if (a.ddelta_bias != nullptr) red_add(a.ddelta_bias + c0 + pc, db_acc);
+    }
   }
-  if (pq == 0 && pc_ok) {
-    if (a.dD != nullptr) red_add(a.dD + c0 + pc, dD_acc);
-    if (a.ddelta_bias != nullptr) red_add(a.ddelta_bias + c0 + pc, db_acc);
+}
+
+// dstate > 16: the element gradients from the (S1, S2) sums over every state group that the
+// scan CTAs left in the workspace ([b][c][t][2]), with the element phases' formulas
+// (backward_kernel.cu:499-521 and the gate):
+//   du = D dy + delta' S2,   ddelta = (S1 + u S2) * softplus'(delta + bias),   dz = gz * y,
+// plus dD += dy u and ddelta_bias += ddelta (one atomic per block: a block covers 256 steps of
+// one (batch, channel) row).  One thread per element.
+template <typename IT>
+__global__ void __launch_bounds__(256) bwd_finish_kernel(const __grid_constant__ ss_bwd_args a, int nlc) {
+  const ss_fwd_args& f = a.f;
+  const int64_t row = blockIdx.x / nlc;               // b * dim + c
+  const int t = (blockIdx.x % nlc) * 256 + threadIdx.x;
+  const int64_t b = row / f.dim, c = row % f.dim;
+  float dD = 0.f, db = 0.f;
+  if (t < f.seqlen) {
+    const float u = to_f<IT>(((const IT*)f.u)[b * f.u_batch_stride + c * f.u_dim_stride + t]);
+    const float v = to_f<IT>(((const IT*)f.delta)[b * f.delta_batch_stride + c * f.delta_dim_stride + t]) +
+                    (f.delta_bias != nullptr ? f.delta_bias[c] : 0.f);
+    float dt = v, sg = 1.f;
+    if (f.delta_softplus) softplus_and_slope(v, dt, sg);
+    const float g = to_f<IT>(((const IT*)a.dout)[b * a.dout_batch_stride + c * a.dout_dim_stride + t]);
+    float dy = g, gz = 0.f;
+    if (f.z != nullptr) {
+      const float zv = to_f<IT>(((const IT*)f.z)[b * f.z_batch_stride + c * f.z_dim_stride + t]);
+      const float sz = sigmoid_fast(zv);
+      dy = g * zv * sz;
+      gz = g * sz * fmaf(zv, 1.f - sz, 1.f);
+    }
+    const float2 S12 = *reinterpret_cast<const float2*>(f.work + (row * f.seqlen + t) * 2);
+    const float Dv = f.D != nullptr ? f.D[c] : 0.f;
+    const float dd = fmaf(u, S12.y, S12.x) * sg;
+    ((IT*)a.du)[b * a.du_batch_stride + c * a.du_dim_stride + t] = from_f<IT>(fmaf(Dv, dy, dt * S12.y));
+    ((IT*)a.ddelta)[b * a.ddelta_batch_stride + c * a.ddelta_dim_stride + t] = from_f<IT>(dd);
+    if (f.z != nullptr) {
+      const float yv = to_f<IT>(((const IT*)a.y)[b * a.y_batch_stride + c * a.y_dim_stride + t]);
+      ((IT*)a.dz)[b * a.dz_batch_stride + c * a.dz_dim_stride + t] = from_f<IT>(gz * yv);
+    }
+    dD = dy * u;
+    db = dd;
+  }
+  __shared__ float red[2][8];
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    dD += __shfl_xor_sync(0xffffffffu, dD, o);
+    db += __shfl_xor_sync(0xffffffffu, db, o);
+  }
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  if (lane == 0) {
+    red[0][wid] = dD;
+    red[1][wid] = db;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float sD = 0.f, sb = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      sD += red[0][i];
+      sb += red[1][i];
+    }
+    if (a.dD != nullptr) red_add(a.dD + c, sD);
+    if (a.ddelta_bias != nullptr) red_add(a.ddelta_bias + c, sb);
   }
 }
 

@@ -11,6 +11,7 @@
 
 #include "../../include/mamba_b200_ss.h"
 #include "ss_common.cuh"
+#include "ss_step.cuh"  // step_shape
 
 namespace ssb {
 template <typename IT> cudaError_t launch_fwd(const FwdK&, cudaStream_t, bool);
@@ -112,12 +113,24 @@ bool rows16(const void* p, int64_t bs, int64_t ds, size_t es) {
          ((ds * (int64_t)es) & 15) == 0;
 }
 
+constexpr int64_t kMaxGrid = 2147483647;  // gridDim.x
+
 int check_fwd(const ss_fwd_args* a) {
   if (a == nullptr) return SS_ERR_INVALID;
   if (a->batch < 0 || a->dim < 1 || a->seqlen < 0 || a->dstate < 1 || a->ngroups < 1) return SS_ERR_INVALID;
   if (a->dim % a->ngroups != 0) return SS_ERR_INVALID;
-  if (a->batch > 65535) return SS_ERR_UNSUPPORTED;
   if (a->dstate > SS_MAX_DSTATE) return SS_ERR_UNSUPPORTED;
+  // flattened grids: scan CTAs (batch x state groups x 32-channel tiles) and, with state
+  // groups, the finishing pass (batch x dim x 256-step chunks)
+  const int64_t dpg = a->dim / a->ngroups;
+  const int64_t nct = (int64_t)a->ngroups * ((dpg + ssb::kCh - 1) / ssb::kCh);
+  const int64_t nsg = ssb::state_groups(a->dstate);
+  if ((int64_t)a->batch * nsg * nct > kMaxGrid) return SS_ERR_UNSUPPORTED;
+  if (nsg > 1) {
+    if ((int64_t)a->batch * a->dim * (((int64_t)a->seqlen + 255) / 256) > kMaxGrid) return SS_ERR_UNSUPPORTED;
+    if (a->work == nullptr && a->batch > 0 && a->seqlen > 0) return SS_ERR_INVALID;
+    if ((reinterpret_cast<uintptr_t>(a->work) & 15) != 0) return SS_ERR_INVALID;  // vector reductions
+  }
   if (!dtype_ok(a->io_dtype) || !dtype_ok(a->bc_dtype)) return SS_ERR_UNSUPPORTED;
   if (a->bc_dtype != SS_F32 && a->bc_dtype != a->io_dtype) return SS_ERR_UNSUPPORTED;
   if (!a->u || !a->delta || !a->A || !a->B || !a->C) return SS_ERR_INVALID;
@@ -127,10 +140,13 @@ int check_fwd(const ss_fwd_args* a) {
   return SS_OK;
 }
 
-void derive(const ss_fwd_args& a, int& dpg, int& tpg, int& ntiles) {
-  dpg = a.dim / a.ngroups;
-  tpg = (dpg + ssb::kCh - 1) / ssb::kCh;
-  ntiles = (a.seqlen + ssb::kTile - 1) / ssb::kTile;
+template <typename K>
+void derive(const ss_fwd_args& a, K& P) {
+  P.dpg = a.dim / a.ngroups;
+  P.tpg = (P.dpg + ssb::kCh - 1) / ssb::kCh;
+  P.nct = a.ngroups * P.tpg;
+  P.nsg = ssb::state_groups(a.dstate);
+  P.ntiles = (a.seqlen + ssb::kTile - 1) / ssb::kTile;
 }
 
 template <typename F>
@@ -153,6 +169,11 @@ size_t ss_ckpt_elems(int batch, int dim, int seqlen, int dstate) {
   return (size_t)batch * ntiles * (size_t)dstate * (size_t)dim;
 }
 
+size_t ss_work_elems(int batch, int dim, int seqlen, int dstate) {
+  if (batch <= 0 || dim <= 0 || seqlen <= 0 || dstate <= ssb::kGroupStates) return 0;
+  return 2 * (size_t)batch * (size_t)dim * (size_t)seqlen;
+}
+
 int ss_fwd(const ss_fwd_args* args, void* stream) {
   int rc = check_fwd(args);
   if (rc != SS_OK) return rc;
@@ -160,13 +181,14 @@ int ss_fwd(const ss_fwd_args* args, void* stream) {
   if (args->batch == 0 || args->seqlen == 0) return SS_OK;
   ssb::FwdK P{};
   P.a = *args;
-  derive(P.a, P.dpg, P.tpg, P.ntiles);
+  derive(P.a, P);
   const size_t es = esize(args->io_dtype);
   P.vec_u = rows16(args->u, args->u_batch_stride, args->u_dim_stride, es);
   P.vec_d = rows16(args->delta, args->delta_batch_stride, args->delta_dim_stride, es);
   P.vec_z = args->z ? rows16(args->z, args->z_batch_stride, args->z_dim_stride, es) : 0;
   P.vec_out = rows16(args->out, args->out_batch_stride, args->out_dim_stride, es);
   P.vec_y = args->out_y ? rows16(args->out_y, args->out_y_batch_stride, args->out_y_dim_stride, es) : 0;
+  P.vec_work = args->work != nullptr && (reinterpret_cast<uintptr_t>(args->work) & 15) == 0 && (args->seqlen % 4) == 0;
   P.status = status_ptr();
   const ss_fwd_args& a = *args;
   bool tma = map_rows(&P.tm_u, a.u, a.io_dtype, a, a.u_batch_stride, a.u_dim_stride) &&
@@ -201,7 +223,7 @@ int ss_bwd(const ss_bwd_args* args, void* stream) {
   if (f.batch == 0 || f.seqlen == 0) return SS_OK;
   ssb::BwdK P{};
   P.a = *args;
-  derive(f, P.dpg, P.tpg, P.ntiles);
+  derive(f, P);
   const size_t es = esize(f.io_dtype);
   P.vec_u = rows16(f.u, f.u_batch_stride, f.u_dim_stride, es);
   P.vec_d = rows16(f.delta, f.delta_batch_stride, f.delta_dim_stride, es);
@@ -238,7 +260,13 @@ int ss_bwd(const ss_bwd_args* args, void* stream) {
 int ss_step(const ss_step_args* a, void* stream) {
   if (a == nullptr) return SS_ERR_INVALID;
   if (a->batch < 0 || a->dim < 1 || a->dstate < 1 || a->ngroups < 1 || a->dim % a->ngroups) return SS_ERR_INVALID;
-  if (a->dstate > SS_MAX_DSTATE || a->batch > 65535) return SS_ERR_UNSUPPORTED;
+  if (a->dstate > SS_MAX_DSTATE) return SS_ERR_UNSUPPORTED;
+  {
+    int tpc, chunks;
+    ssb::step_shape(a->dstate, tpc, chunks);
+    const int64_t cpb = 128 / tpc;
+    if ((int64_t)a->batch * ((a->dim + cpb - 1) / cpb) > kMaxGrid) return SS_ERR_UNSUPPORTED;
+  }
   if (!dtype_ok(a->io_dtype) || !dtype_ok(a->bc_dtype)) return SS_ERR_UNSUPPORTED;
   if (a->bc_dtype != SS_F32 && a->bc_dtype != a->io_dtype) return SS_ERR_UNSUPPORTED;
   if (!a->state || !a->x || !a->dt || !a->A || !a->B || !a->C || !a->out) return SS_ERR_INVALID;
@@ -253,7 +281,7 @@ const char* ss_status_string(int s) {
   switch (s) {
     case SS_OK: return "ok";
     case SS_ERR_INVALID: return "invalid argument (null pointer, size, stride or group count)";
-    case SS_ERR_UNSUPPORTED: return "unsupported dtype combination, dstate > 16 or batch > 65535";
+    case SS_ERR_UNSUPPORTED: return "unsupported dtype combination, dstate > 256 or a size beyond the launch grid";
     case SS_ERR_CUDA: return "CUDA runtime error (see ss_last_cuda_error)";
     default: return "unknown status";
   }

@@ -3,7 +3,8 @@
 // Work decomposition used by every kernel here:
 //   * one CTA owns one batch row b and a tile of 32 channels of one group (lane = channel);
 //   * warp w owns states 4w .. 4w+3 of those channels, so a CTA has ceil(dstate/4)
-//     warps (1, 2 or 4; dstate <= 16);
+//     warps (1, 2 or 4) for dstate <= 16; above that the states split into groups of 16,
+//     one CTA (4 warps) per group, whose per-element partial sums meet in a workspace;
 //   * time advances in tiles of kTile = 16 steps; each lane carries its 4 states in
 //     registers across tiles, so the whole sequence is scanned without any cross-thread
 //     scan (the reference runs a CUB block scan per state per 128-token chunk,
@@ -276,57 +277,6 @@ __device__ __forceinline__ void store_run(T* __restrict__ dst, const float (&v)[
   }
 }
 
-// Warp-wide transpose-reduction of per-step dB / dC contributions (a butterfly over the 32
-// lanes = channels).  Conceptually lane l holds K values v[type*64 + j*16 + t] (type 0 = B,
-// 1 = C; state j of the warp; step t of the tile), and after the five stages lane l holds
-// the sums over all lanes of entries (K/32)*l + i.  The stages whose pairs share a step run
-// inside the step loop (fold_step_*), the last ones once per tile (fold_tile), so at most
-// one partial per step stays live.
-__device__ __forceinline__ float bfly(float keep, float send, int o) {
-  return keep + __shfl_xor_sync(0xffffffffu, send, o);
-}
-// both B and C variable: stages with offsets 16 (B vs C), 8 (j vs j+2), 4 (j vs j+1)
-__device__ __forceinline__ float fold_step_bc(const float (&vB)[4], const float (&vC)[4], int lane) {
-  const bool u16 = lane & 16, u8 = lane & 8, u4 = lane & 4;
-  float x[4];
-#pragma unroll
-  for (int j = 0; j < 4; ++j) x[j] = bfly(u16 ? vC[j] : vB[j], u16 ? vB[j] : vC[j], 16);
-  float y[2];
-#pragma unroll
-  for (int j = 0; j < 2; ++j) y[j] = bfly(u8 ? x[j + 2] : x[j], u8 ? x[j] : x[j + 2], 8);
-  return bfly(u4 ? y[1] : y[0], u4 ? y[0] : y[1], 4);
-}
-// only one of B, C variable: stages with offsets 16 (j vs j+2), 8 (j vs j+1)
-__device__ __forceinline__ float fold_step_one(const float (&v)[4], int lane) {
-  const bool u16 = lane & 16, u8 = lane & 8;
-  float y[2];
-#pragma unroll
-  for (int j = 0; j < 2; ++j) y[j] = bfly(u16 ? v[j + 2] : v[j], u16 ? v[j] : v[j + 2], 16);
-  return bfly(u8 ? y[1] : y[0], u8 ? y[0] : y[1], 8);
-}
-// remaining stages over the 16 per-step partials W[t]; PER = 4 (offsets 2, 1: lane keeps
-// steps 4*(lane&3) ..) or PER = 2 (offsets 4, 2, 1: lane keeps steps 2*(lane&7) ..)
-template <int PER>
-__device__ __forceinline__ void fold_tile(const float (&W)[16], float (&out)[PER], int lane) {
-  if constexpr (PER == 4) {
-    const bool u2 = lane & 2, u1 = lane & 1;
-    float a[8];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) a[i] = bfly(u2 ? W[i + 8] : W[i], u2 ? W[i] : W[i + 8], 2);
-#pragma unroll
-    for (int i = 0; i < 4; ++i) out[i] = bfly(u1 ? a[i + 4] : a[i], u1 ? a[i] : a[i + 4], 1);
-  } else {
-    const bool u4 = lane & 4, u2 = lane & 2, u1 = lane & 1;
-    float a[8], b2[4];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) a[i] = bfly(u4 ? W[i + 8] : W[i], u4 ? W[i] : W[i + 8], 4);
-#pragma unroll
-    for (int i = 0; i < 4; ++i) b2[i] = bfly(u2 ? a[i + 4] : a[i], u2 ? a[i] : a[i + 4], 2);
-#pragma unroll
-    for (int i = 0; i < 2; ++i) out[i] = bfly(u1 ? b2[i + 2] : b2[i], u1 ? b2[i] : b2[i + 2], 1);
-  }
-}
-
 // Kernel-side parameter blocks (host fills the derived fields).  Tensor maps come first:
 // CUtensorMap is 64-byte aligned.
 struct FwdK {
@@ -334,18 +284,24 @@ struct FwdK {
   ss_fwd_args a;
   int dpg;        // channels per group
   int tpg;        // 32-channel tiles per group
+  int nct;        // 32-channel tiles in all (ngroups * tpg)
+  int nsg;        // state groups (1 for dstate <= 16, else ceil(dstate / 16))
   int ntiles;     // ceil(seqlen / kTile)
   int vec_u, vec_d, vec_z, vec_out, vec_y;
+  int vec_work;   // workspace rows are 16-byte aligned (seqlen % 4 == 0)
   int* status;    // device status word (kStatus* bits), nullable
 };
 
 struct BwdK {
   CUtensorMap tm_u, tm_d, tm_z, tm_g, tm_y, tm_B, tm_C, tm_h;
   ss_bwd_args a;
-  int dpg, tpg, ntiles;
+  int dpg, tpg, nct, nsg, ntiles;
   int vec_u, vec_d, vec_z, vec_dout, vec_du, vec_dd, vec_dz, vec_y;
   int vec_dbc;    // dB/dC rows are 16-byte aligned (seqlen % 4 == 0)
   int* status;
 };
+
+constexpr int kGroupStates = 16;  // states per CTA when dstate > 16 (4 warps x 4)
+inline int state_groups(int dstate) { return dstate <= kGroupStates ? 1 : (dstate + kGroupStates - 1) / kGroupStates; }
 
 }  // namespace ssb

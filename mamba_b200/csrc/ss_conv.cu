@@ -25,7 +25,9 @@ int check_conv(const ss_conv_args* a) {
   if (a == nullptr) return SS_ERR_INVALID;
   if (a->batch < 0 || a->dim < 1 || a->seqlen < 0 || a->width < 1) return SS_ERR_INVALID;
   if (a->width > SS_MAX_CONV_WIDTH) return SS_ERR_UNSUPPORTED;
-  if (a->batch > 65535 || ((int64_t)a->seqlen + kConvT - 1) / kConvT > 65535) return SS_ERR_UNSUPPORTED;
+  if ((int64_t)a->batch * (((int64_t)a->seqlen + kConvT - 1) / kConvT) * ((a->dim + kConvC - 1) / kConvC) >
+      2147483647LL)
+    return SS_ERR_UNSUPPORTED;
   if (!dt_ok(a->io_dtype)) return SS_ERR_UNSUPPORTED;
   if (!a->x || !a->weight) return SS_ERR_INVALID;
   if (a->x_batch_stride < 0 || a->x_seq_stride < 0) return SS_ERR_INVALID;
@@ -82,7 +84,9 @@ int ss_conv_fwd(const ss_conv_args* a, void* stream) {
   P.vec_u = al16(a->u, a->u_batch_stride, a->u_dim_stride, es);
   P.vec_z = a->z ? (al16(a->z, a->z_batch_stride, a->z_seq_stride, es) && a->dim % vw == 0) : 0;
   P.vec_zt = a->z ? al16(a->zt, a->zt_batch_stride, a->zt_dim_stride, es) : 0;
-  dim3 grid((a->dim + kConvC - 1) / kConvC, (a->seqlen + kConvT - 1) / kConvT, a->batch);
+  P.nc = (a->dim + kConvC - 1) / kConvC;
+  P.nt = (a->seqlen + kConvT - 1) / kConvT;
+  dim3 grid((unsigned)((int64_t)a->batch * P.nt * P.nc));
   return by_dtype(a->io_dtype, [&](auto tag) {
     using IT = decltype(tag);
     return by_width(K, [&](auto kc) {
@@ -123,7 +127,9 @@ int ss_conv_bwd(const ss_conv_bwd_args* a, void* stream) {
   P.vec_dx = al16(a->dx, a->dx_batch_stride, a->dx_seq_stride, es) && f.dim % vw == 0;
   P.vec_dzt = a->dzt ? al16(a->dzt, a->dzt_batch_stride, a->dzt_dim_stride, es) : 0;
   P.vec_dz = a->dzt ? (al16(a->dz, a->dz_batch_stride, a->dz_seq_stride, es) && f.dim % vw == 0) : 0;
-  dim3 grid((f.dim + kConvC - 1) / kConvC, (f.seqlen + kConvT - 1) / kConvT, f.batch);
+  P.nc = (f.dim + kConvC - 1) / kConvC;
+  P.nt = (f.seqlen + kConvT - 1) / kConvT;
+  dim3 grid((unsigned)((int64_t)f.batch * P.nt * P.nc));
   return by_dtype(f.io_dtype, [&](auto tag) {
     using IT = decltype(tag);
     return by_width(K, [&](auto kc) {
@@ -142,17 +148,18 @@ int ss_conv_step(const ss_conv_step_args* a, void* stream) {
   if (a == nullptr) return SS_ERR_INVALID;
   if (a->batch < 0 || a->dim < 1 || a->width < 1) return SS_ERR_INVALID;
   if (a->width > SS_MAX_CONV_WIDTH) return SS_ERR_UNSUPPORTED;
-  if (a->batch > 65535) return SS_ERR_UNSUPPORTED;
+  const int ncb = (a->dim + 127) / 128;
+  if ((int64_t)a->batch * ncb > 2147483647LL) return SS_ERR_UNSUPPORTED;
   if (!dt_ok(a->io_dtype)) return SS_ERR_UNSUPPORTED;
   if (!a->x || !a->weight || !a->u || (a->width > 1 && !a->state)) return SS_ERR_INVALID;
   if (a->state_batch_stride < 0 || a->x_batch_stride < 0 || a->u_batch_stride < 0) return SS_ERR_INVALID;
   if (a->batch == 0) return SS_OK;
   cudaStream_t st = (cudaStream_t)stream;
-  dim3 grid((a->dim + 127) / 128, a->batch);
+  dim3 grid((unsigned)((int64_t)a->batch * ncb));
   return by_dtype(a->io_dtype, [&](auto tag) {
     using IT = decltype(tag);
     return by_width(a->width, [&](auto kc) {
-      conv_step_kernel<IT, decltype(kc)::value><<<grid, 128, 0, st>>>(*a);
+      conv_step_kernel<IT, decltype(kc)::value><<<grid, 128, 0, st>>>(*a, ncb);
       return cudaGetLastError();
     });
   });

@@ -30,8 +30,11 @@ constexpr int kConvC = 64;   // channels per tile
 constexpr int kConvThreads = 256;
 constexpr int kConvTPT = 16; // steps per thread (kConvThreads / kConvC thread rows of 16)
 
+// The conv grids are flattened: blockIdx.x = (batch row * nt + step tile) * nc + channel
+// tile, so no size is bound by gridDim.y / gridDim.z.
 struct ConvK {
   ss_conv_args a;
+  int nc, nt;   // channel tiles, step tiles
   int vec_x;    // x rows 16-byte aligned with dim a multiple of the vector width
   int vec_u;    // u rows 16-byte aligned
   int vec_z, vec_zt;
@@ -39,6 +42,7 @@ struct ConvK {
 
 struct ConvBwdK {
   ss_conv_bwd_args a;
+  int nc, nt;
   int vec_x, vec_du, vec_dx, vec_dzt, vec_dz;
 };
 
@@ -206,7 +210,8 @@ __global__ void __launch_bounds__(kConvThreads) conv_fwd_kernel(const __grid_con
   extern __shared__ __align__(16) unsigned char conv_smem[];
   ConvFwdSmem<IT, K>& sm = *reinterpret_cast<ConvFwdSmem<IT, K>*>(conv_smem);
   const ss_conv_args& a = P.a;
-  const int c0 = blockIdx.x * kConvC, t0 = blockIdx.y * kConvT, b = blockIdx.z;
+  const int c0 = (blockIdx.x % P.nc) * kConvC, t0 = ((blockIdx.x / P.nc) % P.nt) * kConvT;
+  const int b = blockIdx.x / P.nc / P.nt;
   const int L = a.seqlen, dim = a.dim;
   const IT* xb = (const IT*)a.x + (int64_t)b * a.x_batch_stride;
   const float* state_b = a.state_in != nullptr ? a.state_in + (int64_t)b * dim * (K - 1) : nullptr;
@@ -278,7 +283,8 @@ __global__ void __launch_bounds__(kConvThreads) conv_bwd_kernel(const __grid_con
   ConvBwdSmem<IT, K>& sm = *reinterpret_cast<ConvBwdSmem<IT, K>*>(conv_smem);
   const ss_conv_bwd_args& a = P.a;
   const ss_conv_args& f = a.f;
-  const int c0 = blockIdx.x * kConvC, t0 = blockIdx.y * kConvT, b = blockIdx.z;
+  const int c0 = (blockIdx.x % P.nc) * kConvC, t0 = ((blockIdx.x / P.nc) % P.nt) * kConvT;
+  const int b = blockIdx.x / P.nc / P.nt;
   const int L = f.seqlen, dim = f.dim;
   const IT* xb = (const IT*)f.x + (int64_t)b * f.x_batch_stride;
   const float* state_b = f.state_in != nullptr ? f.state_in + (int64_t)b * dim * (K - 1) : nullptr;
@@ -386,8 +392,8 @@ __global__ void __launch_bounds__(kConvThreads) conv_bwd_kernel(const __grid_con
 // One decode step: window = [state (oldest first), x]; u = silu(bias + w . window);
 // state <- window[1:].  One thread per (batch, channel).
 template <typename IT, int K>
-__global__ void __launch_bounds__(128) conv_step_kernel(const __grid_constant__ ss_conv_step_args a) {
-  const int c = blockIdx.x * 128 + threadIdx.x, b = blockIdx.y;
+__global__ void __launch_bounds__(128) conv_step_kernel(const __grid_constant__ ss_conv_step_args a, int ncb) {
+  const int c = (blockIdx.x % ncb) * 128 + threadIdx.x, b = blockIdx.x / ncb;
   if (c >= a.dim) return;
   float win[K];
   float* st = a.state + (int64_t)b * a.state_batch_stride + (int64_t)c * (K - 1);

@@ -21,6 +21,14 @@
 // ckpt[b][tile][n][c] (coalesced over channels); the last tile's entry is the final state.
 // When a tensor cannot be described by a TMA map (unaligned pointer or stride) the same
 // kernel loads each tile synchronously with vector or scalar loads instead (kTMA = false).
+//
+// dstate > 16 (the reference's kernels take up to 256): the states split into groups of 16,
+// one CTA per (32 channels, state group), each running its states from zero exactly as above.
+// The sum over states then spans CTAs, so with kMulti each CTA adds its partial
+// sum_n C*h (group 0 also D*u) into an fp32 workspace row with vector reductions instead of
+// finishing the output; fwd_finish_kernel applies the gate and stores out / out_y afterwards.
+// The grid is flattened: blockIdx.x = (batch row * state groups + group) * channel tiles + tile,
+// so batch is not bound by gridDim.y.
 #pragma once
 #include "ss_common.cuh"
 
@@ -80,8 +88,9 @@ __device__ __forceinline__ void widen_bc_warp(float (*Bd)[NS], float (*Cd)[NS], 
   for (int t = 0; t < kTile; ++t) dst[t][n] = v[t];
 }
 
-template <typename IT, int kNW, bool kVarB, bool kVarC, bool kHasZ, bool kTMA>
+template <typename IT, int kNW, bool kVarB, bool kVarC, bool kHasZ, bool kTMA, bool kMulti = false>
 __global__ void __launch_bounds__(32 * kNW, 4) ss_fwd_kernel(const __grid_constant__ FwdK P) {
+  static_assert(!(kMulti && kHasZ), "state groups apply the gate in fwd_finish_kernel");
   constexpr int NT = 32 * kNW;
   constexpr int NS = kSPW * kNW;   // states covered by the CTA (dstate padded up)
   constexpr int S = kTile / kNW;   // steps per thread in the element-wise phases
@@ -91,11 +100,15 @@ __global__ void __launch_bounds__(32 * kNW, 4) ss_fwd_kernel(const __grid_consta
   const ss_fwd_args& a = P.a;
 
   const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
-  const int grp = blockIdx.x / P.tpg;
-  const int cl0 = (blockIdx.x % P.tpg) * kCh;
+  const int ctile = blockIdx.x % P.nct;
+  const int bsg = blockIdx.x / P.nct;
+  const int sg = bsg % P.nsg;            // state group: states n0 .. n0 + 15
+  const int b = bsg / P.nsg;
+  const int grp = ctile / P.tpg;
+  const int cl0 = (ctile % P.tpg) * kCh;
   const int c0 = grp * P.dpg + cl0;
   const int nvalid = min(kCh, P.dpg - cl0);
-  const int b = blockIdx.y;
+  const int n0 = sg * kSPW * kNW;
   const int N = a.dstate, L = a.seqlen;
   const bool bc_f32 = a.bc_dtype == SS_F32;
   const int ntiles = P.ntiles;
@@ -109,7 +122,7 @@ __global__ void __launch_bounds__(32 * kNW, 4) ss_fwd_kernel(const __grid_consta
     float av[2], bv[2], cv[2];
 #pragma unroll
     for (int q = 0; q < 2; ++q) {
-      const int n = kSPW * w + 2 * p + q;
+      const int n = n0 + kSPW * w + 2 * p + q;
       const bool ok = lane_ok && n < N;
       const int64_t ia = (int64_t)c * N + n;
       av[q] = ok ? a.A[ia] * kLog2e : 0.f;
@@ -133,7 +146,7 @@ __global__ void __launch_bounds__(32 * kNW, 4) ss_fwd_kernel(const __grid_consta
   IT* yrow = (kHasZ && a.out_y != nullptr)
                  ? (IT*)a.out_y + (int64_t)b * a.out_y_batch_stride + (int64_t)(c0 + pc) * a.out_y_dim_stride
                  : nullptr;
-  const int64_t bc_off = ((int64_t)b * a.ngroups + grp) * N * (int64_t)L;
+  const int64_t bc_off = (((int64_t)b * a.ngroups + grp) * N + n0) * (int64_t)L;  // row n0 of this group
 
   // ---- producer (thread 0): TMA ring
   const uint32_t bc_bytes = NS * kTile * (bc_f32 ? 4u : (uint32_t)sizeof(IT));
@@ -146,8 +159,8 @@ __global__ void __launch_bounds__(32 * kNW, 4) ss_fwd_kernel(const __grid_consta
     tma_load_3d(&sm.u[s][0][0], &P.tm_u, t0, c0, b, bar);
     tma_load_3d(&sm.d[s][0][0], &P.tm_d, t0, c0, b, bar);
     if constexpr (kHasZ) tma_load_3d(&sm.z[s][0][0], &P.tm_z, t0, c0, b, bar);
-    if constexpr (kVarB) tma_load_3d(&sm.Braw[s][0], &P.tm_B, t0, 0, b * a.ngroups + grp, bar);
-    if constexpr (kVarC) tma_load_3d(&sm.Craw[s][0], &P.tm_C, t0, 0, b * a.ngroups + grp, bar);
+    if constexpr (kVarB) tma_load_3d(&sm.Braw[s][0], &P.tm_B, t0, n0, b * a.ngroups + grp, bar);
+    if constexpr (kVarC) tma_load_3d(&sm.Craw[s][0], &P.tm_C, t0, n0, b * a.ngroups + grp, bar);
   };
   if constexpr (kTMA) {
     if (tid == 0) {
@@ -176,12 +189,12 @@ __global__ void __launch_bounds__(32 * kNW, 4) ss_fwd_kernel(const __grid_consta
       load_tile<IT, NT>(sm.d[0], db + t0, a.delta_dim_stride, nvalid, tlen, P.vec_d);
       if constexpr (kHasZ) load_tile<IT, NT>(sm.z[0], zb + t0, a.z_dim_stride, nvalid, tlen, P.vec_z);
       if constexpr (kVarB) {
-        if (bc_f32) load_bc_tile<float, NT, NS>(sm.B_s, (const float*)a.B + bc_off + t0, L, N, tlen);
-        else load_bc_tile<IT, NT, NS>(sm.B_s, (const IT*)a.B + bc_off + t0, L, N, tlen);
+        if (bc_f32) load_bc_tile<float, NT, NS>(sm.B_s, (const float*)a.B + bc_off + t0, L, N - n0, tlen);
+        else load_bc_tile<IT, NT, NS>(sm.B_s, (const IT*)a.B + bc_off + t0, L, N - n0, tlen);
       }
       if constexpr (kVarC) {
-        if (bc_f32) load_bc_tile<float, NT, NS>(sm.C_s, (const float*)a.C + bc_off + t0, L, N, tlen);
-        else load_bc_tile<IT, NT, NS>(sm.C_s, (const IT*)a.C + bc_off + t0, L, N, tlen);
+        if (bc_f32) load_bc_tile<float, NT, NS>(sm.C_s, (const float*)a.C + bc_off + t0, L, N - n0, tlen);
+        else load_bc_tile<IT, NT, NS>(sm.C_s, (const IT*)a.C + bc_off + t0, L, N - n0, tlen);
       }
       __syncthreads();
     }
@@ -276,14 +289,36 @@ __global__ void __launch_bounds__(32 * kNW, 4) ss_fwd_kernel(const __grid_consta
       const float hv[kSPW] = {h[0].x, h[0].y, h[1].x, h[1].y};
 #pragma unroll
       for (int j = 0; j < kSPW; ++j) {
-        const int n = kSPW * w + j;
+        const int n = n0 + kSPW * w + j;
         if (n < N) ck[(int64_t)n * a.dim] = hv[j];
       }
     }
     __syncthreads();
 
     // ---- 3. combine the warps' partial sums, add D*u, gate, store
-    {
+    if constexpr (kMulti) {
+      // state groups: this CTA's share of y (group 0 adds D*u) goes to the fp32 workspace
+      float uo[S], ys[S];
+      lds_run<IT, S>(&sm.u[stg][pc][pq * S], uo);
+#pragma unroll
+      for (int i = 0; i < S; ++i) {
+        const int t = pq * S + i;
+        float y = sg == 0 ? Dv * uo[i] : 0.f;
+#pragma unroll
+        for (int g = 0; g < kNW; ++g) y += sm.y_s[k & 1][g][t][pc];
+        ys[i] = y;
+      }
+      const int nv = pc_ok ? max(0, min(S, tlen - pq * S)) : 0;
+      float* wrow = a.work + ((int64_t)b * a.dim + c0 + pc) * L + t0 + pq * S;
+      if (P.vec_work && nv == S) {
+#pragma unroll
+        for (int i = 0; i < S; i += 4) red_add_v4(wrow + i, ys[i], ys[i + 1], ys[i + 2], ys[i + 3]);
+      } else {
+#pragma unroll
+        for (int i = 0; i < S; ++i)
+          if (i < nv) red_add(wrow + i, ys[i]);
+      }
+    } else {
       float yv[S], uo[S], zo[S], yu[S];
       lds_run<IT, S>(&sm.u[stg][pc][pq * S], uo);
       if constexpr (kHasZ) lds_run<IT, S>(&sm.z[stg][pc][pq * S], zo);
@@ -315,10 +350,28 @@ __global__ void __launch_bounds__(32 * kNW, 4) ss_fwd_kernel(const __grid_consta
     const float hv[kSPW] = {h[0].x, h[0].y, h[1].x, h[1].y};
 #pragma unroll
     for (int j = 0; j < kSPW; ++j) {
-      const int n = kSPW * w + j;
+      const int n = n0 + kSPW * w + j;
       if (n < N) ls[n] = hv[j];
     }
   }
+}
+
+// dstate > 16: out = work * silu(z) (or work), out_y = work when a gate is given; work holds
+// D*u + sum over all states of C*h for every (batch, channel, step), packed [b][c][t].
+// One thread per element; the grid is flattened over rows x 256-step chunks.
+template <typename IT>
+__global__ void __launch_bounds__(256) fwd_finish_kernel(const __grid_constant__ ss_fwd_args a, int nlc) {
+  const int64_t row = blockIdx.x / nlc;              // b * dim + c
+  const int t = (blockIdx.x % nlc) * 256 + threadIdx.x;
+  if (t >= a.seqlen) return;
+  const int64_t b = row / a.dim, c = row % a.dim;
+  float y = a.work[row * a.seqlen + t];
+  if (a.z != nullptr) {
+    const float zv = to_f<IT>(((const IT*)a.z)[b * a.z_batch_stride + c * a.z_dim_stride + t]);
+    if (a.out_y != nullptr) ((IT*)a.out_y)[b * a.out_y_batch_stride + c * a.out_y_dim_stride + t] = from_f<IT>(y);
+    y *= zv * sigmoid_fast(zv);
+  }
+  ((IT*)a.out)[b * a.out_batch_stride + c * a.out_dim_stride + t] = from_f<IT>(y);
 }
 
 }  // namespace ssb

@@ -1,6 +1,6 @@
-// Kernel launchers: compile-time dispatch over the warp count (dstate <= 4, 8, 16),
-// variable / constant B and C, the z gate and the load path (TMA ring or synchronous).
-// Instantiated once per I/O dtype.
+// Kernel launchers: compile-time dispatch over the warp count (dstate <= 4, 8, 16, or state
+// groups of 16 above that), variable / constant B and C, the z gate and the load path (TMA
+// ring or synchronous).  Instantiated once per I/O dtype.
 #pragma once
 #include "ss_fwd.cuh"
 #include "ss_bwd.cuh"
@@ -20,73 +20,110 @@ static cudaError_t launch_dyn(K kernel, dim3 grid, int threads, size_t smem, cud
   return cudaGetLastError();
 }
 
-template <typename IT, int NW, bool VB, bool VC, bool Z>
+// ---- forward
+template <typename IT, int NW, bool VB, bool VC, bool Z, bool M>
 static cudaError_t fwd_go(const FwdK& P, dim3 grid, cudaStream_t st, bool tma) {
   const size_t smem = sizeof(FwdSmem<IT, NW, VB, VC, Z>);
-  if (tma) return launch_dyn(ss_fwd_kernel<IT, NW, VB, VC, Z, true>, grid, 32 * NW, smem, st, P);
-  return launch_dyn(ss_fwd_kernel<IT, NW, VB, VC, Z, false>, grid, 32 * NW, smem, st, P);
+  if (tma) return launch_dyn(ss_fwd_kernel<IT, NW, VB, VC, Z, true, M>, grid, 32 * NW, smem, st, P);
+  return launch_dyn(ss_fwd_kernel<IT, NW, VB, VC, Z, false, M>, grid, 32 * NW, smem, st, P);
 }
-template <typename IT, int NW, bool VB, bool VC>
+template <typename IT, int NW, bool VB, bool VC, bool M>
 static cudaError_t fwd_z(const FwdK& P, dim3 grid, cudaStream_t st, bool tma) {
-  return P.a.z != nullptr ? fwd_go<IT, NW, VB, VC, true>(P, grid, st, tma)
-                          : fwd_go<IT, NW, VB, VC, false>(P, grid, st, tma);
+  if constexpr (M) return fwd_go<IT, NW, VB, VC, false, true>(P, grid, st, tma);  // gate in the finish
+  else
+    return P.a.z != nullptr ? fwd_go<IT, NW, VB, VC, true, false>(P, grid, st, tma)
+                            : fwd_go<IT, NW, VB, VC, false, false>(P, grid, st, tma);
 }
-template <typename IT, int NW>
+template <typename IT, int NW, bool M>
 static cudaError_t fwd_bc(const FwdK& P, dim3 grid, cudaStream_t st, bool tma) {
   const bool vb = P.a.var_B != 0, vc = P.a.var_C != 0;
-  if (vb && vc) return fwd_z<IT, NW, true, true>(P, grid, st, tma);
-  if (vb) return fwd_z<IT, NW, true, false>(P, grid, st, tma);
-  if (vc) return fwd_z<IT, NW, false, true>(P, grid, st, tma);
-  return fwd_z<IT, NW, false, false>(P, grid, st, tma);
+  if (vb && vc) return fwd_z<IT, NW, true, true, M>(P, grid, st, tma);
+  if (vb) return fwd_z<IT, NW, true, false, M>(P, grid, st, tma);
+  if (vc) return fwd_z<IT, NW, false, true, M>(P, grid, st, tma);
+  return fwd_z<IT, NW, false, false, M>(P, grid, st, tma);
 }
 template <typename IT>
 cudaError_t launch_fwd(const FwdK& P, cudaStream_t st, bool tma) {
-  dim3 grid(P.a.ngroups * P.tpg, P.a.batch);
-  switch (warps_for(P.a.dstate)) {
-    case 1: return fwd_bc<IT, 1>(P, grid, st, tma);
-    case 2: return fwd_bc<IT, 2>(P, grid, st, tma);
-    default: return fwd_bc<IT, 4>(P, grid, st, tma);
+  const ss_fwd_args& a = P.a;
+  dim3 grid((unsigned)((int64_t)a.batch * P.nsg * P.nct));  // sizes checked on the host
+  if (P.nsg > 1) {
+    // state groups: partial sums meet in the workspace, then the gate is applied
+    cudaError_t e = cudaMemsetAsync(a.work, 0, (size_t)a.batch * a.dim * (size_t)a.seqlen * sizeof(float), st);
+    if (e != cudaSuccess) return e;
+    e = fwd_bc<IT, 4, true>(P, grid, st, tma);
+    if (e != cudaSuccess) return e;
+    const int nlc = (a.seqlen + 255) / 256;
+    fwd_finish_kernel<IT><<<(unsigned)((int64_t)a.batch * a.dim * nlc), 256, 0, st>>>(a, nlc);
+    return cudaGetLastError();
+  }
+  switch (warps_for(a.dstate)) {
+    case 1: return fwd_bc<IT, 1, false>(P, grid, st, tma);
+    case 2: return fwd_bc<IT, 2, false>(P, grid, st, tma);
+    default: return fwd_bc<IT, 4, false>(P, grid, st, tma);
   }
 }
 
-template <typename IT, int NW, bool VB, bool VC, bool Z>
+// ---- backward
+template <typename IT, int NW, bool VB, bool VC, bool Z, bool M>
 static cudaError_t bwd_go(const BwdK& P, dim3 grid, cudaStream_t st, bool tma) {
   const size_t smem = sizeof(BwdSmem<IT, NW, VB, VC, Z>);
-  if (tma) return launch_dyn(ss_bwd_kernel<IT, NW, VB, VC, Z, true>, grid, 32 * NW, smem, st, P);
-  return launch_dyn(ss_bwd_kernel<IT, NW, VB, VC, Z, false>, grid, 32 * NW, smem, st, P);
+  if (tma) return launch_dyn(ss_bwd_kernel<IT, NW, VB, VC, Z, true, M>, grid, 32 * NW, smem, st, P);
+  return launch_dyn(ss_bwd_kernel<IT, NW, VB, VC, Z, false, M>, grid, 32 * NW, smem, st, P);
 }
-template <typename IT, int NW, bool VB, bool VC>
+template <typename IT, int NW, bool VB, bool VC, bool M>
 static cudaError_t bwd_z(const BwdK& P, dim3 grid, cudaStream_t st, bool tma) {
-  return P.a.f.z != nullptr ? bwd_go<IT, NW, VB, VC, true>(P, grid, st, tma)
-                            : bwd_go<IT, NW, VB, VC, false>(P, grid, st, tma);
+  return P.a.f.z != nullptr ? bwd_go<IT, NW, VB, VC, true, M>(P, grid, st, tma)
+                            : bwd_go<IT, NW, VB, VC, false, M>(P, grid, st, tma);
 }
-template <typename IT, int NW>
+template <typename IT, int NW, bool M>
 static cudaError_t bwd_bc(const BwdK& P, dim3 grid, cudaStream_t st, bool tma) {
   const bool vb = P.a.f.var_B != 0, vc = P.a.f.var_C != 0;
-  if (vb && vc) return bwd_z<IT, NW, true, true>(P, grid, st, tma);
-  if (vb) return bwd_z<IT, NW, true, false>(P, grid, st, tma);
-  if (vc) return bwd_z<IT, NW, false, true>(P, grid, st, tma);
-  return bwd_z<IT, NW, false, false>(P, grid, st, tma);
+  if (vb && vc) return bwd_z<IT, NW, true, true, M>(P, grid, st, tma);
+  if (vb) return bwd_z<IT, NW, true, false, M>(P, grid, st, tma);
+  if (vc) return bwd_z<IT, NW, false, true, M>(P, grid, st, tma);
+  return bwd_z<IT, NW, false, false, M>(P, grid, st, tma);
 }
 template <typename IT>
 cudaError_t launch_bwd(const BwdK& P, cudaStream_t st, bool tma) {
-  dim3 grid(P.a.f.ngroups * P.tpg, P.a.f.batch);
-  switch (warps_for(P.a.f.dstate)) {
-    case 1: return bwd_bc<IT, 1>(P, grid, st, tma);
-    case 2: return bwd_bc<IT, 2>(P, grid, st, tma);
-    default: return bwd_bc<IT, 4>(P, grid, st, tma);
+  const ss_fwd_args& f = P.a.f;
+  dim3 grid((unsigned)((int64_t)f.batch * P.nsg * P.nct));  // sizes checked on the host
+  if (P.nsg > 1) {
+    cudaError_t e =
+        cudaMemsetAsync(f.work, 0, 2 * (size_t)f.batch * f.dim * (size_t)f.seqlen * sizeof(float), st);
+    if (e != cudaSuccess) return e;
+    e = bwd_bc<IT, 4, true>(P, grid, st, tma);
+    if (e != cudaSuccess) return e;
+    const int nlc = (f.seqlen + 255) / 256;
+    bwd_finish_kernel<IT><<<(unsigned)((int64_t)f.batch * f.dim * nlc), 256, 0, st>>>(P.a, nlc);
+    return cudaGetLastError();
+  }
+  switch (warps_for(f.dstate)) {
+    case 1: return bwd_bc<IT, 1, false>(P, grid, st, tma);
+    case 2: return bwd_bc<IT, 2, false>(P, grid, st, tma);
+    default: return bwd_bc<IT, 4, false>(P, grid, st, tma);
   }
 }
 
+// ---- decode step
+template <typename IT, int TPC, int R>
+static cudaError_t step_go(const ss_step_args& a, cudaStream_t st) {
+  constexpr int CPB = 128 / TPC;
+  const int nblk = (a.dim + CPB - 1) / CPB;
+  ss_step_kernel<IT, TPC, R><<<(unsigned)((int64_t)a.batch * nblk), 128, 0, st>>>(a, nblk);
+  return cudaGetLastError();
+}
 template <typename IT>
 cudaError_t launch_step(const ss_step_args& a, cudaStream_t st) {
-  const int tpc = warps_for(a.dstate);  // threads per channel = ceil(dstate / 4), as 1/2/4
-  const int cpb = 128 / tpc;
-  dim3 grid((a.dim + cpb - 1) / cpb, a.batch);
-  if (tpc == 1) ss_step_kernel<IT, 1><<<grid, 128, 0, st>>>(a);
-  else if (tpc == 2) ss_step_kernel<IT, 2><<<grid, 128, 0, st>>>(a);
-  else ss_step_kernel<IT, 4><<<grid, 128, 0, st>>>(a);
-  return cudaGetLastError();
+  int tpc, chunks;
+  step_shape(a.dstate, tpc, chunks);
+  switch (tpc) {
+    case 1: return step_go<IT, 1, 1>(a, st);
+    case 2: return step_go<IT, 2, 1>(a, st);
+    case 4: return step_go<IT, 4, 1>(a, st);
+    case 8: return step_go<IT, 8, 1>(a, st);
+    case 16: return step_go<IT, 16, 1>(a, st);
+    default: return chunks == 1 ? step_go<IT, 32, 1>(a, st) : step_go<IT, 32, 2>(a, st);
+  }
 }
 
 }  // namespace ssb

@@ -11,42 +11,46 @@ namespace {
 
 using namespace ssb;
 
-template <typename IT, int K, int TPC, int CL>
+template <typename IT, int K, int TPC, int R, int CL>
 cudaError_t launch_mix(const MixK& P, cudaStream_t st) {
   const size_t smem = sizeof(float) * ((size_t)P.cs + 2 * (size_t)P.J);
-  auto kern = mamba_step_kernel<IT, K, TPC, CL>;
+  auto kern = mamba_step_kernel<IT, K, TPC, R, CL>;
   if (smem > 48 * 1024) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
   }
-  kern<<<dim3(P.a.batch * CL), kMixThreads, smem, st>>>(P);
+  kern<<<dim3((unsigned)((int64_t)P.a.batch * CL)), kMixThreads, smem, st>>>(P);
   return cudaGetLastError();
 }
 
-template <typename IT, int K, int TPC>
+template <typename IT, int K, int TPC, int R>
 cudaError_t by_cluster(int cl, const MixK& P, cudaStream_t st) {
   switch (cl) {
-    case 1: return launch_mix<IT, K, TPC, 1>(P, st);
-    case 2: return launch_mix<IT, K, TPC, 2>(P, st);
-    case 4: return launch_mix<IT, K, TPC, 4>(P, st);
-    default: return launch_mix<IT, K, TPC, 8>(P, st);
+    case 1: return launch_mix<IT, K, TPC, R, 1>(P, st);
+    case 2: return launch_mix<IT, K, TPC, R, 2>(P, st);
+    case 4: return launch_mix<IT, K, TPC, R, 4>(P, st);
+    default: return launch_mix<IT, K, TPC, R, 8>(P, st);
   }
 }
 
+// lanes per channel in the SSM phase: 1, 2, 4 for dstate <= 4, 8, 16; 32 lanes with one or
+// two 128-state chunks above
 template <typename IT, int K>
-cudaError_t by_tpc(int tpc, int cl, const MixK& P, cudaStream_t st) {
-  if (tpc == 1) return by_cluster<IT, K, 1>(cl, P, st);
-  if (tpc == 2) return by_cluster<IT, K, 2>(cl, P, st);
-  return by_cluster<IT, K, 4>(cl, P, st);
+cudaError_t by_tpc(int dstate, int cl, const MixK& P, cudaStream_t st) {
+  if (dstate <= 4) return by_cluster<IT, K, 1, 1>(cl, P, st);
+  if (dstate <= 8) return by_cluster<IT, K, 2, 1>(cl, P, st);
+  if (dstate <= 16) return by_cluster<IT, K, 4, 1>(cl, P, st);
+  if (dstate <= 128) return by_cluster<IT, K, 32, 1>(cl, P, st);
+  return by_cluster<IT, K, 32, 2>(cl, P, st);
 }
 
 template <typename IT>
-cudaError_t by_width(int K, int tpc, int cl, const MixK& P, cudaStream_t st) {
+cudaError_t by_width(int K, int dstate, int cl, const MixK& P, cudaStream_t st) {
   switch (K) {
-    case 1: return by_tpc<IT, 1>(tpc, cl, P, st);
-    case 2: return by_tpc<IT, 2>(tpc, cl, P, st);
-    case 3: return by_tpc<IT, 3>(tpc, cl, P, st);
-    default: return by_tpc<IT, 4>(tpc, cl, P, st);
+    case 1: return by_tpc<IT, 1>(dstate, cl, P, st);
+    case 2: return by_tpc<IT, 2>(dstate, cl, P, st);
+    case 3: return by_tpc<IT, 3>(dstate, cl, P, st);
+    default: return by_tpc<IT, 4>(dstate, cl, P, st);
   }
 }
 
@@ -57,7 +61,8 @@ extern "C" {
 int ss_mamba_step(const ss_mamba_step_args* a, void* stream) {
   if (a == nullptr) return SS_ERR_INVALID;
   if (a->batch < 0 || a->dim < 1 || a->dstate < 1 || a->width < 1 || a->dt_rank < 1) return SS_ERR_INVALID;
-  if (a->dstate > SS_MAX_DSTATE || a->width > SS_MAX_CONV_WIDTH || a->batch > 65535) return SS_ERR_UNSUPPORTED;
+  if (a->dstate > SS_MAX_DSTATE || a->width > SS_MAX_CONV_WIDTH || (int64_t)a->batch * 8 > 2147483647LL)
+    return SS_ERR_UNSUPPORTED;
   if (a->io_dtype != SS_F32 && a->io_dtype != SS_BF16 && a->io_dtype != SS_F16) return SS_ERR_UNSUPPORTED;
   const int J = a->dt_rank + 2 * a->dstate;
   if (J > 4096) return SS_ERR_UNSUPPORTED;
@@ -82,12 +87,11 @@ int ss_mamba_step(const ss_mamba_step_args* a, void* stream) {
   P.vec_a = a->dstate % 4 == 0 && (reinterpret_cast<uintptr_t>(a->A) & 15) == 0 &&
             (reinterpret_cast<uintptr_t>(a->ssm_state) & 15) == 0;
   if (sizeof(float) * ((size_t)P.cs + 2 * (size_t)J) > 200 * 1024) return SS_ERR_UNSUPPORTED;
-  const int tpc = a->dstate <= 4 ? 1 : (a->dstate <= 8 ? 2 : 4);
   cudaStream_t st = (cudaStream_t)stream;
   switch (a->io_dtype) {
-    case SS_F32: return record_cuda_status(by_width<float>(a->width, tpc, cl, P, st));
-    case SS_BF16: return record_cuda_status(by_width<__nv_bfloat16>(a->width, tpc, cl, P, st));
-    default: return record_cuda_status(by_width<__half>(a->width, tpc, cl, P, st));
+    case SS_F32: return record_cuda_status(by_width<float>(a->width, a->dstate, cl, P, st));
+    case SS_BF16: return record_cuda_status(by_width<__nv_bfloat16>(a->width, a->dstate, cl, P, st));
+    default: return record_cuda_status(by_width<__half>(a->width, a->dstate, cl, P, st));
   }
 }
 

@@ -3,14 +3,14 @@
 //
 //   x, z   = the two halves of xz[b]                      (modules/mamba_simple.py:93-97)
 //   u      = silu(conv_bias + conv_w . [conv_state, x])   (:97-98; the state then rolls)
-//   dbl    = x_proj . u  -> dt_in (R), B (N), C (N)        (:100-111)
+//   dbl    = x_proj . u  -> dt_in (dt_rank), B (N), C (N)  (:100-111)
 //   dt     = softplus(dt_proj . dt_in + dt_bias)          (:114, forward_kernel.cu:216-221)
 //   state  = exp(dt A) state + dt u B;  y = (C . state + D u) * silu(z)
 //
 // which otherwise takes a conv-step kernel, an x-projection GEMM and the SSM-step kernel.
 // A thread-block cluster of CL CTAs serves one sequence (batch row); CTA r owns channels
 // [r * cs, (r + 1) * cs): it runs their conv step (so each conv-state entry has one owner),
-// forms its partial x projection over them, and the CL partial vectors (R + 2N floats each)
+// forms its partial x projection over them, and the CL partial vectors (dt_rank + 2N floats each)
 // are summed through distributed shared memory between two cluster barriers that every
 // thread reaches (no early exit).  Each CTA then updates the SSM state of its channels.
 // The x projection reads its weight rows once per CTA (from L2); the state traffic is the
@@ -38,7 +38,9 @@ __device__ __forceinline__ float mix_warp_sum(float v) {
   return v;
 }
 
-template <typename IT, int K, int TPC, int CL>
+// TPC lanes per channel in the SSM phase, each holding R chunks of 4 states (state
+// n = 4 (q + TPC r) + j): TPC = 1, 2, 4 for dstate <= 16, TPC = 32 with R = 1 or 2 above.
+template <typename IT, int K, int TPC, int R, int CL>
 __global__ void __cluster_dims__(CL, 1, 1) __launch_bounds__(kMixThreads)
     mamba_step_kernel(const __grid_constant__ MixK P) {
   namespace cg = cooperative_groups;
@@ -47,7 +49,7 @@ __global__ void __cluster_dims__(CL, 1, 1) __launch_bounds__(kMixThreads)
   const int rank = (int)cluster.block_rank();
   const int b = blockIdx.x / CL;
   const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
-  const int d = a.dim, N = a.dstate, R = a.dt_rank, J = P.J, cs = P.cs;
+  const int d = a.dim, N = a.dstate, J = P.J, cs = P.cs;
   const int c_begin = rank * cs, c_end = min(d, c_begin + cs);
   extern __shared__ __align__(16) float mix_smem[];
   float* u_s = mix_smem;       // [cs]  this CTA's u (rounded to the I/O dtype, as a stored activation)
@@ -120,9 +122,10 @@ __global__ void __cluster_dims__(CL, 1, 1) __launch_bounds__(kMixThreads)
   }
   cluster.sync();  // the remote reads are done (CTAs may exit after this) and dbl is visible
 
-  // 3. SSM step of this CTA's channels: TPC lanes per channel, 4 states per lane
-  const float* Bv = dbl + R;
-  const float* Cv = dbl + R + N;
+  // 3. SSM step of this CTA's channels: TPC lanes per channel, R chunks of 4 states per lane
+  const int DR = a.dt_rank;
+  const float* Bv = dbl + DR;
+  const float* Cv = dbl + DR + N;
   const int q = tid % TPC;
   for (int base = c_begin; base < c_end; base += kMixThreads / TPC) {
     const int c = base + tid / TPC;
@@ -131,29 +134,33 @@ __global__ void __cluster_dims__(CL, 1, 1) __launch_bounds__(kMixThreads)
     // the state and A loads do not depend on dt: issue them first
     float* st = a.ssm_state + ((int64_t)b * d + cc) * N;
     const bool vec = P.vec_a != 0;
-    float s[kSPW], av[kSPW];
-    if (vec && 4 * q < N) {
-      const float4 v = *reinterpret_cast<const float4*>(st + 4 * q);
-      const float4 w = *reinterpret_cast<const float4*>(a.A + (int64_t)cc * N + 4 * q);
-      s[0] = v.x; s[1] = v.y; s[2] = v.z; s[3] = v.w;
-      av[0] = w.x; av[1] = w.y; av[2] = w.z; av[3] = w.w;
-    } else {
+    float s[R][kSPW], av[R][kSPW];
 #pragma unroll
-      for (int j = 0; j < kSPW; ++j) {
-        s[j] = (4 * q + j < N) ? st[4 * q + j] : 0.f;
-        av[j] = (4 * q + j < N) ? a.A[(int64_t)cc * N + 4 * q + j] : 0.f;
+    for (int rr = 0; rr < R; ++rr) {
+      const int nb = 4 * (q + TPC * rr);
+      if (vec && nb < N) {
+        const float4 v = *reinterpret_cast<const float4*>(st + nb);
+        const float4 w = *reinterpret_cast<const float4*>(a.A + (int64_t)cc * N + nb);
+        s[rr][0] = v.x; s[rr][1] = v.y; s[rr][2] = v.z; s[rr][3] = v.w;
+        av[rr][0] = w.x; av[rr][1] = w.y; av[rr][2] = w.z; av[rr][3] = w.w;
+      } else {
+#pragma unroll
+        for (int j = 0; j < kSPW; ++j) {
+          s[rr][j] = (nb + j < N) ? st[nb + j] : 0.f;
+          av[rr][j] = (nb + j < N) ? a.A[(int64_t)cc * N + nb + j] : 0.f;
+        }
       }
     }
-    // delta projection: the channel's TPC lanes split the R-long dot product
-    const IT* wrow = (const IT*)a.dt_proj + (int64_t)cc * R;
+    // delta projection: the channel's TPC lanes split the dt_rank-long dot product
+    const IT* wrow = (const IT*)a.dt_proj + (int64_t)cc * DR;
     float dv = 0.f, d1 = 0.f;
     int r = q;
 #pragma unroll 4
-    for (; r + TPC < R; r += 2 * TPC) {
+    for (; r + TPC < DR; r += 2 * TPC) {
       dv = fmaf(dbl[r], to_f<IT>(wrow[r]), dv);
       d1 = fmaf(dbl[r + TPC], to_f<IT>(wrow[r + TPC]), d1);
     }
-    if (r < R) dv = fmaf(dbl[r], to_f<IT>(wrow[r]), dv);
+    if (r < DR) dv = fmaf(dbl[r], to_f<IT>(wrow[r]), dv);
     dv += d1;
 #pragma unroll
     for (int o = 1; o < TPC; o <<= 1) dv += __shfl_xor_sync(0xffffffffu, dv, o);
@@ -163,19 +170,23 @@ __global__ void __cluster_dims__(CL, 1, 1) __launch_bounds__(kMixThreads)
     float y = 0.f;
     if (ok) {
 #pragma unroll
-      for (int j = 0; j < kSPW; ++j) {
-        const int n = 4 * q + j;
-        if (n < N) {
-          s[j] = fmaf(exp_fast(dt * av[j]), s[j], dt * uv * Bv[n]);
-          y = fmaf(Cv[n], s[j], y);
-        }
-      }
-      if (vec && 4 * q < N) {
-        *reinterpret_cast<float4*>(st + 4 * q) = make_float4(s[0], s[1], s[2], s[3]);
-      } else {
+      for (int rr = 0; rr < R; ++rr) {
+        const int nb = 4 * (q + TPC * rr);
 #pragma unroll
-        for (int j = 0; j < kSPW; ++j)
-          if (4 * q + j < N) st[4 * q + j] = s[j];
+        for (int j = 0; j < kSPW; ++j) {
+          const int n = nb + j;
+          if (n < N) {
+            s[rr][j] = fmaf(exp_fast(dt * av[rr][j]), s[rr][j], dt * uv * Bv[n]);
+            y = fmaf(Cv[n], s[rr][j], y);
+          }
+        }
+        if (vec && nb < N) {
+          *reinterpret_cast<float4*>(st + nb) = make_float4(s[rr][0], s[rr][1], s[rr][2], s[rr][3]);
+        } else {
+#pragma unroll
+          for (int j = 0; j < kSPW; ++j)
+            if (nb + j < N) st[nb + j] = s[rr][j];
+        }
       }
     }
 #pragma unroll

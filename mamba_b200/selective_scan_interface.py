@@ -102,7 +102,12 @@ class _Prepared:
         self.b, self.d, self.l, self.n = b, d, l, n
         self.io = io
 
-    def fwd_args(self, out, ckpt=None, last=None, out_y=None):
+    def work(self):
+        """fp32 scratch of the native call (dstate > 16: the state groups' partial sums), or None."""
+        n = L.work_elems(self.b, self.d, self.l, self.n)
+        return torch.empty(n, dtype=torch.float32, device=self.device) if n else None
+
+    def fwd_args(self, out, ckpt=None, last=None, out_y=None, work=None):
         u, dl, z = self.u, self.delta, self.z
         return L.FwdArgs(
             self.b, self.d, self.l, self.n, self.ngroups, self.var_B, self.var_C, self.softplus,
@@ -115,7 +120,7 @@ class _Prepared:
             out.data_ptr(), out.stride(0), out.stride(1),
             L.ptr(ckpt), L.ptr(last),
             L.ptr(out_y), out_y.stride(0) if out_y is not None else 0,
-            out_y.stride(1) if out_y is not None else 0)
+            out_y.stride(1) if out_y is not None else 0, L.ptr(work))
 
 
 def _new_ckpt(p: _Prepared):
@@ -130,7 +135,8 @@ def scan_forward(p: _Prepared, want_ckpt: bool, want_last: bool):
     ckpt = _new_ckpt(p) if want_ckpt else None
     y = torch.empty_like(out) if (want_ckpt and p.z is not None) else None
     last = torch.empty((p.b, p.d, p.n), dtype=torch.float32, device=p.device) if want_last else None
-    args = p.fwd_args(out, ckpt, last, y)
+    work = p.work()
+    args = p.fwd_args(out, ckpt, last, y, work)
     with torch.cuda.device(p.device):
         L.check(L.lib().ss_fwd(args, L.stream_of(p.device)), "ss_fwd")
     return out, ckpt, last, y
@@ -155,8 +161,9 @@ def scan_backward(p: _Prepared, dout, ckpt, y=None):
     dD = torch.empty(p.d, dtype=torch.float32, device=dev) if p.D is not None else None
     dbias = torch.empty(p.d, dtype=torch.float32, device=dev) if p.delta_bias is not None else None
     placeholder = du  # stands in for the unused output row pointer of the embedded forward args
+    work = p.work()  # held until the launch below is queued
     args = L.BwdArgs(
-        p.fwd_args(placeholder, ckpt, None),
+        p.fwd_args(placeholder, ckpt, None, None, work),
         dout.data_ptr(), dout.stride(0), dout.stride(1),
         du.data_ptr(), du.stride(0), du.stride(1),
         ddelta.data_ptr(), ddelta.stride(0), ddelta.stride(1),

@@ -18,7 +18,7 @@ The final state is read from the reference's chunk carry x (the second float of 
 1/B (forward_kernel.cu:265), so no state is stored for those cases.
 
 Run on a GPU box (the committed .npz files are its output):
-    python tests/golden/make_golden.py --out tests/golden
+    python tests/golden/make_golden.py --out tests/golden [--cases name,name]
 """
 from __future__ import annotations
 
@@ -44,6 +44,11 @@ CASES = [
     ("constBC", 2, 8, 64, 16, 2, 2, 1, True, True, True, "s4d"),
     ("single_step", 1, 4, 1, 16, 4, 4, 1, True, True, True, "s4d"),
     ("long_l600", 2, 8, 600, 16, 4, 4, 1, True, True, True, "s4d"),
+    # dstate above 16 (the reference dispatches up to 256, static_switch.h:15-35)
+    ("n32_ragged", 2, 16, 200, 32, 4, 4, 1, True, True, True, "rand"),
+    ("n64_g2_constC", 1, 16, 150, 64, 4, 2, 2, True, True, True, "rand"),
+    ("n128_constB", 1, 8, 100, 128, 2, 4, 1, True, True, True, "s4d"),
+    ("n256", 1, 8, 64, 256, 4, 4, 1, True, True, True, "rand"),
 ]
 
 
@@ -84,10 +89,14 @@ def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--out", default=HERE)
     ap.add_argument("--ref", default=os.path.join(ROOT, "oracle", "_ref", "selective_scan.so"))
+    ap.add_argument("--cases", default="", help="comma-separated case names (default: all)")
     a = ap.parse_args()
+    only = set(filter(None, a.cases.split(",")))
     ref = load_reference_module(a.ref)
     os.makedirs(a.out, exist_ok=True)
     for i, (name, b, d, L, n, bk, ck, g, hD, hb, sp, ak) in enumerate(CASES):
+        if only and name not in only:
+            continue
         inp = make_inputs(1000 + i, b, d, L, n, bk, ck, g, hD, hb, sp, ak)
         cu = {k: (v.cuda() if v is not None else None) for k, v in inp.items()}
         out, x = ref.forward(cu["u"], cu["delta"], cu["A"], cu["B"], cu["C"], cu["D"], cu["delta_bias"], sp)

@@ -33,7 +33,7 @@ def test_library_exports_every_declared_symbol():
 
 def test_abi_version_and_struct_layout():
     lib = L.lib()
-    assert lib.ss_abi_version() == 6
+    assert lib.ss_abi_version() == 7
     for i, st in enumerate(L.STRUCTS):
         assert lib.ss_struct_size(i) == ctypes.sizeof(st)
     assert lib.ss_struct_size(len(L.STRUCTS)) == 0
@@ -43,6 +43,14 @@ def test_ckpt_elems():
     assert L.ckpt_elems(2, 64, 33, 16) == 2 * 3 * 16 * 64
     assert L.ckpt_elems(8, 1536, 2048, 16) == 8 * 128 * 16 * 1536
     assert L.ckpt_elems(0, 64, 33, 16) == 0
+
+
+def test_work_elems():
+    # scratch exists only for state groups (dstate > 16): two floats per element
+    assert L.work_elems(2, 64, 33, 16) == 0
+    assert L.work_elems(2, 64, 33, 17) == 2 * 2 * 64 * 33
+    assert L.work_elems(2, 64, 33, 256) == 2 * 2 * 64 * 33
+    assert L.work_elems(0, 64, 33, 64) == 0
 
 
 def test_status_strings():
@@ -65,8 +73,10 @@ def _valid_fwd():
     return a
 
 
+# every case is rejected before any device access (the pointers are dummies)
 @pytest.mark.parametrize("field,value,status", [
-    ("dstate", 17, L.SS_ERR_UNSUPPORTED),
+    ("dstate", 257, L.SS_ERR_UNSUPPORTED),     # the reference dispatches up to 256
+    ("dstate", 17, L.SS_ERR_INVALID),          # state groups need the workspace
     ("dstate", 0, L.SS_ERR_INVALID),
     ("ngroups", 3, L.SS_ERR_INVALID),          # 64 % 3 != 0
     ("io_dtype", 7, L.SS_ERR_UNSUPPORTED),
@@ -74,13 +84,21 @@ def _valid_fwd():
     ("u", None, L.SS_ERR_INVALID),
     ("A", None, L.SS_ERR_INVALID),
     ("out", None, L.SS_ERR_INVALID),
-    ("batch", 70000, L.SS_ERR_UNSUPPORTED),
+    ("batch", 2**31 - 1, L.SS_ERR_UNSUPPORTED),  # batch x channel tiles beyond the flattened grid
     ("u_dim_stride", -1, L.SS_ERR_INVALID),
 ])
 def test_fwd_validation(field, value, status):
     a = _valid_fwd()
     setattr(a, field, value)
     assert L.lib().ss_fwd(ctypes.byref(a), None) == status
+
+
+def test_state_groups_need_an_aligned_workspace():
+    a = _valid_fwd()
+    a.dstate = 64
+    assert L.lib().ss_fwd(ctypes.byref(a), None) == L.SS_ERR_INVALID  # no workspace
+    a.work = 0x1004
+    assert L.lib().ss_fwd(ctypes.byref(a), None) == L.SS_ERR_INVALID  # not 16-byte aligned
 
 
 def test_bwd_validation():
@@ -106,7 +124,7 @@ def test_step_validation():
     s.batch, s.dim, s.dstate, s.ngroups = 2, 64, 16, 1
     s.io_dtype = s.bc_dtype = L.SS_F32
     assert lib.ss_step(ctypes.byref(s), None) == L.SS_ERR_INVALID
-    s.dstate = 40
+    s.dstate = 257
     assert lib.ss_step(ctypes.byref(s), None) == L.SS_ERR_UNSUPPORTED
     assert lib.ss_step(None, None) == L.SS_ERR_INVALID
 
@@ -142,7 +160,7 @@ def _valid_conv():
     ("u", None, L.SS_ERR_INVALID),
     ("z", 0x2000, L.SS_ERR_INVALID),       # z without zt
     ("x_seq_stride", -1, L.SS_ERR_INVALID),
-    ("batch", 70000, L.SS_ERR_UNSUPPORTED),
+    ("batch", 2**31 - 1, L.SS_ERR_UNSUPPORTED),  # beyond the flattened grid
 ])
 def test_conv_validation(field, value, status):
     a = _valid_conv()
@@ -197,7 +215,7 @@ def test_mamba_step_validation():
     a.xz_batch_stride, a.y_batch_stride = 100, 64
     assert lib.ss_mamba_step(ctypes.byref(a), None) == L.SS_ERR_INVALID      # xz rows shorter than 2 dim
     a.xz_batch_stride = 128
-    a.dstate = 17
+    a.dstate = 257
     assert lib.ss_mamba_step(ctypes.byref(a), None) == L.SS_ERR_UNSUPPORTED
     a.dstate, a.width = 16, 5
     assert lib.ss_mamba_step(ctypes.byref(a), None) == L.SS_ERR_UNSUPPORTED

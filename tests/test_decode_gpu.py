@@ -46,6 +46,25 @@ def test_block_prefill_then_steps_match_full_forward(dtype):
         assert_close(f"step {t}", y, full[:, t], rtol, max(atol, rtol * scale))
 
 
+def test_block_prefill_then_steps_large_dstate():
+    """state_dim 48: the prefill scans in state groups, the mixer step runs 32 lanes per channel."""
+    from mamba_b200 import mamba_simple_forward
+    from mamba_b200.decode import mamba_simple_prefill, mamba_simple_step
+
+    blk = _block(torch.float32, N=48)
+    b, L0, T = 2, 33, 6
+    h = torch.randn(b, L0 + T, 64, generator=torch.Generator().manual_seed(2)).cuda()
+    with torch.no_grad():
+        full = mamba_simple_forward(blk, h)
+    y0, conv_state, ssm_state = mamba_simple_prefill(blk, h[:, :L0])
+    scale = float(full.abs().max())
+    assert_close("prefill", y0, full[:, :L0], 1e-4, 1e-4 * scale)
+    assert ssm_state.shape == (b, 128, 48)
+    for t in range(L0, L0 + T):
+        y = mamba_simple_step(blk, h[:, t].contiguous(), conv_state, ssm_state)
+        assert_close(f"step {t}", y, full[:, t], 1e-4, 1e-4 * scale)
+
+
 def _model(dtype, seed=3):
     torch.manual_seed(seed)
     m = CausalLMRef(vocab_size=97, model_dim=32, state_dim=16, num_layers=3)
@@ -120,7 +139,8 @@ def test_sampled_generate_is_reproducible():
 
 
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16, torch.float16])
-@pytest.mark.parametrize("batch,dm,N", [(3, 64, 16), (64, 32, 16), (1, 48, 8), (5, 40, 4)])
+@pytest.mark.parametrize("batch,dm,N", [(3, 64, 16), (64, 32, 16), (1, 48, 8), (5, 40, 4),
+                                        (4, 64, 32), (2, 32, 200)])
 def test_fused_mixer_step_matches_separate_kernels(dtype, batch, dm, N):
     """ss_mamba_step against the composition it replaces: the conv-step kernel, the x projection
     as a GEMM, and the SSM-step kernel (with its fused delta projection) — several tokens in a

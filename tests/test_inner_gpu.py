@@ -130,6 +130,31 @@ def test_mamba_inner_fn_matches_block_reference(dtype, L, conv_bias, bias):
         assert_close(name, p.grad, q.grad, rtol, max(atol, rtol * float(q.grad.abs().max())))
 
 
+@pytest.mark.parametrize("dtype,N", [(torch.float32, 32), (torch.bfloat16, 64)])
+def test_mamba_inner_fn_large_dstate(dtype, N):
+    """A block with state_dim above 16 (the reference's kernels take up to 256): the scan runs in
+    state groups; outputs and every gradient against the float64 restatement."""
+    from mamba_b200.inner import mamba_simple_forward
+
+    blk = _block(dtype, N=N)
+    ref = _block(torch.float64, N=N)
+    ref.load_state_dict({k: v.double() for k, v in blk.state_dict().items()})
+    g = torch.Generator().manual_seed(6)
+    h = torch.randn(2, 70, 64, generator=g).to(dtype).cuda()
+    dy = torch.randn(2, 70, 64, generator=g).to(dtype).cuda()
+    h1 = h.clone().requires_grad_()
+    y = mamba_simple_forward(blk, h1)
+    y.backward(dy)
+    h2 = h.double().requires_grad_()
+    y_ref = ref(h2)
+    y_ref.backward(dy.double())
+    rtol, atol = TOL[dtype]
+    assert_close("out", y, y_ref, rtol, max(atol, rtol * float(y_ref.detach().abs().max())))
+    assert_close("d hidden", h1.grad, h2.grad, rtol, max(atol, rtol * float(h2.grad.abs().max())))
+    for (name, p), q in zip(blk.named_parameters(), ref.parameters()):
+        assert_close(name, p.grad, q.grad, rtol, max(atol, rtol * float(q.grad.abs().max())))
+
+
 def test_mamba_inner_fn_without_gradients_and_errors():
     from mamba_b200.inner import mamba_inner_fn, mamba_simple_forward
 

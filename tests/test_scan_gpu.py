@@ -90,6 +90,20 @@ CASES = {
     "bf16_base": (2, 64, 512, 16, dict(dtype=torch.bfloat16, has_z=True)),
     "bf16_bcf32": (2, 64, 130, 16, dict(dtype=torch.bfloat16, bc_f32=True)),
     "f16_base": (2, 32, 160, 16, dict(dtype=torch.float16, has_z=True)),
+    # dstate > 16 (the reference dispatches up to 256): state groups of 16 per CTA, partial sums
+    # over the groups in the workspace, then the finishing pass
+    "f32_n17_partial_group": (2, 64, 100, 17, dict(has_z=True)),
+    "f32_n32_groups3": (2, 96, 150, 32, dict(groups=3, akind="rand")),
+    "f32_n64_constB": (1, 32, 64, 64, dict(bc=("const", "var4"), has_z=True)),
+    "f32_n48_constC": (2, 32, 50, 48, dict(bc=("var4", "const"))),
+    "f32_n40_constBC": (1, 32, 33, 40, dict(bc="const", has_z=True)),
+    "f32_n24_noD_nobias_nosp": (2, 32, 70, 24, dict(has_D=False, has_bias=False, softplus=False)),
+    "f32_n32_var3_L15_dim33": (2, 33, 15, 32, dict(bc="var3")),
+    "f32_n128": (1, 32, 48, 128, dict(akind="rand")),
+    "f32_n256_z": (1, 32, 40, 256, dict(has_z=True, akind="rand")),
+    "bf16_n64": (2, 64, 300, 64, dict(dtype=torch.bfloat16, has_z=True)),
+    "bf16_n32_bcf32": (2, 64, 90, 32, dict(dtype=torch.bfloat16, bc_f32=True, has_z=True)),
+    "f16_n48_L77": (2, 32, 77, 48, dict(dtype=torch.float16, has_z=True)),
 }
 
 
@@ -232,3 +246,26 @@ def test_config4_full_size_fwd_bwd():
     got_rows = {k: full[k][rows] for k in ("out", "last_state", "du", "ddelta", "dz", "dB", "dC")}
     compare(got_rows, want, torch.bfloat16, keys=("out", "last_state", "du", "ddelta", "dz", "dB", "dC"))
     compare(sub, want, torch.bfloat16, keys=("dA", "dD", "ddelta_bias"))
+
+
+def test_batch_beyond_65535():
+    """The grids are flattened, so a batch larger than gridDim.y's 65535 runs (the reference puts
+    batch on gridDim.x and accepts it).  Rows are independent: a spread of rows is checked
+    against the oracle, forward and backward, plus the summed gradients over all rows by
+    linearity (two halves)."""
+    import mamba_b200
+
+    b, d, L, n = 70000, 32, 5, 4
+    inp = make_inputs(b, d, L, n, has_z=True, seed=12)
+    got = run_case(inp)
+    rows = [0, 1, 65535, 65536, b - 1]
+    sub = {k: (v[rows] if isinstance(v, torch.Tensor) and k in ("u", "delta", "z", "B", "C", "dout") else v)
+           for k, v in inp.items()}
+    want = oracle_case(sub)
+    got_rows = {k: got[k][rows] for k in ("out", "last_state", "du", "ddelta", "dz", "dB", "dC")}
+    compare(got_rows, want, torch.float32, keys=("out", "last_state", "du", "ddelta", "dz", "dB", "dC"))
+    halves = [run_case({k: (v[sl] if isinstance(v, torch.Tensor) and k in ("u", "delta", "z", "B", "C", "dout")
+                            else v) for k, v in inp.items()}) for sl in (slice(0, b // 2), slice(b // 2, b))]
+    for k in ("dA", "dD", "ddelta_bias"):
+        tot = halves[0][k] + halves[1][k]
+        assert_close(k, got[k], tot, 1e-4, 1e-4 * float(tot.abs().max()))

@@ -21,6 +21,13 @@ pytestmark = pytest.mark.gpu
     (torch.float32, 5, 1, True, False),
     (torch.bfloat16, 16, 1, True, True),
     (torch.float16, 16, 4, True, True),
+    # dstate > 16: 8 / 16 / 32 lanes per channel, two 128-state chunks per lane above 128
+    (torch.float32, 32, 1, True, True),
+    (torch.float32, 50, 2, False, True),
+    (torch.bfloat16, 64, 1, True, True),
+    (torch.float32, 128, 1, True, False),
+    (torch.float32, 200, 1, True, True),
+    (torch.float16, 256, 4, True, True),
 ])
 def test_step_matches_oracle(dtype, n, groups, has_z, has_D):
     import mamba_b200
@@ -96,3 +103,23 @@ def test_step_fused_dt_projection_and_strided_bc(dtype, n, rank):
     rtol, atol = TOL[dtype]
     assert_close("state", s2, s1, rtol, atol)
     assert_close("out", y2, y1, rtol, atol)
+
+
+def test_step_batch_beyond_65535():
+    """The step grid is flattened over (batch row, channel block): a batch above 65535 runs."""
+    import mamba_b200
+
+    b, d, n = 70000, 32, 8
+    g = torch.Generator().manual_seed(9)
+    state = torch.randn(b, d, n, generator=g)
+    x, dt, z = (torch.randn(b, d, generator=g) for _ in range(3))
+    A = -torch.exp(0.5 * torch.randn(d, n, generator=g))
+    B, C = torch.randn(b, 1, n, generator=g), torch.randn(b, 1, n, generator=g)
+    rows = [0, 65535, 65536, b - 1]
+    st_ref, out_ref = O.selective_state_update_ref(state[rows].numpy().copy(), x[rows], dt[rows], A, B[rows],
+                                                   C[rows], None, z[rows], None, True)
+    st = state.cuda()
+    out = mamba_b200.selective_state_update(st, x.cuda(), dt.cuda(), A.cuda(), B.cuda(), C.cuda(), None, z.cuda(),
+                                            None, dt_softplus=True)
+    assert_close("out", out[rows], out_ref, 1e-4, 1e-5)
+    assert_close("state", st[rows], st_ref, 1e-4, 1e-5)
