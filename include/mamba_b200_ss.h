@@ -265,7 +265,8 @@ SS_API int ss_bwd(const ss_bwd_args* args, void* stream);
  * device looks up that array's address (do it before any stream capture).  All calls on a
  * device share the array: calls that overlap on the GPU race.  du (and dz, with a gate)
  * receive the recomputed forward outputs before the backward overwrites them, so they must
- * not alias an input; args->y is ignored. */
+ * not alias an input; args->y is ignored.  With dstate > 16 the caller's args->f.work
+ * (ss_work_elems floats) is required, as for ss_bwd. */
 SS_API int ss_bwd_noalloc(const ss_bwd_args* args, void* stream);
 
 /* One decode step: state <- exp(dt'*A) state + dt'*x*B; out = (C.state + D x) [* silu(z)],
