@@ -269,3 +269,42 @@ def test_batch_beyond_65535():
     for k in ("dA", "dD", "ddelta_bias"):
         tot = halves[0][k] + halves[1][k]
         assert_close(k, got[k], tot, 1e-4, 1e-4 * float(tot.abs().max()))
+
+
+def _sweep_cases(n_cases=40, seed=2024):
+    """Seeded random configurations: shapes (ragged channel tiles, partial time tiles, single
+    steps), state counts across both code paths (<= 16 and state groups up to 256), groups,
+    every B / C kind, optional gate / D / bias / softplus, all I/O dtypes."""
+    import random
+
+    rng = random.Random(seed)
+    cases = []
+    for i in range(n_cases):
+        n = rng.choice([1, 3, 4, 7, 8, 12, 16, 17, 20, 33, 64, 100, 256])
+        groups = rng.choice([1, 1, 2, 3])
+        d = groups * rng.choice([8, 17, 32, 40, 64])
+        L = rng.choice([1, 5, 16, 31, 64, 97, 130])
+        b = rng.choice([1, 2, 3])
+        dtype = rng.choice([torch.float32, torch.float32, torch.bfloat16, torch.float16])
+        bc = rng.choice(["var4", "var4", "var3", "const", ("const", "var4"), ("var4", "const")])
+        if bc == "var3":
+            groups = 1
+        softplus = rng.random() < 0.8
+        # without softplus the step is delta + bias itself; the configs' bias (an inverse softplus
+        # of a small dt) is negative, which would make exp(delta' A) grow without bound
+        kw = dict(dtype=dtype, bc=bc, groups=groups, has_D=rng.random() < 0.8, has_z=rng.random() < 0.6,
+                  has_bias=softplus and rng.random() < 0.8, softplus=softplus,
+                  akind=rng.choice(["s4d", "rand"]), bc_f32=dtype != torch.float32 and rng.random() < 0.3)
+        cases.append((f"sweep{i}_b{b}_d{d}_L{L}_n{n}", b, d, L, n, kw))
+    return cases
+
+
+SWEEP = _sweep_cases()
+
+
+@pytest.mark.parametrize("name,b,d,L,n,kw", SWEEP, ids=[c[0] for c in SWEEP])
+def test_random_config_sweep(name, b, d, L, n, kw):
+    inp = make_inputs(b, d, L, n, seed=zlib.crc32(name.encode()) % 1000, **kw)
+    got = run_case(inp)
+    want = oracle_case(inp)
+    compare(got, want, inp["u"].dtype)
