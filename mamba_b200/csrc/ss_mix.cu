@@ -78,7 +78,7 @@ int ss_mamba_step(const ss_mamba_step_args* a, void* stream) {
   cudaGetLastError();
   int cl = 1;
   while (cl < 8 && a->batch * cl < 2 * sms && (a->dim + 2 * cl - 1) / (2 * cl) >= 32) cl *= 2;
-  MixK P;
+  MixK P{};  // every field is set below; value-initialised so none is ever read uninitialised
   P.a = *a;
   P.J = J;
   P.cs = (((a->dim + cl - 1) / cl) + 31) / 32 * 32;

@@ -57,6 +57,16 @@ def oracle_case(inp, grads=True):
     return want
 
 
+# du and ddelta are, per element, sums over the dstate states (S2 = sum_n B dh, S1 = sum_n A g):
+# where those terms cancel, an fp32 result near zero carries the rounding of terms as large as
+# the tensor's largest values, which a fixed atol cannot express.  Their atol is therefore
+# floored at 1e-2 * rtol * max|ref| (1e-6 of the largest magnitude for fp32 I/O); for tensors
+# of magnitude ~1 that leaves the stated atol.  (Example: a softplus-off, 33-state sweep case
+# whose ddelta reaches 171 — the oracle's own fp32 instantiation already uses 97 % of the plain
+# elementwise tolerance against its fp64 one.)
+STATE_SUMS = ("du", "ddelta")
+
+
 def compare(got, want, dtype, keys=None):
     rtol, atol = TOL[dtype]
     for k, w in want.items():
@@ -67,7 +77,12 @@ def compare(got, want, dtype, keys=None):
         g = got[k]
         if k in ("dB", "dC"):
             g = g.reshape(w.shape)
-        a = max(atol, _sum_atol(w, rtol)) if k in SUMMED else atol
+        if k in SUMMED:
+            a = max(atol, _sum_atol(w, rtol))
+        elif k in STATE_SUMS:
+            a = max(atol, 1e-2 * _sum_atol(w, rtol))
+        else:
+            a = atol
         assert_close(k, g, w, rtol, a)
 
 
