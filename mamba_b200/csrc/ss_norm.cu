@@ -67,7 +67,13 @@ int ss_rmsnorm_fwd(const ss_rmsnorm_args* a, void* stream) {
           aligned_rows(a->residual, a->residual_row_stride, es) && aligned_rows(a->y, a->y_row_stride, es) &&
           aligned_rows(a->residual_out, a->residual_out_row_stride, es);
   cudaStream_t st = (cudaStream_t)stream;
-  dim3 grid((a->rows + kNormWarps - 1) / kNormWarps);
+  // persistent grid: each warp walks rows with a stride of the grid's warps
+  int sms = 148;
+  int dev = 0;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  cudaGetLastError();
+  const int ctas = (a->rows + kNormWarps - 1) / kNormWarps;
+  dim3 grid(ctas < 4 * sms ? ctas : 4 * sms);
   return by_dtype(a->io_dtype, [&](auto tag) {
     using IT = decltype(tag);
     SSB_NORM_LAUNCH(rmsnorm_fwd_kernel)
