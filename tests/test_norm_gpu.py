@@ -58,6 +58,16 @@ def test_rms_norm_forward_backward(dtype, shape, with_res):
     assert_close("dweight", wr.grad, wd.grad, rtol, rtol * float(wd.grad.abs().max()))
 
 
+@pytest.mark.parametrize("dtype,dim", [(torch.bfloat16, 768), (torch.float32, 768), (torch.bfloat16, 2048),
+                                       (torch.float16, 512)])
+def test_rms_norm_many_rows_per_warp(dtype, dim):
+    """More rows than the persistent grid has warps (at most 4 CTAs x 4 warps per SM), and not a
+    multiple of it: each warp walks several rows, with the next row's loads already in flight
+    (rows of up to 4 vectors per lane: bf16 768, fp16 512) or loaded at the top of each row (bf16
+    2048, fp32 768).  Outputs and every gradient against float64, as above."""
+    test_rms_norm_forward_backward(dtype, (7141, dim), True)
+
+
 def test_rms_norm_module_matches_reference_module():
     from mamba_b200.norm import rms_norm
 
