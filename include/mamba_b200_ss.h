@@ -91,7 +91,7 @@ typedef struct ss_fwd_args {
   const float* delta_bias;  /* nullable: bias = 0                                         */
   void* out;         int64_t out_batch_stride, out_dim_stride; /* y or y * silu(z)        */
   float* ckpt;              /* nullable: skip the states the backward needs               */
-  float* last_state;        /* nullable                                                   */
+  float* last_state;        /* nullable; zeros when seqlen == 0 (the zero initial state)  */
   void* out_y;       int64_t out_y_batch_stride, out_y_dim_stride;
                             /* nullable: the ungated y (D*u + C.h), which ss_bwd needs when
                                z is given; written only when z is given                   */

@@ -133,7 +133,10 @@ int check_fwd(const ss_fwd_args* a) {
   }
   if (!dtype_ok(a->io_dtype) || !dtype_ok(a->bc_dtype)) return SS_ERR_UNSUPPORTED;
   if (a->bc_dtype != SS_F32 && a->bc_dtype != a->io_dtype) return SS_ERR_UNSUPPORTED;
-  if (!a->u || !a->delta || !a->A || !a->B || !a->C) return SS_ERR_INVALID;
+  // empty (batch, dim, seqlen) tensors may carry null data pointers; A and constant B / C never are empty
+  const bool empty = a->batch == 0 || a->seqlen == 0;
+  if (!a->A || (!a->var_B && !a->B) || (!a->var_C && !a->C)) return SS_ERR_INVALID;
+  if (!empty && (!a->u || !a->delta || !a->B || !a->C)) return SS_ERR_INVALID;
   if (a->u_batch_stride < 0 || a->u_dim_stride < 0 || a->delta_batch_stride < 0 || a->delta_dim_stride < 0)
     return SS_ERR_INVALID;
   if (a->z && (a->z_batch_stride < 0 || a->z_dim_stride < 0)) return SS_ERR_INVALID;
@@ -177,8 +180,14 @@ size_t ss_work_elems(int batch, int dim, int seqlen, int dstate) {
 int ss_fwd(const ss_fwd_args* args, void* stream) {
   int rc = check_fwd(args);
   if (rc != SS_OK) return rc;
-  if (!args->out || (args->out_batch_stride < 0 || args->out_dim_stride < 0)) return SS_ERR_INVALID;
-  if (args->batch == 0 || args->seqlen == 0) return SS_OK;
+  if (args->out_batch_stride < 0 || args->out_dim_stride < 0) return SS_ERR_INVALID;
+  if (args->batch == 0) return SS_OK;
+  if (!args->out && args->seqlen > 0) return SS_ERR_INVALID;
+  if (args->seqlen == 0) {  // no steps: the final state is the zero initial state
+    if (args->last_state == nullptr) return SS_OK;
+    const size_t bytes = (size_t)args->batch * args->dim * args->dstate * sizeof(float);
+    return cuda_status(cudaMemsetAsync(args->last_state, 0, bytes, (cudaStream_t)stream));
+  }
   ssb::FwdK P{};
   P.a = *args;
   derive(P.a, P);
@@ -205,8 +214,11 @@ int ss_bwd(const ss_bwd_args* args, void* stream) {
   const ss_fwd_args& f = args->f;
   int rc = check_fwd(&f);
   if (rc != SS_OK) return rc;
-  if (!args->dout || !args->du || !args->ddelta || !args->dA || !args->dB || !args->dC) return SS_ERR_INVALID;
-  if (f.z && (!args->dz || !args->y)) return SS_ERR_INVALID;
+  // with no batch rows or no steps the (batch, dim, seqlen) tensors and variable dB / dC are empty
+  const bool empty = f.batch == 0 || f.seqlen == 0;
+  if (!args->dA || (!f.var_B && !args->dB) || (!f.var_C && !args->dC)) return SS_ERR_INVALID;
+  if (!empty && (!args->dout || !args->du || !args->ddelta || !args->dB || !args->dC)) return SS_ERR_INVALID;
+  if (f.z && !empty && (!args->dz || !args->y)) return SS_ERR_INVALID;
   if (!f.ckpt && f.seqlen > ssb::kTile && f.batch > 0) return SS_ERR_INVALID;
   cudaStream_t st = (cudaStream_t)stream;
   // accumulated outputs start from zero

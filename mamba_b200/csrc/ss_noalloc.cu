@@ -61,7 +61,7 @@ extern "C" SS_API int ss_bwd_noalloc(const ss_bwd_args* args, void* stream) {
   if (f.batch < 0 || f.dim < 1 || f.seqlen < 0 || f.dstate < 1) return SS_ERR_INVALID;
   if (ss_ckpt_elems(f.batch, f.dim, f.seqlen, f.dstate) > (size_t)SS_NOALLOC_MAX_CKPT_ELEMS)
     return SS_ERR_UNSUPPORTED;
-  if (args->du == nullptr) return SS_ERR_INVALID;
+  if (args->du == nullptr && f.batch > 0 && f.seqlen > 0) return SS_ERR_INVALID;  // empty: may be null
   float* scratch = nullptr;
   int rc = scratch_for_current_device(&scratch);
   if (rc != SS_OK) return rc;

@@ -93,6 +93,20 @@ def test_fwd_validation(field, value, status):
     assert L.lib().ss_fwd(ctypes.byref(a), None) == status
 
 
+def test_empty_batch_accepts_null_tensors():
+    """Zero batch rows: the (batch, dim, seqlen) tensors and variable B / C are empty and may
+    carry null pointers; there is nothing to launch.  A must still be given."""
+    a = _valid_fwd()
+    a.batch = 0
+    for f in ("u", "delta", "B", "C", "out"):
+        setattr(a, f, None)
+    assert L.lib().ss_fwd(ctypes.byref(a), None) == L.SS_OK
+    a.A = None
+    assert L.lib().ss_fwd(ctypes.byref(a), None) == L.SS_ERR_INVALID
+    a.A, a.batch, a.var_B = 0x1000, 0, 0
+    assert L.lib().ss_fwd(ctypes.byref(a), None) == L.SS_ERR_INVALID  # constant B is never empty
+
+
 def test_state_groups_need_an_aligned_workspace():
     a = _valid_fwd()
     a.dstate = 64

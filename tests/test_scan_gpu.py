@@ -160,6 +160,33 @@ def test_strided_inputs_match_contiguous():
     assert torch.equal(a, b)
 
 
+@pytest.mark.parametrize("b, L", [(2, 0), (0, 48), (0, 0)])
+@pytest.mark.parametrize("bc", ["var4", "const"])
+def test_empty_inputs(b, L, bc):
+    """No batch rows or no steps: outputs are empty, the final state is the zero initial
+    state, and the summed gradients (dA, dD, ddelta_bias and constant dB / dC) are zeros —
+    what the oracle gives.  Empty tensors may carry null data pointers; the C ABI accepts
+    them.  The last state is also checked through ss_fwd directly with a NaN-filled buffer,
+    so a call that left it unwritten would fail."""
+    from mamba_b200 import _lib as Lb
+    from mamba_b200.selective_scan_interface import _Prepared
+
+    inp = make_inputs(b, 64, L, 16, dtype=torch.bfloat16, bc=bc, has_z=True, seed=11)
+    got, want = run_case(inp), oracle_case(inp)
+    for k, v in want.items():
+        ref = np_(v)
+        assert tuple(got[k].shape) == ref.shape, k
+        assert np.array_equal(np_(got[k]), ref), k
+
+    dev = to_dev(inp)
+    p = _Prepared(dev["u"], dev["delta"], dev["A"], dev["B"], dev["C"], dev["D"], dev["z"], dev["delta_bias"], True)
+    out = torch.empty((p.b, p.d, p.l), dtype=p.io, device="cuda")
+    last = torch.full((p.b, p.d, p.n), float("nan"), device="cuda")
+    assert Lb.lib().ss_fwd(p.fwd_args(out, None, last), Lb.stream_of(p.device)) == Lb.SS_OK
+    torch.cuda.synchronize()
+    assert torch.equal(last, torch.zeros_like(last))
+
+
 @pytest.mark.slow
 def test_config0_fp32_forward_full():
     """Config 0: b2 d1536 L2048 N16 fp32 forward + last state, z and D = 1, full size."""
