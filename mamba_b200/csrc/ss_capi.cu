@@ -281,10 +281,10 @@ int ss_step(const ss_step_args* a, void* stream) {
   }
   if (!dtype_ok(a->io_dtype) || !dtype_ok(a->bc_dtype)) return SS_ERR_UNSUPPORTED;
   if (a->bc_dtype != SS_F32 && a->bc_dtype != a->io_dtype) return SS_ERR_UNSUPPORTED;
-  if (!a->state || !a->x || !a->dt || !a->A || !a->B || !a->C || !a->out) return SS_ERR_INVALID;
-  if (a->B_batch_stride < 0 || a->C_batch_stride < 0) return SS_ERR_INVALID;
+  if (!a->A || a->B_batch_stride < 0 || a->C_batch_stride < 0) return SS_ERR_INVALID;
   if (a->dt_proj && (a->dt_rank < 1 || a->dt_rank > 1024)) return a->dt_rank < 1 ? SS_ERR_INVALID : SS_ERR_UNSUPPORTED;
-  if (a->batch == 0) return SS_OK;
+  if (a->batch == 0) return SS_OK;  // the per-sequence tensors are empty and may carry null pointers
+  if (!a->state || !a->x || !a->dt || !a->B || !a->C || !a->out) return SS_ERR_INVALID;
   cudaStream_t st = (cudaStream_t)stream;
   return dispatch(a->io_dtype, [&](auto tag) { return ssb::launch_step<decltype(tag)>(*a, st); });
 }

@@ -29,7 +29,8 @@ int check_conv(const ss_conv_args* a) {
       2147483647LL)
     return SS_ERR_UNSUPPORTED;
   if (!dt_ok(a->io_dtype)) return SS_ERR_UNSUPPORTED;
-  if (!a->x || !a->weight) return SS_ERR_INVALID;
+  // empty tensors (no batch rows or no steps) may carry null data pointers
+  if (!a->weight || (!a->x && a->batch > 0 && a->seqlen > 0)) return SS_ERR_INVALID;
   if (a->x_batch_stride < 0 || a->x_seq_stride < 0) return SS_ERR_INVALID;
   if (a->state_out != nullptr && a->state_out == a->state_in) return SS_ERR_INVALID;
   return SS_OK;
@@ -62,7 +63,7 @@ extern "C" {
 int ss_conv_fwd(const ss_conv_args* a, void* stream) {
   int s = check_conv(a);
   if (s != SS_OK) return s;
-  if (!a->u || a->u_batch_stride < 0 || a->u_dim_stride < 0) return SS_ERR_INVALID;
+  if ((!a->u && a->batch > 0 && a->seqlen > 0) || a->u_batch_stride < 0 || a->u_dim_stride < 0) return SS_ERR_INVALID;
   if (a->z && (!a->zt || a->z_batch_stride < 0 || a->z_seq_stride < 0 || a->zt_batch_stride < 0 ||
                a->zt_dim_stride < 0))
     return SS_ERR_INVALID;
@@ -105,7 +106,7 @@ int ss_conv_bwd(const ss_conv_bwd_args* a, void* stream) {
   if (a == nullptr) return SS_ERR_INVALID;
   int s = check_conv(&a->f);
   if (s != SS_OK) return s;
-  if (!a->du || !a->dx || !a->dweight) return SS_ERR_INVALID;
+  if (!a->dweight || ((!a->du || !a->dx) && a->f.batch > 0 && a->f.seqlen > 0)) return SS_ERR_INVALID;
   if (a->du_batch_stride < 0 || a->du_dim_stride < 0 || a->dx_batch_stride < 0 || a->dx_seq_stride < 0)
     return SS_ERR_INVALID;
   if (a->dzt && (!a->dz || a->dzt_batch_stride < 0 || a->dzt_dim_stride < 0 || a->dz_batch_stride < 0 ||
@@ -151,9 +152,10 @@ int ss_conv_step(const ss_conv_step_args* a, void* stream) {
   const int ncb = (a->dim + 127) / 128;
   if ((int64_t)a->batch * ncb > 2147483647LL) return SS_ERR_UNSUPPORTED;
   if (!dt_ok(a->io_dtype)) return SS_ERR_UNSUPPORTED;
-  if (!a->x || !a->weight || !a->u || (a->width > 1 && !a->state)) return SS_ERR_INVALID;
-  if (a->state_batch_stride < 0 || a->x_batch_stride < 0 || a->u_batch_stride < 0) return SS_ERR_INVALID;
-  if (a->batch == 0) return SS_OK;
+  if (!a->weight || a->state_batch_stride < 0 || a->x_batch_stride < 0 || a->u_batch_stride < 0)
+    return SS_ERR_INVALID;
+  if (a->batch == 0) return SS_OK;  // empty tensors may carry null data pointers
+  if (!a->x || !a->u || (a->width > 1 && !a->state)) return SS_ERR_INVALID;
   cudaStream_t st = (cudaStream_t)stream;
   dim3 grid((unsigned)((int64_t)a->batch * ncb));
   return by_dtype(a->io_dtype, [&](auto tag) {

@@ -66,11 +66,10 @@ int ss_mamba_step(const ss_mamba_step_args* a, void* stream) {
   if (a->io_dtype != SS_F32 && a->io_dtype != SS_BF16 && a->io_dtype != SS_F16) return SS_ERR_UNSUPPORTED;
   const int J = a->dt_rank + 2 * a->dstate;
   if (J > 4096) return SS_ERR_UNSUPPORTED;
-  if (!a->xz || !a->conv_weight || !a->x_proj || !a->dt_proj || !a->A || !a->ssm_state || !a->y)
-    return SS_ERR_INVALID;
-  if (a->width > 1 && !a->conv_state) return SS_ERR_INVALID;
+  if (!a->conv_weight || !a->x_proj || !a->dt_proj || !a->A) return SS_ERR_INVALID;
   if (a->xz_batch_stride < 2LL * a->dim || a->y_batch_stride < a->dim) return SS_ERR_INVALID;
-  if (a->batch == 0) return SS_OK;
+  if (a->batch == 0) return SS_OK;  // the per-sequence tensors are empty and may carry null pointers
+  if (!a->xz || !a->ssm_state || !a->y || (a->width > 1 && !a->conv_state)) return SS_ERR_INVALID;
   // a cluster of cl CTAs per sequence, so that batch x cl covers about two CTAs per SM, each
   // CTA keeping at least 32 channels
   int sms = 148, dev = 0;

@@ -201,6 +201,36 @@ def test_conv_bwd_and_step_validation():
     assert lib.ss_conv_step(ctypes.byref(s), None) == L.SS_ERR_UNSUPPORTED
 
 
+def test_empty_conv_and_steps_accept_null_tensors():
+    """No batch rows: the per-sequence tensors are empty and may carry null pointers (nothing
+    is launched); the weights must still be given."""
+    lib = L.lib()
+    a = _valid_conv()
+    a.batch, a.x, a.u = 0, None, None
+    assert lib.ss_conv_fwd(ctypes.byref(a), None) == L.SS_OK
+    a.weight = None
+    assert lib.ss_conv_fwd(ctypes.byref(a), None) == L.SS_ERR_INVALID
+    s = L.ConvStepArgs()
+    s.batch, s.dim, s.width, s.silu, s.io_dtype, s.weight = 0, 64, 4, 1, L.SS_F32, 0x1000
+    assert lib.ss_conv_step(ctypes.byref(s), None) == L.SS_OK
+    s.weight = None
+    assert lib.ss_conv_step(ctypes.byref(s), None) == L.SS_ERR_INVALID
+    t = L.StepArgs()
+    t.batch, t.dim, t.dstate, t.ngroups, t.A = 0, 64, 16, 1, 0x1000
+    t.io_dtype = t.bc_dtype = L.SS_F32
+    assert lib.ss_step(ctypes.byref(t), None) == L.SS_OK
+    t.A = None
+    assert lib.ss_step(ctypes.byref(t), None) == L.SS_ERR_INVALID
+    m = L.MambaStepArgs()
+    m.batch, m.dim, m.dstate, m.width, m.dt_rank, m.io_dtype = 0, 64, 16, 4, 4, L.SS_BF16
+    for f in ("conv_weight", "x_proj", "dt_proj", "A"):
+        setattr(m, f, 0x1000)
+    m.xz_batch_stride, m.y_batch_stride = 128, 64
+    assert lib.ss_mamba_step(ctypes.byref(m), None) == L.SS_OK
+    m.x_proj = None
+    assert lib.ss_mamba_step(ctypes.byref(m), None) == L.SS_ERR_INVALID
+
+
 def test_rmsnorm_validation():
     lib = L.lib()
     a = L.RmsNormArgs()

@@ -81,6 +81,26 @@ def test_conv_backward_matches_autograd(dtype, b, L, d, K, bias, state):
         assert_close("dbias", db, br.grad, rtol, rtol * float(br.grad.abs().max()))
 
 
+@pytest.mark.parametrize("b,L", [(0, 8), (2, 0)])
+def test_conv_empty_inputs(b, L):
+    """No batch rows or no steps: empty outputs (empty tensors may carry null pointers); with no
+    steps the state passes through unchanged; the weight / bias gradients are zeros."""
+    from mamba_b200.inner import conv_backward, conv_forward
+
+    d, K = 64, 4
+    xz, w, bs, st = _conv_inputs(b, L, d, K, torch.bfloat16, seed=1, state=True)
+    x, z = xz[..., :d], xz[..., d:]
+    u, zt, st_out = conv_forward(x, w, bs, z, state_in=st, want_state=True)
+    torch.cuda.synchronize()
+    assert u.shape == (b, d, L) and zt.shape == (b, d, L)
+    assert torch.equal(st_out, st)
+    dxz = torch.empty_like(xz)
+    du = torch.empty(b, d, L, dtype=torch.bfloat16, device="cuda")
+    dw, db = conv_backward(x, w, bs, du, dxz[..., :d], du, dxz[..., d:], state_in=st)
+    torch.cuda.synchronize()
+    assert not dw.any() and not db.any()
+
+
 @pytest.mark.parametrize("K", [4, 2])
 def test_conv_step_continues_the_forward(K):
     from mamba_b200.inner import conv_forward, conv_step

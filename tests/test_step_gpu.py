@@ -123,3 +123,19 @@ def test_step_batch_beyond_65535():
                                             None, dt_softplus=True)
     assert_close("out", out[rows], out_ref, 1e-4, 1e-5)
     assert_close("state", st[rows], st_ref, 1e-4, 1e-5)
+
+
+def test_step_with_no_sequences():
+    """An empty decode batch is accepted (its tensors may carry null pointers) and gives an
+    empty output."""
+    import mamba_b200
+
+    d, n = 64, 16
+    state = torch.empty(0, d, n, device="cuda")
+    x = torch.empty(0, d, device="cuda")
+    B = torch.empty(0, n, device="cuda")
+    A = -torch.arange(1, n + 1, dtype=torch.float32, device="cuda").repeat(d, 1)
+    out = mamba_b200.selective_state_update(state, x, x, A, B, B, torch.ones(d, device="cuda"), z=x,
+                                            dt_bias=torch.zeros(d, device="cuda"), dt_softplus=True)
+    torch.cuda.synchronize()
+    assert out.shape == (0, d) and out.dtype == torch.float32
