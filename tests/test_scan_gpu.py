@@ -290,6 +290,42 @@ def test_config4_full_size_fwd_bwd():
     compare(sub, want, torch.bfloat16, keys=("dA", "dD", "ddelta_bias"))
 
 
+@pytest.mark.slow
+def test_more_than_2_31_elements_per_tensor():
+    """b130 d4096 L4096: 2.18G elements per (batch, dim, seqlen) tensor, so the last batch rows
+    start beyond 2^31 elements (the reference's 32-bit strides overflow at 2^32; every offset
+    here is 64-bit).  bf16 fwd + bwd with z; ~50 GB on the device.  The first and the last batch
+    row (all channels, all steps) are checked against the oracle: out, last state, du, ddelta,
+    dz and the rows' dB / dC."""
+    import math
+
+    import mamba_b200
+
+    b, d, L, n = 130, 4096, 4096, 16
+    assert b * d * L > 2**31 and (b - 1) * d * L >= 2**31
+    g = torch.Generator(device="cuda").manual_seed(9)
+    rn = lambda *s: torch.randn(*s, generator=g, device="cuda").bfloat16()
+    x = dict(u=rn(b, d, L), delta=rn(b, d, L).mul_(0.5), z=rn(b, d, L), B=rn(b, 1, n, L), C=rn(b, 1, n, L))
+    dout = rn(b, d, L)
+    gc = torch.Generator().manual_seed(9)
+    dt = torch.exp(torch.rand(d, generator=gc) * (math.log(0.1) - math.log(1e-3)) + math.log(1e-3)).clamp(min=1e-4)
+    x.update(A=-torch.arange(1, n + 1, dtype=torch.float32).repeat(d, 1).cuda(), D=torch.ones(d, device="cuda"),
+             delta_bias=(dt + torch.log(-torch.expm1(-dt))).cuda())
+    keys = ("u", "delta", "A", "B", "C", "D", "z", "delta_bias")
+    t = {k: x[k].requires_grad_() for k in keys}
+    out, last = mamba_b200.selective_scan_fn(t["u"], t["delta"], t["A"], t["B"], t["C"], t["D"], t["z"],
+                                             t["delta_bias"], True, return_last_state=True)
+    out.backward(dout)
+    torch.cuda.synchronize()
+    rows = [0, b - 1]
+    got = {"out": out.detach()[rows], "last_state": last[rows]}
+    got.update({"d" + k: t[k].grad[rows] for k in ("u", "delta", "z", "B", "C")})
+    del out, last, t
+    cpu = {k: (x[k][rows] if k in ("u", "delta", "z", "B", "C") else x[k]).detach().cpu() for k in keys}
+    cpu.update(softplus=True, dout=dout[rows].cpu())
+    compare(got, oracle_case(cpu), torch.bfloat16, keys=("out", "last_state", "du", "ddelta", "dz", "dB", "dC"))
+
+
 def test_batch_beyond_65535():
     """The grids are flattened, so a batch larger than gridDim.y's 65535 runs (the reference puts
     batch on gridDim.x and accepts it).  Rows are independent: a spread of rows is checked
