@@ -179,7 +179,7 @@ def lib():
                 L.ss_mamba_step.argtypes = [ctypes.POINTER(MambaStepArgs), c_vp]
                 for f in ("ss_fwd", "ss_bwd", "ss_step", "ss_last_cuda_error", "ss_abi_version",
                           "ss_conv_fwd", "ss_conv_bwd", "ss_conv_step", "ss_rmsnorm_fwd", "ss_rmsnorm_bwd",
-           "ss_mamba_step"):
+                          "ss_mamba_step"):
                     getattr(L, f).restype = c_int
                 L.ss_ckpt_elems.argtypes = [c_int, c_int, c_int, c_int]
                 L.ss_ckpt_elems.restype = ctypes.c_size_t
