@@ -43,3 +43,24 @@ def test_cpu_baseline_sampler_reports_a_rate():
 def test_compute_floor_is_a_fraction_of_the_step():
     f = bench.compute_floor(8, 1536, 2048, 16, ms_step=0.87, sm_mhz=1965.0)
     assert 0.2 < f["mufu_frac"] < 0.6 and f["mufu_floor_ms"] > 0
+
+
+def test_reference_arm_line_and_other_ranks(capsys, monkeypatch):
+    """`--impl reference`: rank 0 prints one line with the arm's keys and the median of the timed
+    steps (warm-up steps dropped); other ranks print nothing and exit 0.  The sampler is faked so
+    the test does not spend the arm's CPU budget."""
+    import argparse
+    import json
+
+    monkeypatch.setattr(bench, "cpu_sample_rate",
+                        lambda elems, tokens, budget, seed=0, shape=None: (1000.0 + seed, 8, "fake sample", 0.1))
+    a = argparse.Namespace(workload="scan", steps=3, warmup=1)
+    assert bench.reference_arm(a, 2, 1) == 0
+    assert capsys.readouterr().out == ""
+    assert bench.reference_arm(a, 2, 0) == 0
+    line = json.loads(capsys.readouterr().out.strip().splitlines()[-1])
+    assert line["impl"] == "reference" and line["n_gpus"] == 2 and line["steps"] == 3
+    assert line["value"] == 1002.0  # median of seeds 1..3; seed 0 was the warm-up
+    assert line["cpu_baseline"]["kind"] == "port" and line["cpu_baseline"]["cores"] == 8
+    assert line["e2e"] == {"value": 1002.0, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}
+    assert line["metric"] == bench.METRIC and line["config"]["global_batch"] == 16
