@@ -1,7 +1,7 @@
 #!/usr/bin/env python
 """Selective-scan fwd+bwd throughput on B200 — the benchmark contract of this repository.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl mamba_b200|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl mamba_b200|reference] [--workload W]
     torchrun --nproc-per-node N bench.py --gpus N ...          (N > 1, one rank per GPU)
 
 A step is one forward + backward of the selective scan (public operator
@@ -10,17 +10,23 @@ north-star point of BASELINE.json: per GPU batch 8, d_inner 1536, seqlen 2048, d
 bf16 u / delta / z / B / C, fp32 A / D / delta_bias, softplus on, SiLU(z) gate.  Inputs per
 step (u, delta, z, dout: 4 x 50 MB) exceed the 126 MB L2, so no flush is needed between
 steps.  N GPUs run N batch shards of a global batch 8N (weak scaling; the scan has no
-exchange, so no collective runs inside the timed region).  ``--workload scan-c4`` runs the
-same step at BASELINE config 4 (d_inner 5120, a global batch of 64 split over the N GPUs:
-strong scaling).
+exchange, so no collective runs inside the timed region).  Other scan workloads:
+``scan-c0`` (config 0: fp32 forward + final state, batch 2), ``scan-c1`` (config 1: bf16
+fwd+bwd, batch 2), ``scan-c2`` (config 2: bf16 forward + final state, batch 1, d_inner 5120,
+seqlen 32768) — per-GPU batch fixed; ``scan-c4`` (config 4: d_inner 5120, a global batch of
+64 split over the N GPUs: strong scaling).  Workloads whose inputs fit in L2 (configs 0 and
+1) flush it between timed steps.
 
 Rank 0 prints one JSON line.  ``value`` is tokens/s of the whole job (inputs resident in
 HBM); ``e2e`` is the same metric with pinned-host inputs copied in and all results copied
-out every step; ``roofline`` covers the dominant kernel (the backward scan) with
-algorithmic bytes; ``cpu_baseline`` is the CPU oracle port (oracle/ss_oracle.c, fp32,
-all host threads) on a bounded sample.  ``--impl reference`` times that CPU port alone:
-the reference (nmquan1503/Mamba) has no CPU implementation of its own, and its CUDA
-extension has no bf16 or z support.
+out every step; ``roofline`` covers the dominant kernel with algorithmic bytes;
+``cpu_baseline`` is the CPU oracle port (oracle/ss_oracle.c, fp32, all host threads) on a
+bounded sample; ``reference_ext`` (N = 1) times the reference's own CUDA extension against
+this library at the same shape in the extension's only mode (fp32, no gate); ``verification``
+(N > 1) reports the NCCL all-gather of the shards and their oracle check, done after the
+timed regions.  ``--impl reference`` times the CPU port alone: the reference
+(nmquan1503/Mamba) has no CPU implementation of its own, and its CUDA extension has no bf16
+or z support.
 """
 from __future__ import annotations
 
@@ -36,18 +42,33 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, HERE)
 
 METRIC = "selective-scan fwd+bwd tokens/s and HBM GB/s (% of ~8 TB/s peak) at 1/2/4/8 B200"
-# scan workloads: "scan" is the north-star point (per-GPU batch fixed, weak scaling); "scan-c4"
-# is BASELINE config 4, a Mamba-2.8B-shaped layer whose global batch of 64 is split over the GPUs
-# (strong scaling)
+# scan workloads: "scan" is the north-star point (per-GPU batch fixed, weak scaling); "scan-c0",
+# "scan-c1" and "scan-c2" are BASELINE configs 0 (fp32 forward + last state), 1 (bf16 fwd+bwd at
+# batch 2) and 2 (long-sequence bf16 forward + last state), per-GPU batch fixed; "scan-c4" is
+# BASELINE config 4, a Mamba-2.8B-shaped layer whose global batch of 64 is split over the GPUs
+# (strong scaling).  dtype: I/O dtype of u / delta / z / B / C (A, D, delta_bias are fp32);
+# passes: "fwd+bwd" (autograd step) or "fwd" (forward only); z: SiLU(z) gate; last: the forward
+# also returns the final state.
 SCAN_WORKLOADS = {
-    "scan": dict(b=8, d=1536, L=2048, n=16, scaling="weak",
+    "scan": dict(b=8, d=1536, L=2048, n=16, scaling="weak", dtype="bf16", passes="fwd+bwd", z=True, last=False,
                  label="selective_scan fwd+bwd, batch 8 per GPU, d_inner 1536, seqlen 2048, d_state 16, "
                        "bf16 I/O + fp32 state, z gate, softplus (north-star point)"),
-    "scan-c4": dict(b=64, d=5120, L=2048, n=16, scaling="strong",
+    "scan-c0": dict(b=2, d=1536, L=2048, n=16, scaling="weak", dtype="f32", passes="fwd", z=False, last=True,
+                    label="selective_scan forward + last state, batch 2 per GPU, d_inner 1536, seqlen 2048, "
+                          "d_state 16, fp32 I/O, no gate, softplus (config 0)"),
+    "scan-c1": dict(b=2, d=1536, L=2048, n=16, scaling="weak", dtype="bf16", passes="fwd+bwd", z=True, last=False,
+                    label="selective_scan fwd+bwd, batch 2 per GPU, d_inner 1536, seqlen 2048, d_state 16, "
+                          "bf16 I/O + fp32 state, z gate, softplus (config 1)"),
+    "scan-c2": dict(b=1, d=5120, L=32768, n=16, scaling="weak", dtype="bf16", passes="fwd", z=True, last=True,
+                    label="selective_scan forward + last state, batch 1 per GPU, d_inner 5120, seqlen 32768, "
+                          "d_state 16, bf16 I/O + fp32 state, z gate, softplus (config 2, long sequence)"),
+    "scan-c4": dict(b=64, d=5120, L=2048, n=16, scaling="strong", dtype="bf16", passes="fwd+bwd", z=True,
+                    last=False,
                     label="selective_scan fwd+bwd, global batch 64 split over the GPUs, d_inner 5120, seqlen 2048, "
                           "d_state 16, bf16 I/O + fp32 state, z gate, softplus (config 4, Mamba-2.8B-shaped layer)"),
 }
 PER_GPU = {k: SCAN_WORKLOADS["scan"][k] for k in ("b", "d", "L", "n")}
+ES = {"bf16": 2, "f32": 4}
 
 
 def scan_shape(workload, world):
@@ -71,8 +92,13 @@ def args_():
     ap.add_argument("--e2e-steps", type=int, default=20)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="CPU-baseline sample budget")
-    ap.add_argument("--workload", default="scan", choices=["scan", "scan-c4", "block", "decode", "norm", "model"],
-                    help="scan: the north-star selective scan (default); scan-c4: the scan at config 4 "
+    ap.add_argument("--no-reference-ext", action="store_true",
+                    help="skip the reference extension comparison (N = 1 scan workloads)")
+    ap.add_argument("--workload", default="scan",
+                    choices=["scan", "scan-c0", "scan-c1", "scan-c2", "scan-c4", "block", "decode", "norm", "model"],
+                    help="scan: the north-star selective scan (default); scan-c0 / scan-c1 / scan-c2: BASELINE "
+                         "configs 0 (fp32 forward), 1 (bf16 fwd+bwd, batch 2), 2 (bf16 forward, L 32768); "
+                         "scan-c4: the scan at config 4 "
                          "(global batch 64 over the GPUs, d_inner 5120); block: one MambaSimple block "
                          "(d_model 768) fwd+bwd, fused mamba_inner_fn against the reference's op sequence; "
                          "decode: a 24-layer CausalLM (d_model 768) decoding 256 tokens after a 128-token prompt "
@@ -88,25 +114,28 @@ def args_():
     return ap.parse_args()
 
 
-def algorithmic_bytes(b, d, L, n, es=2):
-    """Bytes the path must move (bf16 I/O, z gate, variable B / C, fp32 dB / dC).
-    fwd: read u, delta, z; write out            -> 4 es per element; B, C -> 2 n es per token
-    bwd: read u, delta, z, dout; write du, ddelta, dz -> 7 es per element;
+def algorithmic_bytes(b, d, L, n, es=2, z=True, last=False):
+    """Bytes the path must move (I/O element size es, variable B / C, fp32 dB / dC).
+    fwd: read u, delta (, z); write out          -> (3 + z) es per element; B, C -> 2 n es per
+         token; the final state, when returned, 4 n per (batch, channel)
+    bwd: read u, delta, dout (, z); write du, ddelta (, dz) -> (5 + 2 z) es per element;
          read B, C (2 n es) and write dB, dC fp32 (2 n 4) per token."""
     elems, tokens = b * d * L, b * L
-    fwd = elems * 4 * es + tokens * 2 * n * es
-    bwd = elems * 7 * es + tokens * (2 * n * es + 2 * n * 4)
+    fwd = elems * (3 + int(z)) * es + tokens * 2 * n * es + (b * d * n * 4 if last else 0)
+    bwd = elems * (5 + 2 * int(z)) * es + tokens * (2 * n * es + 2 * n * 4)
     return fwd, bwd
 
 
-def compute_floor(b, d, L, n, ms_step, sm_mhz):
+def compute_floor(b, d, L, n, ms_step, sm_mhz, z=True, backward=True):
     """The step's MUFU (ex2 / lg2 / rcp) work, counted from the kernels' arithmetic, against the
     B200's 148 SMs x 16 MUFU lanes per clock at the sampled SM clock: the compute floor that
-    keeps this path far from its HBM roofline.  Per element: forward 1 ex2 per state + 4
-    (softplus: ex2, lg2; SiLU gate: ex2, rcp); backward 2 ex2 per state (the tile's forward
-    recompute and the reverse step) + 5 (softplus and its slope: ex2, lg2, rcp; gate: ex2, rcp)."""
+    keeps this path far from its HBM roofline.  Per element: forward 1 ex2 per state + 2
+    (softplus: ex2, lg2) + 2 with a gate (SiLU: ex2, rcp); backward 2 ex2 per state (the tile's
+    forward recompute and the reverse step) + 3 (softplus and its slope: ex2, lg2, rcp) + 2 with
+    a gate."""
     elems = b * d * L
-    mufu = elems * ((n + 4) + (2 * n + 5))
+    g = 2 if z else 0
+    mufu = elems * ((n + 2 + g) + ((2 * n + 3 + g) if backward else 0))
     mhz = sm_mhz or 1965.0
     peak = 148 * 16 * mhz * 1e6
     floor_ms = mufu / peak * 1e3
@@ -126,16 +155,25 @@ def load_peaks():
         return 6650.0, "fallback"
 
 
-def profile_traffic():
-    """dram bytes per backward launch from the committed ncu summary, if present."""
-    p = os.path.join(HERE, "profiles", "ss_bwd_north_traffic.txt")
+def profile_traffic(workload, kernel):
+    """dram bytes (read + write) of one launch of `kernel` at `workload`, from the committed ncu
+    table profiles/scan_kernels_dram_traffic.txt (lines "workload kernel bytes"), if present."""
+    p = os.path.join(HERE, "profiles", "scan_kernels_dram_traffic.txt")
     try:
         for line in open(p):
-            if line.startswith("bytes_per_launch_full"):
-                return float(line.split("=")[1])
+            f = line.split()
+            if len(f) == 3 and not line.startswith("#") and f[0] == workload and f[1] == kernel:
+                return float(f[2])
     except OSError:
         pass
     return None
+
+
+def launches_per_step(d, n, backward):
+    """This library's kernels per step: the forward scan, the backward scan with it, and a
+    finishing pass after each when the states run in groups (dstate > 16)."""
+    per_pass = 2 if n > 16 else 1
+    return per_pass * (2 if backward else 1)
 
 
 # ----------------------------------------------------------------------------- clocks
@@ -217,20 +255,26 @@ class ClockSampler:
 
 
 # ----------------------------------------------------------------------------- inputs
-def make_inputs(b, d, L, n, seed, device="cpu"):
+def make_inputs(b, d, L, n, seed, device="cpu", dtype="bf16", z=True, dout=True):
     """Seeded inputs with the configs' distributions, generated on `device` (the CPU for the
-    north-star point; the GPU for config 4, whose 671M-element tensors take minutes to draw on
-    one host thread)."""
+    north-star point; the GPU for the large configs, whose 168M- to 671M-element tensors take
+    minutes to draw on one host thread).  u, delta, z, B, C, dout in `dtype`; A, D, delta_bias
+    fp32; z / dout left out when not wanted."""
     import torch
 
     g = torch.Generator(device=device).manual_seed(seed)
     rn = lambda *s: torch.randn(*s, generator=g, dtype=torch.float32, device=device)
     dt = torch.exp(torch.rand(d, generator=g, device=device) * (math.log(0.1) - math.log(1e-3))
                    + math.log(1e-3)).clamp(min=1e-4)
-    bf = lambda t: t.bfloat16()
-    x = dict(u=bf(rn(b, d, L)), delta=bf(0.5 * rn(b, d, L)), z=bf(rn(b, d, L)),
-             B=bf(rn(b, 1, n, L)), C=bf(rn(b, 1, n, L)), dout=bf(rn(b, d, L)),
-             A=-torch.arange(1, n + 1, dtype=torch.float32, device=device).repeat(d, 1),
+    io = torch.bfloat16 if dtype == "bf16" else torch.float32
+    cv = lambda t: t.to(io)
+    x = dict(u=cv(rn(b, d, L)), delta=cv(0.5 * rn(b, d, L)))
+    if z:
+        x["z"] = cv(rn(b, d, L))
+    x.update(B=cv(rn(b, 1, n, L)), C=cv(rn(b, 1, n, L)))
+    if dout:
+        x["dout"] = cv(rn(b, d, L))
+    x.update(A=-torch.arange(1, n + 1, dtype=torch.float32, device=device).repeat(d, 1),
              D=torch.ones(d, device=device), delta_bias=dt + torch.log(-torch.expm1(-dt)))
     return x
 
@@ -242,17 +286,20 @@ def cpu_sample_rate(n_full_elems, tokens_full, budget_s, seed=0, shape=None):
     import torch
     from oracle import oracle as O
 
-    shape = shape or PER_GPU
+    shape = shape or SCAN_WORKLOADS["scan"]
     d_full, L, n = shape["d"], shape["L"], shape["n"]
+    with_z, bwd, last = shape.get("z", True), shape.get("passes", "fwd+bwd") == "fwd+bwd", shape.get("last", False)
 
     def run(rows):
         bsl, dsl = (1, rows) if rows <= d_full else (rows // d_full, d_full)
-        h = make_inputs(bsl, dsl, L, n, seed, "cpu")
+        h = make_inputs(bsl, dsl, L, n, seed, "cpu", dtype="f32", z=with_z, dout=bwd)
+        zz = h.get("z")
         t = time.perf_counter()
-        O.selective_scan_ref(h["u"], h["delta"], h["A"], h["B"], h["C"], h["D"], h["z"], h["delta_bias"], True,
-                             precision="f32")
-        O.selective_scan_ref_bwd(h["u"], h["delta"], h["A"], h["B"], h["C"], h["D"], h["z"], h["delta_bias"], True,
-                                 h["dout"], precision="f32")
+        O.selective_scan_ref(h["u"], h["delta"], h["A"], h["B"], h["C"], h["D"], zz, h["delta_bias"], True,
+                             return_last_state=last, precision="f32")
+        if bwd:
+            O.selective_scan_ref_bwd(h["u"], h["delta"], h["A"], h["B"], h["C"], h["D"], zz, h["delta_bias"], True,
+                                     h["dout"], precision="f32")
         return time.perf_counter() - t
 
     threads = O.max_threads()
@@ -269,7 +316,8 @@ def cpu_sample_rate(n_full_elems, tokens_full, budget_s, seed=0, shape=None):
     bsl, dsl = (1, rows) if rows <= d_full else (rows // d_full, d_full)
     rate_elems = reps * rows * L / t
     value = tokens_full / (n_full_elems / rate_elems)
-    return value, threads, (f"{reps} x batch {bsl} x {dsl} channels x {L} steps (fwd+bwd, fp32 port) "
+    return value, threads, (f"{reps} x batch {bsl} x {dsl} channels x {L} steps ({'fwd+bwd' if bwd else 'fwd'}, "
+                            f"fp32 port) "
                             f"in {t:.2f} s"), t
 
 
@@ -302,13 +350,166 @@ def reference_arm(a, world, rank):
     return 0
 
 
+L2_BYTES = 126 * 1024 * 1024
+
+
+def step_input_bytes(shape):
+    """Bytes of the per-element tensors a step reads (u, delta, z, dout) on one GPU."""
+    b, d, L = shape["b"], shape["d"], shape["L"]
+    k = 2 + int(shape["z"]) + int(shape["passes"] == "fwd+bwd")
+    return k * b * d * L * ES[shape["dtype"]]
+
+
+def flushes_l2(shape):
+    """Workloads whose step inputs fit in the L2 get the L2 flushed between timed steps; the others
+    read more than the L2 holds every step."""
+    return step_input_bytes(shape) <= L2_BYTES
+
+
 def config_dict(world, shape):
     b, d, L = shape["b"], shape["d"], shape["L"]
-    step_mb = 4 * b * d * L * 2 / 1e6
+    mb = step_input_bytes(shape) / 1e6
+    l2 = (f"L2 flushed between timed steps (a 256 MiB buffer written outside the per-step events; "
+          f"{mb:.0f} MB of per-element inputs per GPU per step)" if flushes_l2(shape) else
+          f"inputs larger than L2 ({mb:.0f} MB of per-element inputs per GPU per step)")
     return {"workload": shape["label"],
             "global_batch": shape["global_b"], "per_gpu_batch": b, "d_inner": d, "seq_len": L,
             "d_state": shape["n"], "parallelism": f"batch-sharded x{world}, no collective in the path",
-            "l2": f"inputs larger than L2 ({step_mb:.0f} MB per GPU per step of u/delta/z/dout)"}
+            "l2": l2}
+
+
+# ----------------------------------------------------------------------------- baselines / checks
+REF_SO = os.path.join(HERE, "oracle", "_ref", "selective_scan.so")
+
+
+def gpu_lead(ms=5.0):
+    """Enqueue ~ms of idle GPU work (a spin kernel) so the host gets ahead of the device before a
+    timed region: the CUDA events that bracket each step then measure the device's time for the
+    step, not the host's launch latency (which matters for the sub-millisecond small-batch steps).
+    The lead itself lies before the first event of the region."""
+    import torch
+
+    torch.cuda._sleep(int(ms * 1e-3 * 2.0e9))
+
+
+def _timed_calls(fn, iters, warmup=3, scrub=None):
+    """Mean ms of fn() over `iters` calls on the current stream (CUDA events per call, the host
+    ahead of the device; the L2 is flushed before each call when `scrub` is given, outside the
+    call's events)."""
+    import torch
+
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    gpu_lead()
+    evs = []
+    for _ in range(iters):
+        if scrub is not None:
+            scrub.zero_()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        fn()
+        e1.record()
+        evs.append((e0, e1))
+    torch.cuda.synchronize()
+    return statistics.mean(e0.elapsed_time(e1) for e0, e1 in evs)
+
+
+def reference_ext_compare(shape, dev, backward, iters=5):
+    """The reference's own CUDA extension (csrc/selective_scan/*, compiled unmodified from its
+    sources into oracle/_ref/ by oracle/build_ref.py) against this library on the same GPU, at
+    this workload's shape in the only mode the extension supports: fp32 I/O, no gate.  Both run
+    through the same positional entry points (selective_scan.cpp:331-334 of the reference;
+    mamba_b200.selective_scan_ext here), on identical seeded inputs; outputs are compared as a
+    sanity check.  A baseline measurement beside the bench line, not part of the timed step."""
+    import importlib.util
+
+    import torch
+
+    import mamba_b200.selective_scan_ext as ours
+
+    if not os.path.exists(REF_SO):
+        return {"unavailable": "reference extension not built (oracle/build_ref.py needs the reference sources)"}
+    spec = importlib.util.spec_from_file_location("selective_scan", REF_SO)
+    ref = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(ref)
+    b, d, L, n = shape["b"], shape["d"], shape["L"], shape["n"]
+    x = make_inputs(b, d, L, n, seed=7, device=dev, dtype="f32", z=False, dout=backward)
+    args = (x["u"], x["delta"], x["A"], x["B"], x["C"], x["D"], x["delta_bias"])
+    scrub = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev) if flushes_l2(
+        dict(shape, dtype="f32", z=False)) else None
+    r_out, r_x = ref.forward(*args, True)
+    o_out, o_x = ours.forward(*args, True)
+    torch.cuda.synchronize()
+    diff = (o_out - r_out).abs()
+    excess = float((diff / (1e-5 + 1e-4 * r_out.abs())).max())
+    del diff
+    res = {"mode": "fp32 I/O, no gate (the reference extension's only mode), same shape, GPU and inputs",
+           "out_max_excess_fp32_tol": excess}
+    for tag, mod, xs in (("reference_ext", ref, r_x), ("mamba_b200", ours, o_x)):
+        if backward:
+            ms = _timed_calls(lambda: mod.backward(*args, x["dout"], mod.forward(*args, True)[1], True), iters,
+                              scrub=scrub)
+        else:
+            ms = _timed_calls(lambda: mod.forward(*args, True), iters, scrub=scrub)
+        res[f"{tag}_ms"] = ms
+        res[f"{tag}_tokens_per_s"] = b * L / (ms / 1e3)
+    res["pass"] = "fwd+bwd" if backward else "fwd"
+    res["speedup"] = res["reference_ext_ms"] / res["mamba_b200_ms"]
+    return res
+
+
+def verify_shards(x, host, shape, rank, world, dev, step, backward):
+    """Verification of a sharded run (outside every timed region), through
+    mamba_b200.sharding.verify: every rank recomputes its shard, the shards' outputs are
+    all-gathered over NCCL with their owners' checksums, and each rank checks three sampled
+    (batch row, channel) rows of its shard — out and, with a backward, du / ddelta / dz —
+    against the CPU oracle (rows are independent, so a row's inputs alone determine them)."""
+    import numpy as np
+    import torch
+
+    from mamba_b200 import sharding
+    from oracle import oracle as O
+
+    b, d, L, n = shape["b"], shape["d"], shape["L"], shape["n"]
+    if backward:
+        for k in ("u", "delta", "A", "B", "C", "D", "z", "delta_bias"):
+            if k in x:
+                x[k].grad = None
+        out, _ = step(x)
+        out.backward(x["dout"])
+    else:
+        with torch.no_grad():
+            out, _ = step(x)
+    torch.cuda.synchronize()
+    rtol, atol = (1e-4, 1e-5) if shape["dtype"] == "f32" else (2e-2, 5e-2)
+    br, chans = rank % b, sorted({0, d // 2 + 1, d - 1})
+    sl = lambda t: t[br:br + 1, chans].float()
+    hz = host.get("z")
+    args = (sl(host["u"]), sl(host["delta"]), host["A"][chans], host["B"][br:br + 1].float(),
+            host["C"][br:br + 1].float(), host["D"][chans], None if hz is None else sl(hz),
+            host["delta_bias"][chans], True)
+    got, want = [out.detach()[br:br + 1, chans]], [O.selective_scan_ref(*args)]
+    if backward:
+        g = O.selective_scan_ref_bwd(*args, sl(host["dout"]))
+        got += [x["u"].grad[br:br + 1, chans], x["delta"].grad[br:br + 1, chans]]
+        want += [g["du"], g["ddelta"]]
+        if hz is not None:
+            got.append(x["z"].grad[br:br + 1, chans])
+            want.append(g["dz"])
+    got_rows = torch.cat([t.float().reshape(-1).cpu() for t in got])
+    want_rows = np.concatenate([np.asarray(w, np.float64).reshape(-1) for w in want])
+    s = sharding.plan(b * world, d, world, rank)
+    rep = sharding.verify(out.detach(), s, got_rows, want_rows, rtol, atol)
+    res = {"shards": world, "collective": "NCCL all_gather of every shard's output (mamba_b200.sharding.verify)",
+           "gathered_bytes": int(rep["gathered"].numel() * rep["gathered"].element_size()),
+           "checksum_bad_ranks": rep["checksum_bad_ranks"], "rows_checked_per_shard": len(chans),
+           "max_row_excess": max(rep["row_excess"]), "bad_ranks": rep["bad_ranks"],
+           "tolerance": f"rtol {rtol}, atol {atol} against the CPU oracle", "pass": rep["ok"]}
+    del rep
+    if rank == 0:
+        print(f"[bench] shard verification: {json.dumps(res)}", file=sys.stderr, flush=True)
+    return res
 
 
 # ----------------------------------------------------------------------------- gpu arm
@@ -744,20 +945,29 @@ def main():
 
     shape = scan_shape(a.workload, world)
     b, d, L, n = shape["b"], shape["d"], shape["L"], shape["n"]
-    if a.workload == "scan":
-        host = make_inputs(b, d, L, n, seed=1000 + rank, device="cpu")
+    with_z, backward, last = shape["z"], shape["passes"] == "fwd+bwd", shape["last"]
+    mk = dict(dtype=shape["dtype"], z=with_z, dout=backward)
+    if b * d * L <= 32 * 1024 * 1024:  # small configs: drawn on the host, like the tests
+        host = make_inputs(b, d, L, n, seed=1000 + rank, device="cpu", **mk)
         x = {k: v.to(dev) for k, v in host.items()}
     else:
-        x = make_inputs(b, d, L, n, seed=1000 + rank, device=dev)
+        x = make_inputs(b, d, L, n, seed=1000 + rank, device=dev, **mk)
         host = {k: v.cpu() for k, v in x.items()}
-    leaves = ["u", "delta", "A", "B", "C", "D", "z", "delta_bias"]
-    for k in leaves:
-        x[k].requires_grad_(True)
+    leaves = [k for k in ("u", "delta", "A", "B", "C", "D", "z", "delta_bias") if k in x]
 
     def step(t):
-        out = mamba_b200.selective_scan_fn(t["u"], t["delta"], t["A"], t["B"], t["C"], t["D"], t["z"],
-                                           t["delta_bias"], True)
-        return out
+        r = mamba_b200.selective_scan_fn(t["u"], t["delta"], t["A"], t["B"], t["C"], t["D"], t.get("z"),
+                                         t["delta_bias"], True, return_last_state=last)
+        return r if last else (r, None)
+
+    def run_step(t):
+        """One step; returns (out, last_state | None).  Forward-only workloads run without autograd."""
+        if backward:
+            out, ls = step(t)
+            out.backward(t["dout"])
+            return out, ls
+        with torch.no_grad():
+            return step(t)
 
     def clear(t):
         for k in leaves:
@@ -767,32 +977,45 @@ def main():
         if world > 1:
             dist.barrier()
 
+    if backward:
+        for k in leaves:
+            x[k].requires_grad_(True)
     for _ in range(a.warmup):
-        out = step(x)
-        out.backward(x["dout"])
+        run_step(x)
         clear(x)
     torch.cuda.synchronize()
 
     K = a.steps
+    flush = flushes_l2(shape)
+    scrub = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev) if flush else None
     ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(K)]
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier()
     torch.cuda.synchronize()
     with ClockSampler(dev.index) as clk:
+        gpu_lead()  # outside the region: the host runs ahead of the device through it
         t0.record()
         for i in range(K):
+            if flush:
+                scrub.zero_()  # evicts the previous step's tensors from L2 (outside the step's events)
             ev[i][0].record()
-            out = step(x)
-            ev[i][1].record()
-            out.backward(x["dout"])
+            if backward:
+                out, _ = step(x)
+                ev[i][1].record()
+                out.backward(x["dout"])
+            else:
+                with torch.no_grad():
+                    out, _ = step(x)
+                ev[i][1].record()
             ev[i][2].record()
             clear(x)
         t1.record()
         torch.cuda.synchronize()
         barrier()
-    elapsed = t0.elapsed_time(t1)  # ms
+    # ms: the whole region, or with a flush the sum of the steps' own event intervals
+    elapsed = sum(e[0].elapsed_time(e[2]) for e in ev) if flush else t0.elapsed_time(t1)
     fwd_ms = statistics.mean(e[0].elapsed_time(e[1]) for e in ev)
-    bwd_ms = statistics.mean(e[1].elapsed_time(e[2]) for e in ev)
+    bwd_ms = statistics.mean(e[1].elapsed_time(e[2]) for e in ev) if backward else 0.0
     if world > 1:
         tt = torch.tensor([elapsed], device=dev, dtype=torch.float64)
         dist.all_reduce(tt, op=dist.ReduceOp.MAX)
@@ -806,7 +1029,7 @@ def main():
     # copied in while step i computes, and step i's results are copied out while step i+1
     # computes (the host link is full duplex).  Every step still moves all of its bytes both
     # ways; inputs alternate between two device buffer sets.
-    names = ("u", "delta", "z", "B", "C", "dout", "A", "D", "delta_bias")
+    names = tuple(k for k in ("u", "delta", "z", "B", "C", "dout", "A", "D", "delta_bias") if k in host)
     pin = {k: v.pin_memory() for k, v in host.items()}
     bufs = [{k: torch.empty_like(v, device=dev) for k, v in host.items()} for _ in range(2)]
     s_in, s_cmp, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev), torch.cuda.Stream(dev)
@@ -835,10 +1058,11 @@ def main():
                 copy_in(i + 1)
             with torch.cuda.stream(s_cmp):
                 s_cmp.wait_event(in_done[i])
-                t = {k: bufs[i % 2][k].detach().requires_grad_(k in leaves) for k in names}
-                out = step(t)
-                out.backward(t["dout"])
-                res = [out.detach()] + [t[k].grad for k in leaves]
+                t = {k: bufs[i % 2][k].detach().requires_grad_(backward and k in leaves) for k in names}
+                out, ls = run_step(t)
+                res = [out.detach()] + ([ls] if ls is not None else [])
+                if backward:
+                    res += [t[k].grad for k in leaves]
                 cmp_done[i] = torch.cuda.Event()
                 cmp_done[i].record(s_cmp)
             if not outs_host:
@@ -867,12 +1091,18 @@ def main():
         e2e_ms = float(tt.item())
     e2e_value = tokens_job / (e2e_ms / 1e3)
 
+    # ---- shard verification (N > 1, outside every timed region): the shards are NCCL
+    # all-gathered and each one's sampled rows are checked against the CPU oracle on its owner
+    verification = None
     if world > 1:
+        verification = verify_shards(x, host, shape, rank, world, dev, step, backward)
         dist.destroy_process_group()
     if rank != 0:
         return 0
 
-    fwd_bytes, bwd_bytes = algorithmic_bytes(b, d, L, n)
+    fwd_bytes, bwd_bytes = algorithmic_bytes(b, d, L, n, ES[shape["dtype"]], with_z, last)
+    if not backward:
+        bwd_bytes = 0
     peak, peak_kind = load_peaks()
     dom_ms, dom_bytes, dom = (bwd_ms, bwd_bytes, "ss_bwd_kernel") if bwd_ms >= fwd_ms else (fwd_ms, fwd_bytes, "ss_fwd_kernel")
     achieved = dom_bytes / (dom_ms / 1e3) / 1e9
@@ -880,20 +1110,27 @@ def main():
     line = {
         "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": K, "warmup": a.warmup,
         "ms_per_step": ms_step, "higher_is_better": True, "scaling": shape["scaling"], "vs_baseline": None,
-        "dtype": "bf16", "data": "synthetic", "config": config_dict(world, shape),
+        "dtype": shape["dtype"], "data": "synthetic", "config": config_dict(world, shape),
         "hbm_gbs_step": step_gbs, "hbm_frac_step": step_gbs / peak, "hbm_frac_step_nominal_8tbs": step_gbs / 8000.0,
         "kernels_ms": {"fwd": fwd_ms, "bwd": bwd_ms},
         "roofline": {"kernel": dom, "bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                      "frac": achieved / peak, "peak_source": peak_kind,
                      "algorithmic_bytes_per_launch": dom_bytes,
-                     "traffic": profile_traffic() if a.workload == "scan" else None},
+                     "traffic": profile_traffic(a.workload, dom)},
         "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "pipeline": "copy-in, compute and copy-out of consecutive steps on three streams",
                 "ms_per_step": e2e_ms},
-        "gpu_launches": 2 * K,
+        "gpu_launches": launches_per_step(d, n, backward) * K,
         "clocks": clk.summary(),
     }
-    line["compute"] = compute_floor(b, d, L, n, ms_step, line["clocks"].get("sm_mhz"))
+    line["compute"] = compute_floor(b, d, L, n, ms_step, line["clocks"].get("sm_mhz"), with_z, backward)
+    if verification is not None:
+        line["verification"] = verification
+    if world == 1 and not a.no_reference_ext:
+        try:
+            line["reference_ext"] = reference_ext_compare(shape, dev, backward)
+        except Exception as e:  # a reported comparison, never required
+            line["reference_ext"] = {"unavailable": repr(e)}
     if world == 1 and not a.no_cpu_baseline:
         try:
             v, thr, sample, _ = cpu_sample_rate(b * d * L, b * L, a.cpu_seconds, shape=shape)
@@ -903,7 +1140,6 @@ def main():
                                     "sample": f"failed: {e!r}"}
     print(json.dumps(line), flush=True)
     return 0
-
 
 if __name__ == "__main__":
     sys.exit(main())

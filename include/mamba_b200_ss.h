@@ -53,7 +53,7 @@
 extern "C" {
 #endif
 
-#define SS_ABI_VERSION 7
+#define SS_ABI_VERSION 8
 /* the reference's kernels dispatch dstate up to 256 (csrc/selective_scan/static_switch.h:15-35) */
 #define SS_MAX_DSTATE 256
 #define SS_MAX_CONV_WIDTH 4
@@ -245,8 +245,11 @@ typedef struct ss_mamba_step_args {
 /* Number of fp32 elements of the forward-to-backward state buffer. */
 SS_API size_t ss_ckpt_elems(int batch, int dim, int seqlen, int dstate);
 
-/* Number of fp32 elements of the scratch ss_fwd_args.work must hold: 0 for dstate <= 16,
- * else 2 * batch * dim * seqlen (ss_fwd uses the first half, ss_bwd all of it). */
+/* Number of fp32 elements of the scratch ss_fwd_args.work holds.  dstate > 16: 2 * batch * dim *
+ * seqlen (ss_fwd uses the first half, ss_bwd all of it; required).  dstate <= 16: 0 when one
+ * CTA per (batch row, 32 channels) fills the GPU, else batch * K * (dstate + 1) * dim for the
+ * K time chunks the sequence is cut into (a summary per chunk); optional — a call without it
+ * scans each row in one piece.  Size it after any ss_set_time_chunks call. */
 SS_API size_t ss_work_elems(int batch, int dim, int seqlen, int dstate);
 
 /* Forward scan: out = (D*u + sum_n C*h) [* silu(z)], h_t = exp(delta'*A) h_{t-1} + delta'*u*B. */
@@ -261,9 +264,10 @@ SS_API int ss_bwd(const ss_bwd_args* args, void* stream);
  * the reference.  It ignores args->f.ckpt: it recomputes the forward states into a
  * state array held by the library (one per GPU that loads it, kept until exit) and runs
  * the backward from there, calling no allocator.  Limits: ss_ckpt_elems(...) of the call
- * must be <= SS_NOALLOC_MAX_CKPT_ELEMS, else SS_ERR_UNSUPPORTED.  The first call on a
- * device looks up that array's address (do it before any stream capture).  All calls on a
- * device share the array: calls that overlap on the GPU race.  du (and dz, with a gate)
+ * must be <= SS_NOALLOC_MAX_CKPT_ELEMS, else SS_ERR_UNSUPPORTED.  Every argument is checked
+ * before anything is launched.  The first call on a device (and the first after its CUDA
+ * context changes) looks up that array's address: make it before any stream capture.  All calls
+ * on a device share the array: calls that overlap on the GPU race.  du (and dz, with a gate)
  * receive the recomputed forward outputs before the backward overwrites them, so they must
  * not alias an input; args->y is ignored.  With dstate > 16 the caller's args->f.work
  * (ss_work_elems floats) is required, as for ss_bwd. */
@@ -302,6 +306,20 @@ SS_API int ss_last_cuda_error(void);
  * wait for a TMA tile gave up), or -1 if the status cannot be read.  Synchronizes `stream`;
  * reset != 0 clears the bits. */
 SS_API int ss_device_status(int reset, void* stream);
+
+/* Limit, in SM clock cycles, of every bounded wait the scan kernels make for a TMA tile, for
+ * the launches that follow from this process (all threads); returns the previous limit.
+ * cycles < 0 restores the default (4e9 cycles, about 2 s).  A wait that runs out raises bit 1
+ * of the device status (ss_device_status), lets the CTA's copies in flight land (bounded by
+ * the default) and ends the CTA, leaving its outputs incomplete.  No counterpart in the
+ * reference, whose kernels have no waits on memory copies. */
+SS_API long long ss_set_wait_limit(long long cycles);
+
+/* Time chunks per scan pass for the calls that follow from this process: 0 (the default)
+ * chooses them from the shape, k >= 1 forces min(k, tiles of 16 steps) whenever a workspace of
+ * ss_work_elems floats is given (1: never split).  Returns the previous setting.  A testing
+ * and tuning knob; no counterpart in the reference. */
+SS_API int ss_set_time_chunks(int chunks);
 
 /* SS_ABI_VERSION of the loaded library. */
 SS_API int ss_abi_version(void);

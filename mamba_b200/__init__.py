@@ -10,7 +10,10 @@ Public operators (all CUDA-only, backed by libmamba_b200_ss.so):
   rms_norm_fn, rms_norm                residual add + RMSNorm in one kernel (forward / backward)
   causal_lm_forward                    a CausalLM's forward through the fused block and norm
   generate, Decoder                    prefill + cached single-token decode (CUDA-graph step)
+  check_device_status                  raise if a kernel's bounded wait gave up since the last check
+  set_status_check                     check after every scan call (debugging; synchronises)
 """
+from ._lib import check_device_status, set_status_check
 from .decode import Decoder, generate
 from .inner import MambaInnerFn, mamba_inner_fn, mamba_simple_forward
 from .lm import causal_lm_forward
@@ -18,5 +21,6 @@ from .norm import rms_norm, rms_norm_fn
 from .selective_scan_interface import SelectiveScanFn, selective_scan_fn, selective_state_update
 
 __all__ = ["SelectiveScanFn", "selective_scan_fn", "selective_state_update", "MambaInnerFn", "mamba_inner_fn",
-           "mamba_simple_forward", "rms_norm_fn", "rms_norm", "causal_lm_forward", "generate", "Decoder"]
+           "mamba_simple_forward", "rms_norm_fn", "rms_norm", "causal_lm_forward", "generate", "Decoder",
+           "check_device_status", "set_status_check"]
 __version__ = "0.1.0"

@@ -142,13 +142,13 @@ class MambaStepArgs(ctypes.Structure):
 # ss_struct_size index order
 STRUCTS = (FwdArgs, BwdArgs, StepArgs, ConvArgs, ConvBwdArgs, ConvStepArgs, RmsNormArgs, RmsNormBwdArgs,
            MambaStepArgs)
-ABI_VERSION = 7
+ABI_VERSION = 8
 MAX_CONV_WIDTH = 4
 
 EXPORTS = ("ss_fwd", "ss_bwd", "ss_step", "ss_ckpt_elems", "ss_work_elems", "ss_status_string",
            "ss_last_cuda_error", "ss_abi_version", "ss_struct_size", "ss_device_status",
            "ss_bwd_noalloc", "ss_conv_fwd", "ss_conv_bwd", "ss_conv_step", "ss_rmsnorm_fwd", "ss_rmsnorm_bwd",
-           "ss_mamba_step")
+           "ss_mamba_step", "ss_set_wait_limit", "ss_set_time_chunks")
 NOALLOC_MAX_CKPT_ELEMS = 4194304  # SS_NOALLOC_MAX_CKPT_ELEMS
 
 _lib = None
@@ -179,7 +179,7 @@ def lib():
                 L.ss_mamba_step.argtypes = [ctypes.POINTER(MambaStepArgs), c_vp]
                 for f in ("ss_fwd", "ss_bwd", "ss_step", "ss_last_cuda_error", "ss_abi_version",
                           "ss_conv_fwd", "ss_conv_bwd", "ss_conv_step", "ss_rmsnorm_fwd", "ss_rmsnorm_bwd",
-                          "ss_mamba_step"):
+                          "ss_mamba_step", "ss_set_wait_limit", "ss_set_time_chunks"):
                     getattr(L, f).restype = c_int
                 L.ss_ckpt_elems.argtypes = [c_int, c_int, c_int, c_int]
                 L.ss_ckpt_elems.restype = ctypes.c_size_t
@@ -189,6 +189,10 @@ def lib():
                 L.ss_status_string.restype = ctypes.c_char_p
                 L.ss_device_status.argtypes = [c_int, c_vp]
                 L.ss_device_status.restype = c_int
+                L.ss_set_time_chunks.argtypes = [c_int]
+                L.ss_set_time_chunks.restype = c_int
+                L.ss_set_wait_limit.argtypes = [ctypes.c_longlong]
+                L.ss_set_wait_limit.restype = ctypes.c_longlong
                 L.ss_struct_size.argtypes = [c_int]
                 L.ss_struct_size.restype = ctypes.c_size_t
                 if L.ss_abi_version() != ABI_VERSION:
@@ -238,10 +242,58 @@ def device_status(device, reset: bool = True) -> int:
         return int(lib().ss_device_status(int(reset), stream_of(torch.device(device))))
 
 
+STATUS_BITS = {1: "a bounded wait for a TMA tile gave up (the CTA ended early; its outputs are incomplete)"}
+
+
+def check_device_status(device=None, what: str = "mamba_b200") -> None:
+    """Raise RuntimeError if any kernel on `device` (default: the current one) raised an error bit
+    since the last check; clears the bits.  Synchronises the current stream."""
+    import torch
+
+    dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    bits = device_status(dev, reset=True)
+    if bits < 0:
+        raise RuntimeError(f"{what}: the device status word of {dev} could not be read")
+    if bits:
+        why = "; ".join(v for k, v in STATUS_BITS.items() if bits & k) or "unknown bits"
+        raise RuntimeError(f"{what}: kernel error status 0x{bits:x} on {dev}: {why}")
+
+
+# Per-call status checks: off by default (each check synchronises the stream); on with
+# set_status_check(True) or MAMBA_B200_CHECK_STATUS=1 in the environment.
+_status_check = os.environ.get("MAMBA_B200_CHECK_STATUS", "0") not in ("", "0")
+
+
+def set_status_check(enabled: bool) -> bool:
+    """Check the device status word after every scan call (raising on an error bit); returns the
+    previous setting.  Each check synchronises the stream, so it is a debugging aid."""
+    global _status_check
+    prev, _status_check = _status_check, bool(enabled)
+    return prev
+
+
+def maybe_check_status(device, what: str) -> None:
+    if _status_check:
+        check_device_status(device, what)
+
+
+def set_wait_limit(cycles: int) -> int:
+    """Limit (SM clock cycles) of the scan kernels' bounded waits for a TMA tile, for the launches
+    that follow; returns the previous one.  cycles < 0 restores the default (~2 s)."""
+    return int(lib().ss_set_wait_limit(int(cycles)))
+
+
+def set_time_chunks(chunks: int) -> int:
+    """Time chunks per scan pass for the calls that follow (0: chosen from the shape; k >= 1:
+    forced, 1 = never split).  Returns the previous setting."""
+    return int(lib().ss_set_time_chunks(int(chunks)))
+
+
 def ckpt_elems(batch, dim, seqlen, dstate) -> int:
     return int(lib().ss_ckpt_elems(batch, dim, seqlen, dstate))
 
 
 def work_elems(batch, dim, seqlen, dstate) -> int:
-    """fp32 scratch a scan call needs (0 for dstate <= 16)."""
+    """fp32 scratch of a scan call: the state groups' sums (dstate > 16) or the time chunks'
+    summaries (dstate <= 16 when the sequence is split; 0 otherwise)."""
     return int(lib().ss_work_elems(batch, dim, seqlen, dstate))

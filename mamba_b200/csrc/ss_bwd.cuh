@@ -92,8 +92,10 @@ __global__ void __launch_bounds__(32 * kNW, 3) ss_bwd_kernel(const __grid_consta
   const ss_fwd_args& f = a.f;
 
   const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
-  const int ctile = blockIdx.x % P.nct;
-  const int bsg = blockIdx.x / P.nct;
+  const int chunk = blockIdx.x % P.nchunk;
+  const int cta = blockIdx.x / P.nchunk;
+  const int ctile = cta % P.nct;
+  const int bsg = cta / P.nct;
   const int sg = bsg % P.nsg;            // state group: states n0 .. n0 + 15
   const int b = bsg / P.nsg;
   const int grp = ctile / P.tpg;
@@ -128,6 +130,24 @@ __global__ void __launch_bounds__(32 * kNW, 3) ss_bwd_kernel(const __grid_consta
     Cc[p] = make_float2(cv[0], cv[1]);
     dA2[p] = e2[p] = dBc[p] = dCc[p] = make_float2(0.f, 0.f);
   }
+  // a time chunk before the last starts from the carry the later chunks send back: chunk j
+  // maps an incoming carry E to exp(A sum_j delta') E + (its local carry), folded over the
+  // chunks after this one, last first
+  if (chunk < P.nchunk - 1 && lane_ok) {
+    for (int j = P.nchunk - 1; j > chunk; --j) {
+      const int64_t bj = (int64_t)b * P.nchunk + j;
+      const float sdt = P.csum[bj * f.dim + c];
+      const float* cc = P.ccarry + (bj * N + kSPW * w) * (int64_t)f.dim + c;
+#pragma unroll
+      for (int p = 0; p < 2; ++p) {
+        const bool ok0 = kSPW * w + 2 * p < N, ok1 = kSPW * w + 2 * p + 1 < N;
+        const float e0 = ok0 ? cc[(int64_t)(2 * p) * f.dim] : 0.f;
+        const float e1 = ok1 ? cc[(int64_t)(2 * p + 1) * f.dim] : 0.f;
+        e2[p].x = fmaf(ex2(A2[p].x * sdt), e2[p].x, e0);
+        e2[p].y = fmaf(ex2(A2[p].y * sdt), e2[p].y, e1);
+      }
+    }
+  }
 
   // ---- element role
   const int pc = tid / kNW, pq = tid % kNW;
@@ -147,12 +167,14 @@ __global__ void __launch_bounds__(32 * kNW, 3) ss_bwd_kernel(const __grid_consta
   const int64_t bc_off = (((int64_t)b * f.ngroups + grp) * N + n0) * (int64_t)L;  // row n0 of this group
 
   const int ntiles = P.ntiles;
+  const int kb = chunk * P.chunk_tiles;              // this CTA's tiles: kb .. kb + nt - 1
+  const int nt = min(ntiles, kb + P.chunk_tiles) - kb;
   const uint32_t io_bytes = kCh * kTile * (uint32_t)sizeof(IT);
   const uint32_t bc_bytes = NS * kTile * (uint32_t)sizeof(IT);
   const uint32_t h_bytes = NS * kCh * 4u;
-  // iteration i handles tile ntiles-1-i
+  // local iteration i handles tile kb + nt - 1 - i
   auto issue = [&](int i, int s) {
-    const int k = ntiles - 1 - i;
+    const int k = kb + nt - 1 - i;
     uint64_t* bar = &sm.full[s];
     const uint32_t bytes = (3 + (kHasZ ? (kMulti ? 1 : 2) : 0)) * io_bytes +
                            ((kVarB ? 1 : 0) + (kVarC ? 1 : 0)) * bc_bytes + (k > 0 ? h_bytes : 0u);
@@ -176,18 +198,18 @@ __global__ void __launch_bounds__(32 * kNW, 3) ss_bwd_kernel(const __grid_consta
     }
     __syncthreads();
     if (tid == 0)
-      for (int s = 0; s < kStagesBwd<IT> && s < ntiles; ++s) issue(s, s);
+      for (int s = 0; s < kStagesBwd<IT> && s < nt; ++s) issue(s, s);
   }
 
-  for (int it = 0; it < ntiles; ++it) {
-    const int k = ntiles - 1 - it;
+  for (int it = 0; it < nt; ++it) {
+    const int k = kb + nt - 1 - it;
     const int t0 = k * kTile;
     const int tlen = min(kTile, L - t0);
     const int stg = kTMA ? it % kStagesBwd<IT> : 0;
     bool failed = false;
     float2 hp[kTile + 1][2];
     if constexpr (kTMA) {
-      failed = !mbar_wait_bounded(&sm.full[stg], (it / kStagesBwd<IT>) & 1);
+      failed = !mbar_wait_bounded(&sm.full[stg], (it / kStagesBwd<IT>) & 1, P.wait_cycles);
       if (w == 0) widen_bc_warp<IT, NS, kVarB, kVarC>(sm.B_s, sm.C_s, sm.Braw[stg], sm.Craw[stg], false, lane);
 #pragma unroll
       for (int p = 0; p < 2; ++p)
@@ -267,10 +289,12 @@ __global__ void __launch_bounds__(32 * kNW, 3) ss_bwd_kernel(const __grid_consta
       }
     }
     if (__syncthreads_or(failed)) {
+      // a TMA stage did not complete in time: report, let every copy in flight land (this
+      // tile's included: tiles it .. it + kStagesBwd - 1 were issued), and leave
       if (tid == 0) {
         if (P.status != nullptr) atomicOr(P.status, kStatusTimeout);
-        for (int j = it + 1; j < ntiles && j < it + kStagesBwd<IT>; ++j)
-          mbar_wait_bounded(&sm.full[j % kStagesBwd<IT>], (j / kStagesBwd<IT>) & 1);
+        for (int j = it; j < nt && j < it + kStagesBwd<IT>; ++j)
+          mbar_wait_bounded(&sm.full[j % kStagesBwd<IT>], (j / kStagesBwd<IT>) & 1, kWaitCycles);
       }
       __syncthreads();
       return;
@@ -456,7 +480,7 @@ __global__ void __launch_bounds__(32 * kNW, 3) ss_bwd_kernel(const __grid_consta
     }
     __syncthreads();
     if constexpr (kTMA) {
-      if (tid == 0 && it + kStagesBwd<IT> < ntiles) issue(it + kStagesBwd<IT>, stg);
+      if (tid == 0 && it + kStagesBwd<IT> < nt) issue(it + kStagesBwd<IT>, stg);
     }
   }
 

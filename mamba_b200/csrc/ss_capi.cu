@@ -7,7 +7,12 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <algorithm>
+#include <array>
+#include <atomic>
+#include <cmath>
 #include <mutex>
+#include <unordered_map>
 
 #include "../../include/mamba_b200_ss.h"
 #include "ss_common.cuh"
@@ -25,6 +30,10 @@ __device__ int g_ss_status;
 
 namespace {
 thread_local int g_last_cuda = 0;
+// limit of the kernels' bounded waits for a TMA tile, for launches from this process
+std::atomic<long long> g_wait_cycles{ssb::kWaitCycles};
+// time chunks per scan pass: 0 chooses them from the shape (chunk_count below)
+std::atomic<int> g_time_chunks{0};
 }  // namespace
 
 // shared with the other translation units of the library (hidden visibility)
@@ -150,6 +159,70 @@ void derive(const ss_fwd_args& a, K& P) {
   P.nct = a.ngroups * P.tpg;
   P.nsg = ssb::state_groups(a.dstate);
   P.ntiles = (a.seqlen + ssb::kTile - 1) / ssb::kTile;
+  P.nchunk = 1;  // one chunk: the whole sequence (set_chunks may split it)
+  P.chunk_tiles = P.ntiles;
+}
+
+// ---- time chunks.  A scan pass runs one CTA per (batch row, 32-channel tile); when that grid
+// cannot fill the GPU the sequence is cut into chunks (ss_chunk.cuh), which costs a summary
+// pass over all but one chunk (about half a forward, a fifth of a backward) and buys
+// parallelism.  The count minimises a wave model of the pass:
+//     time(K) ~ ceil(ctas K / slots) / K * (1 + extra (K - 1) / K)
+// (slots = SMs x CTAs resident per SM): its minimum, used only when the model gains >= 15 %.
+// Measured on a B200 (forced counts): the forward of batch 2 x 1536 channels x 2048 steps
+// takes 0.177 ms whole and 0.10 ms at 4 - 16 chunks; batch 1 x 5120 x 32768 steps 3.29 ms
+// whole and 1.95 - 2.03 ms at 8 - 48 chunks; batch 8 x 1536 x 2048 (384 CTAs) is slower split.
+constexpr int kSMs = 148;            // B200
+constexpr int kMinChunkTiles = 8;    // >= 128 steps per chunk
+constexpr int kMaxChunks = 64;
+
+int chunk_count(int64_t ctas, int ntiles, int ctas_per_sm, double extra) {
+  const int forced = g_time_chunks.load(std::memory_order_relaxed);
+  if (forced > 0) return std::max(1, std::min(forced, ntiles));
+  const int kmax = (int)std::min<int64_t>(kMaxChunks, ntiles / kMinChunkTiles);
+  if (kmax < 2 || ctas <= 0) return 1;
+  const double slots = (double)kSMs * ctas_per_sm;
+  double tmin = 1.0;
+  int best = 1;
+  for (int k = 2; k <= kmax; ++k) {
+    const double t = std::ceil((double)ctas * k / slots) / k * (1.0 + extra * (k - 1) / k);
+    if (t < tmin) {
+      tmin = t;
+      best = k;
+    }
+  }
+  return tmin > 0.85 ? 1 : best;
+}
+
+int64_t channel_tiles(int dim, int ngroups) {
+  const int64_t dpg = dim / ngroups;
+  return (int64_t)ngroups * ((dpg + ssb::kCh - 1) / ssb::kCh);
+}
+// forward: 4 CTAs per SM; its chunk pass costs about half the forward
+int fwd_chunk_count(int batch, int64_t nct, int ntiles) { return chunk_count((int64_t)batch * nct, ntiles, 4, 0.5); }
+// backward: 3 CTAs per SM; its carry pass costs about a fifth of the backward
+int bwd_chunk_count(int batch, int64_t nct, int ntiles) { return chunk_count((int64_t)batch * nct, ntiles, 3, 0.2); }
+// chunks the workspace of ss_work_elems holds (the larger pass, channel tiles of one group)
+int sized_chunks(int batch, int dim, int seqlen, int dstate) {
+  if (batch <= 0 || dim <= 0 || seqlen <= 0 || dstate > ssb::kGroupStates) return 1;
+  const int ntiles = (seqlen + ssb::kTile - 1) / ssb::kTile;
+  const int64_t nct = channel_tiles(dim, 1);
+  return std::max(fwd_chunk_count(batch, nct, ntiles), bwd_chunk_count(batch, nct, ntiles));
+}
+
+// Splits a pass into chunks when the workspace allows: K from `want`, capped by what the
+// workspace holds; chunk_tiles such that no chunk is empty.  Returns the chunk count.
+template <typename K>
+int set_chunks(K& P, int want, const ss_fwd_args& a) {
+  P.nchunk = 1;
+  P.chunk_tiles = P.ntiles;
+  const int64_t ctas = std::max<int64_t>(1, (int64_t)a.batch * P.nct);
+  const int k = (int)std::min<int64_t>(std::min(want, sized_chunks(a.batch, a.dim, a.seqlen, a.dstate)),
+                                       kMaxGrid / ctas);
+  if (k <= 1 || a.work == nullptr || P.nsg != 1) return 1;
+  P.chunk_tiles = (P.ntiles + k - 1) / k;
+  P.nchunk = (P.ntiles + P.chunk_tiles - 1) / P.chunk_tiles;
+  return P.nchunk;
 }
 
 template <typename F>
@@ -164,6 +237,48 @@ int dispatch(int io, F&& f) {
 
 }  // namespace
 
+cudaError_t ssb::ensure_smem_limit(const void* fn, size_t smem) {
+  if (smem <= 48 * 1024) return cudaSuccess;
+  int dev = -1;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  static std::mutex mu;
+  static std::unordered_map<const void*, std::array<size_t, 64>> done;  // limit set, per device
+  if (dev >= 0 && dev < 64) {
+    std::lock_guard<std::mutex> lock(mu);
+    if (done[fn][dev] >= smem) return cudaSuccess;
+  }
+  e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e == cudaSuccess && dev >= 0 && dev < 64) {
+    std::lock_guard<std::mutex> lock(mu);
+    done[fn][dev] = std::max(done[fn][dev], smem);
+  }
+  return e;
+}
+
+// Argument checks of a backward call (shared with ss_bwd_noalloc, which makes them before it
+// launches anything).  own_states: the caller recomputes the forward's states and ungated
+// output itself, so f.ckpt and y are not required.
+int ssb::check_bwd(const ss_bwd_args* args, bool own_states) {
+  if (args == nullptr) return SS_ERR_INVALID;
+  const ss_fwd_args& f = args->f;
+  int rc = check_fwd(&f);
+  if (rc != SS_OK) return rc;
+  // with no batch rows or no steps the (batch, dim, seqlen) tensors and variable dB / dC are empty
+  const bool empty = f.batch == 0 || f.seqlen == 0;
+  if (!args->dA || (!f.var_B && !args->dB) || (!f.var_C && !args->dC)) return SS_ERR_INVALID;
+  if (!empty && (!args->dout || !args->du || !args->ddelta || !args->dB || !args->dC)) return SS_ERR_INVALID;
+  if (f.z && !empty && (!args->dz || (!own_states && !args->y))) return SS_ERR_INVALID;
+  if (!own_states && !f.ckpt && f.seqlen > kTile && f.batch > 0) return SS_ERR_INVALID;
+  if (args->dout_batch_stride < 0 || args->dout_dim_stride < 0 || args->du_batch_stride < 0 ||
+      args->du_dim_stride < 0 || args->ddelta_batch_stride < 0 || args->ddelta_dim_stride < 0)
+    return SS_ERR_INVALID;
+  if (f.z && (args->dz_batch_stride < 0 || args->dz_dim_stride < 0 ||
+              (!own_states && (args->y_batch_stride < 0 || args->y_dim_stride < 0))))
+    return SS_ERR_INVALID;
+  return SS_OK;
+}
+
 extern "C" {
 
 size_t ss_ckpt_elems(int batch, int dim, int seqlen, int dstate) {
@@ -173,8 +288,11 @@ size_t ss_ckpt_elems(int batch, int dim, int seqlen, int dstate) {
 }
 
 size_t ss_work_elems(int batch, int dim, int seqlen, int dstate) {
-  if (batch <= 0 || dim <= 0 || seqlen <= 0 || dstate <= ssb::kGroupStates) return 0;
-  return 2 * (size_t)batch * (size_t)dim * (size_t)seqlen;
+  if (batch <= 0 || dim <= 0 || seqlen <= 0) return 0;
+  if (dstate > ssb::kGroupStates) return 2 * (size_t)batch * (size_t)dim * (size_t)seqlen;
+  // time chunks: per chunk a state (or carry) per (channel, state) and a sum of delta' per channel
+  const int k = sized_chunks(batch, dim, seqlen, dstate);
+  return k > 1 ? (size_t)batch * k * ((size_t)dstate + 1) * (size_t)dim : 0;
 }
 
 int ss_fwd(const ss_fwd_args* args, void* stream) {
@@ -199,27 +317,25 @@ int ss_fwd(const ss_fwd_args* args, void* stream) {
   P.vec_y = args->out_y ? rows16(args->out_y, args->out_y_batch_stride, args->out_y_dim_stride, es) : 0;
   P.vec_work = args->work != nullptr && (reinterpret_cast<uintptr_t>(args->work) & 15) == 0 && (args->seqlen % 4) == 0;
   P.status = status_ptr();
+  P.wait_cycles = g_wait_cycles.load(std::memory_order_relaxed);
   const ss_fwd_args& a = *args;
   bool tma = map_rows(&P.tm_u, a.u, a.io_dtype, a, a.u_batch_stride, a.u_dim_stride) &&
              map_rows(&P.tm_d, a.delta, a.io_dtype, a, a.delta_batch_stride, a.delta_dim_stride);
   if (tma && a.z) tma = map_rows(&P.tm_z, a.z, a.io_dtype, a, a.z_batch_stride, a.z_dim_stride);
   if (tma && a.var_B) tma = map_bc(&P.tm_B, a.B, a);
   if (tma && a.var_C) tma = map_bc(&P.tm_C, a.C, a);
+  if (tma && set_chunks(P, fwd_chunk_count(a.batch, P.nct, P.ntiles), a) > 1) {
+    P.cstate = a.work;
+    P.csum = a.work + (size_t)a.batch * P.nchunk * a.dstate * (size_t)a.dim;
+  }
   cudaStream_t st = (cudaStream_t)stream;
   return dispatch(args->io_dtype, [&](auto tag) { return ssb::launch_fwd<decltype(tag)>(P, st, tma); });
 }
 
 int ss_bwd(const ss_bwd_args* args, void* stream) {
-  if (args == nullptr) return SS_ERR_INVALID;
-  const ss_fwd_args& f = args->f;
-  int rc = check_fwd(&f);
+  int rc = ssb::check_bwd(args, false);
   if (rc != SS_OK) return rc;
-  // with no batch rows or no steps the (batch, dim, seqlen) tensors and variable dB / dC are empty
-  const bool empty = f.batch == 0 || f.seqlen == 0;
-  if (!args->dA || (!f.var_B && !args->dB) || (!f.var_C && !args->dC)) return SS_ERR_INVALID;
-  if (!empty && (!args->dout || !args->du || !args->ddelta || !args->dB || !args->dC)) return SS_ERR_INVALID;
-  if (f.z && !empty && (!args->dz || !args->y)) return SS_ERR_INVALID;
-  if (!f.ckpt && f.seqlen > ssb::kTile && f.batch > 0) return SS_ERR_INVALID;
+  const ss_fwd_args& f = args->f;
   cudaStream_t st = (cudaStream_t)stream;
   // accumulated outputs start from zero
   const size_t nA = (size_t)f.dim * f.dstate;
@@ -248,6 +364,7 @@ int ss_bwd(const ss_bwd_args* args, void* stream) {
   P.vec_dbc = (f.seqlen % 4) == 0 && (reinterpret_cast<uintptr_t>(args->dB) & 15) == 0 &&
               (reinterpret_cast<uintptr_t>(args->dC) & 15) == 0;
   P.status = status_ptr();
+  P.wait_cycles = g_wait_cycles.load(std::memory_order_relaxed);
   // the checkpoint tile starts at channel c0: TMA needs c0 * 4 bytes to be 16-byte aligned;
   // the TMA ring stages B / C in the I/O dtype
   bool tma = (f.ngroups == 1 || (P.dpg % 4) == 0) && (f.bc_dtype == f.io_dtype || (!f.var_B && !f.var_C)) &&
@@ -265,6 +382,10 @@ int ss_bwd(const ss_bwd_args* args, void* stream) {
                (uint64_t)f.dim * 4, (uint64_t)f.dim * f.dstate * 4, ssb::kCh, ns);
   } else if (tma && P.ntiles > 1) {
     tma = false;
+  }
+  if (tma && set_chunks(P, bwd_chunk_count(f.batch, P.nct, P.ntiles), f) > 1) {
+    P.ccarry = f.work;
+    P.csum = f.work + (size_t)f.batch * P.nchunk * f.dstate * (size_t)f.dim;
   }
   return dispatch(f.io_dtype, [&](auto tag) { return ssb::launch_bwd<decltype(tag)>(P, st, tma); });
 }
@@ -302,6 +423,12 @@ const char* ss_status_string(int s) {
 int ss_last_cuda_error(void) { return g_last_cuda; }
 
 int ss_abi_version(void) { return SS_ABI_VERSION; }
+
+int ss_set_time_chunks(int chunks) { return g_time_chunks.exchange(chunks > 0 ? chunks : 0); }
+
+long long ss_set_wait_limit(long long cycles) {
+  return g_wait_cycles.exchange(cycles < 0 ? ssb::kWaitCycles : cycles);
+}
 
 int ss_device_status(int reset, void* stream) {
   int* p = status_ptr();

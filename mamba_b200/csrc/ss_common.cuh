@@ -26,6 +26,11 @@ namespace ssb {
 
 // Records e as the thread's last CUDA error (ss_last_cuda_error) and maps it to a status.
 int record_cuda_status(cudaError_t e);
+// Argument checks of a backward call (ss_capi.cu); own_states: f.ckpt and y not required.
+int check_bwd(const ss_bwd_args* args, bool own_states);
+// Raises the dynamic shared-memory limit of kernel `fn` to `smem` bytes (when above the 48 KB
+// default) once per (device, kernel): setting the attribute on every launch costs host time.
+cudaError_t ensure_smem_limit(const void* fn, size_t smem);
 
 
 constexpr int kTile = 16;   // time steps per tile = checkpoint interval
@@ -37,7 +42,10 @@ constexpr float kLog2e = 1.4426950408889634f;
 
 // device status word codes (OR-ed into the caller-visible status buffer)
 constexpr int kStatusTimeout = 1;   // a bounded wait on a TMA barrier gave up
-constexpr long long kWaitCycles = 4000000000LL;  // ~2 s at 1.9 GHz
+// default limit of a bounded wait for a TMA tile (SM clock cycles, ~2 s at 1.9 GHz); a launch
+// takes its limit from ss_set_wait_limit.  The drain after a timeout (waiting for the CTA's
+// own copies still in flight before it exits) always uses the default.
+constexpr long long kWaitCycles = 4000000000LL;
 
 // ---- scalar conversions -----------------------------------------------------------
 template <typename T> __device__ __forceinline__ float to_f(T x);
@@ -176,12 +184,24 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
-// Wait for the phase `parity` of an mbarrier, giving up after ~kWaitCycles.
-__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity) {
+// non-blocking probe of the phase `parity` (try_wait may suspend the thread for a while)
+__device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Wait for the phase `parity` of an mbarrier, giving up after `limit` SM clock cycles; a limit
+// <= 0 only probes (non-blocking), so a tile that has not landed yet counts as a timeout.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, long long limit) {
+  if (limit <= 0) return mbar_test_wait(bar, parity);
   if (mbar_try_wait(bar, parity)) return true;
   const long long t0 = clock64();
   while (!mbar_try_wait(bar, parity)) {
-    if (clock64() - t0 > kWaitCycles) return false;
+    if (clock64() - t0 > limit) return false;
   }
   return true;
 }
@@ -290,6 +310,14 @@ struct FwdK {
   int vec_u, vec_d, vec_z, vec_out, vec_y;
   int vec_work;   // workspace rows are 16-byte aligned (seqlen % 4 == 0)
   int* status;    // device status word (kStatus* bits), nullable
+  long long wait_cycles;  // limit of a bounded wait for a TMA tile
+  // time chunks (dstate <= 16, TMA path): the sequence splits into nchunk chunks of
+  // chunk_tiles tiles, one CTA per (batch row, channel tile, chunk); chunk j's local end state
+  // (from a zero state) is cstate[b][j][n][c] and its sum of delta' csum[b][j][c], both written
+  // by ss_fwd_chunk_kernel for j < nchunk - 1 (pointers into the caller's workspace)
+  int nchunk, chunk_tiles;
+  float* cstate;
+  float* csum;
 };
 
 struct BwdK {
@@ -299,6 +327,13 @@ struct BwdK {
   int vec_u, vec_d, vec_z, vec_dout, vec_du, vec_dd, vec_dz, vec_y;
   int vec_dbc;    // dB/dC rows are 16-byte aligned (seqlen % 4 == 0)
   int* status;
+  long long wait_cycles;
+  // time chunks, as in FwdK: chunk j's local carry into the step before it (the reverse
+  // recurrence run over the chunk from a zero carry) is ccarry[b][j][n][c] and its sum of
+  // delta' csum[b][j][c], both written by ss_bwd_carry_kernel for j >= 1
+  int nchunk, chunk_tiles;
+  float* ccarry;
+  float* csum;
 };
 
 constexpr int kGroupStates = 16;  // states per CTA when dstate > 16 (4 warps x 4)

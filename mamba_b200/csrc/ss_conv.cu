@@ -94,7 +94,7 @@ int ss_conv_fwd(const ss_conv_args* a, void* stream) {
       constexpr int KK = decltype(kc)::value;
       const size_t smem = sizeof(ConvFwdSmem<IT, KK>);
       auto kern = a->z ? conv_fwd_kernel<IT, KK, true> : conv_fwd_kernel<IT, KK, false>;
-      cudaError_t e2 = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      cudaError_t e2 = ensure_smem_limit(reinterpret_cast<const void*>(kern), smem);
       if (e2 != cudaSuccess) return e2;
       kern<<<grid, kConvThreads, smem, st>>>(P);
       return cudaGetLastError();
@@ -137,7 +137,7 @@ int ss_conv_bwd(const ss_conv_bwd_args* a, void* stream) {
       constexpr int KK = decltype(kc)::value;
       const size_t smem = sizeof(ConvBwdSmem<IT, KK>);
       auto kern = a->dzt ? conv_bwd_kernel<IT, KK, true> : conv_bwd_kernel<IT, KK, false>;
-      cudaError_t e2 = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      cudaError_t e2 = ensure_smem_limit(reinterpret_cast<const void*>(kern), smem);
       if (e2 != cudaSuccess) return e2;
       kern<<<grid, kConvThreads, smem, st>>>(P);
       return cudaGetLastError();

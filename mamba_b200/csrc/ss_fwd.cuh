@@ -100,8 +100,10 @@ __global__ void __launch_bounds__(32 * kNW, 4) ss_fwd_kernel(const __grid_consta
   const ss_fwd_args& a = P.a;
 
   const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
-  const int ctile = blockIdx.x % P.nct;
-  const int bsg = blockIdx.x / P.nct;
+  const int chunk = blockIdx.x % P.nchunk;
+  const int cta = blockIdx.x / P.nchunk;
+  const int ctile = cta % P.nct;
+  const int bsg = cta / P.nct;
   const int sg = bsg % P.nsg;            // state group: states n0 .. n0 + 15
   const int b = bsg / P.nsg;
   const int grp = ctile / P.tpg;
@@ -112,6 +114,8 @@ __global__ void __launch_bounds__(32 * kNW, 4) ss_fwd_kernel(const __grid_consta
   const int N = a.dstate, L = a.seqlen;
   const bool bc_f32 = a.bc_dtype == SS_F32;
   const int ntiles = P.ntiles;
+  const int kb = chunk * P.chunk_tiles;              // this CTA's tiles: kb .. kb + nt - 1
+  const int nt = min(ntiles, kb + P.chunk_tiles) - kb;
 
   // ---- scan role: channel c0 + lane, states kSPW*w + j
   const bool lane_ok = lane < nvalid;
@@ -136,6 +140,23 @@ __global__ void __launch_bounds__(32 * kNW, 4) ss_fwd_kernel(const __grid_consta
     Cc[p] = make_float2(cv[0], cv[1]);
     h[p] = make_float2(0.f, 0.f);
   }
+  // a later time chunk starts from the state the earlier chunks leave behind: chunk j maps a
+  // start state H to exp(A sum_j delta') H + (its local end state), folded over j < chunk
+  if (chunk > 0 && lane_ok) {
+    for (int j = 0; j < chunk; ++j) {
+      const int64_t bj = (int64_t)b * P.nchunk + j;
+      const float sdt = P.csum[bj * a.dim + c];
+      const float* cs = P.cstate + (bj * N + kSPW * w) * (int64_t)a.dim + c;
+#pragma unroll
+      for (int p = 0; p < 2; ++p) {
+        const bool ok0 = kSPW * w + 2 * p < N, ok1 = kSPW * w + 2 * p + 1 < N;
+        const float s0 = ok0 ? cs[(int64_t)(2 * p) * a.dim] : 0.f;
+        const float s1 = ok1 ? cs[(int64_t)(2 * p + 1) * a.dim] : 0.f;
+        h[p].x = fmaf(ex2(A2[p].x * sdt), h[p].x, s0);
+        h[p].y = fmaf(ex2(A2[p].y * sdt), h[p].y, s1);
+      }
+    }
+  }
 
   // ---- element role: channel c0 + pc, steps pq*S .. pq*S + S - 1 of each tile
   const int pc = tid / kNW, pq = tid % kNW;
@@ -152,10 +173,10 @@ __global__ void __launch_bounds__(32 * kNW, 4) ss_fwd_kernel(const __grid_consta
   const uint32_t bc_bytes = NS * kTile * (bc_f32 ? 4u : (uint32_t)sizeof(IT));
   const uint32_t stage_bytes = (2 + (kHasZ ? 1 : 0)) * kCh * kTile * (uint32_t)sizeof(IT) +
                                ((kVarB ? 1 : 0) + (kVarC ? 1 : 0)) * bc_bytes;
-  auto issue = [&](int k, int s) {
+  auto issue = [&](int i, int s) {  // local tile i (global tile kb + i) into ring slot s
     uint64_t* bar = &sm.full[s];
     mbar_expect_tx(bar, stage_bytes);
-    const int t0 = k * kTile;
+    const int t0 = (kb + i) * kTile;
     tma_load_3d(&sm.u[s][0][0], &P.tm_u, t0, c0, b, bar);
     tma_load_3d(&sm.d[s][0][0], &P.tm_d, t0, c0, b, bar);
     if constexpr (kHasZ) tma_load_3d(&sm.z[s][0][0], &P.tm_z, t0, c0, b, bar);
@@ -169,20 +190,22 @@ __global__ void __launch_bounds__(32 * kNW, 4) ss_fwd_kernel(const __grid_consta
     }
     __syncthreads();
     if (tid == 0)
-      for (int s = 0; s < kStages && s < ntiles; ++s) issue(s, s);
+      for (int s = 0; s < kStages && s < nt; ++s) issue(s, s);
   }
 
   const IT* ub = (const IT*)a.u + (int64_t)b * a.u_batch_stride + (int64_t)c0 * a.u_dim_stride;
   const IT* db = (const IT*)a.delta + (int64_t)b * a.delta_batch_stride + (int64_t)c0 * a.delta_dim_stride;
   const IT* zb = kHasZ ? (const IT*)a.z + (int64_t)b * a.z_batch_stride + (int64_t)c0 * a.z_dim_stride : nullptr;
 
-  for (int k = 0; k < ntiles; ++k) {
+  for (int it = 0; it < nt; ++it) {
+    const int k = kb + it;  // global tile
     const int t0 = k * kTile;
     const int tlen = min(kTile, L - t0);
-    const int stg = kTMA ? k % kStages : 0;
+    const int stg = kTMA ? it % kStages : 0;
+    const int yb = it & 1;  // y_s buffer of this tile
     bool failed = false;
     if constexpr (kTMA) {
-      failed = !mbar_wait_bounded(&sm.full[stg], (k / kStages) & 1);
+      failed = !mbar_wait_bounded(&sm.full[stg], (it / kStages) & 1, P.wait_cycles);
       if (w == 0) widen_bc_warp<IT, NS, kVarB, kVarC>(sm.B_s, sm.C_s, sm.Braw[stg], sm.Craw[stg], bc_f32, lane);
     } else {
       load_tile<IT, NT>(sm.u[0], ub + t0, a.u_dim_stride, nvalid, tlen, P.vec_u);
@@ -223,19 +246,20 @@ __global__ void __launch_bounds__(32 * kNW, 4) ss_fwd_kernel(const __grid_consta
       }
     }
     if (__syncthreads_or(failed)) {  // (every thread has also finished the previous tile's epilogue)
-      // a TMA stage never completed: report, let the copies in flight land, and leave
+      // a TMA stage did not complete in time: report, let every copy in flight land (this
+      // tile's included), and leave
       if (tid == 0) {
         if (P.status != nullptr) atomicOr(P.status, kStatusTimeout);
-        const int issued_end = max(kStages, k + kStages - 1);  // tiles issued before this point
-        for (int j = k + 1; j < ntiles && j < issued_end; ++j)
-          mbar_wait_bounded(&sm.full[j % kStages], (j / kStages) & 1);
+        const int issued_end = max(kStages, it + kStages - 1);  // local tiles issued before this point
+        for (int j = it; j < nt && j < issued_end; ++j)
+          mbar_wait_bounded(&sm.full[j % kStages], (j / kStages) & 1, kWaitCycles);
       }
       __syncthreads();
       return;
     }
     // ---- refill the slot the previous tile used (every thread is past its epilogue)
     if constexpr (kTMA) {
-      if (tid == 0 && k >= 1 && k - 1 + kStages < ntiles) issue(k - 1 + kStages, (k - 1) % kStages);
+      if (tid == 0 && it >= 1 && it - 1 + kStages < nt) issue(it - 1 + kStages, (it - 1) % kStages);
     }
 
     // ---- 2. the recurrence, 4 states per lane, 16 steps.  All 64 decays of the tile are
@@ -281,7 +305,7 @@ __global__ void __launch_bounds__(32 * kNW, 4) ss_fwd_kernel(const __grid_consta
 #pragma unroll
         for (int p = 0; p < 2; ++p) h[p] = fma2(da[t][p], h[p], mul2(f2(dus[st]), Bv[p]));
         const float2 y2 = fma2(Cv[1], h[1], mul2(Cv[0], h[0]));
-        sm.y_s[k & 1][w][t][lane] = y2.x + y2.y;
+        sm.y_s[yb][w][t][lane] = y2.x + y2.y;
       }
     }
     if (a.ckpt != nullptr && lane_ok) {
@@ -305,7 +329,7 @@ __global__ void __launch_bounds__(32 * kNW, 4) ss_fwd_kernel(const __grid_consta
         const int t = pq * S + i;
         float y = sg == 0 ? Dv * uo[i] : 0.f;
 #pragma unroll
-        for (int g = 0; g < kNW; ++g) y += sm.y_s[k & 1][g][t][pc];
+        for (int g = 0; g < kNW; ++g) y += sm.y_s[yb][g][t][pc];
         ys[i] = y;
       }
       const int nv = pc_ok ? max(0, min(S, tlen - pq * S)) : 0;
@@ -327,7 +351,7 @@ __global__ void __launch_bounds__(32 * kNW, 4) ss_fwd_kernel(const __grid_consta
         const int t = pq * S + i;
         float y = Dv * uo[i];
 #pragma unroll
-        for (int g = 0; g < kNW; ++g) y += sm.y_s[k & 1][g][t][pc];
+        for (int g = 0; g < kNW; ++g) y += sm.y_s[yb][g][t][pc];
         yu[i] = y;
         if constexpr (kHasZ) {
           y *= zo[i] * sigmoid_fast(zo[i]);
@@ -345,7 +369,7 @@ __global__ void __launch_bounds__(32 * kNW, 4) ss_fwd_kernel(const __grid_consta
     if constexpr (!kTMA) __syncthreads();
   }
 
-  if (a.last_state != nullptr && lane_ok) {
+  if (a.last_state != nullptr && lane_ok && chunk == P.nchunk - 1) {
     float* ls = a.last_state + ((int64_t)b * a.dim + c) * N;
     const float hv[kSPW] = {h[0].x, h[0].y, h[1].x, h[1].y};
 #pragma unroll

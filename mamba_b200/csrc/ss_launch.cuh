@@ -4,6 +4,7 @@
 #pragma once
 #include "ss_fwd.cuh"
 #include "ss_bwd.cuh"
+#include "ss_chunk.cuh"
 #include "ss_step.cuh"
 
 namespace ssb {
@@ -12,10 +13,8 @@ inline int warps_for(int dstate) { return dstate <= 4 ? 1 : (dstate <= 8 ? 2 : 4
 
 template <typename K, typename Arg>
 static cudaError_t launch_dyn(K kernel, dim3 grid, int threads, size_t smem, cudaStream_t st, const Arg& P) {
-  if (smem > 48 * 1024) {
-    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return e;
-  }
+  cudaError_t e = ensure_smem_limit(reinterpret_cast<const void*>(kernel), smem);
+  if (e != cudaSuccess) return e;
   kernel<<<grid, threads, smem, st>>>(P);
   return cudaGetLastError();
 }
@@ -42,10 +41,30 @@ static cudaError_t fwd_bc(const FwdK& P, dim3 grid, cudaStream_t st, bool tma) {
   if (vc) return fwd_z<IT, NW, false, true, M>(P, grid, st, tma);
   return fwd_z<IT, NW, false, false, M>(P, grid, st, tma);
 }
+// chunk summaries of the forward (time chunks 0 .. nchunk - 2)
+template <typename IT, int NW, bool VB>
+static cudaError_t fwd_chunk_go(const FwdK& P, cudaStream_t st) {
+  dim3 grid((unsigned)((int64_t)P.a.batch * P.nct * (P.nchunk - 1)));
+  return launch_dyn(ss_fwd_chunk_kernel<IT, NW, VB>, grid, 32 * NW, sizeof(FwdChunkSmem<IT, NW, VB>), st, P);
+}
+template <typename IT, int NW>
+static cudaError_t fwd_chunk_b(const FwdK& P, cudaStream_t st) {
+  return P.a.var_B ? fwd_chunk_go<IT, NW, true>(P, st) : fwd_chunk_go<IT, NW, false>(P, st);
+}
+template <typename IT>
+static cudaError_t fwd_chunks(const FwdK& P, cudaStream_t st) {
+  switch (warps_for(P.a.dstate)) {
+    case 1: return fwd_chunk_b<IT, 1>(P, st);
+    case 2: return fwd_chunk_b<IT, 2>(P, st);
+    default: return fwd_chunk_b<IT, 4>(P, st);
+  }
+}
+
 template <typename IT>
 cudaError_t launch_fwd(const FwdK& P, cudaStream_t st, bool tma) {
   const ss_fwd_args& a = P.a;
-  dim3 grid((unsigned)((int64_t)a.batch * P.nsg * P.nct));  // sizes checked on the host
+  // sizes checked on the host; nchunk > 1 only with TMA and dstate <= 16
+  dim3 grid((unsigned)((int64_t)a.batch * P.nsg * P.nct * P.nchunk));
   if (P.nsg > 1) {
     // state groups: partial sums meet in the workspace, then the gate is applied
     cudaError_t e = cudaMemsetAsync(a.work, 0, (size_t)a.batch * a.dim * (size_t)a.seqlen * sizeof(float), st);
@@ -55,6 +74,10 @@ cudaError_t launch_fwd(const FwdK& P, cudaStream_t st, bool tma) {
     const int nlc = (a.seqlen + 255) / 256;
     fwd_finish_kernel<IT><<<(unsigned)((int64_t)a.batch * a.dim * nlc), 256, 0, st>>>(a, nlc);
     return cudaGetLastError();
+  }
+  if (P.nchunk > 1) {
+    cudaError_t e = fwd_chunks<IT>(P, st);
+    if (e != cudaSuccess) return e;
   }
   switch (warps_for(a.dstate)) {
     case 1: return fwd_bc<IT, 1, false>(P, grid, st, tma);
@@ -83,10 +106,32 @@ static cudaError_t bwd_bc(const BwdK& P, dim3 grid, cudaStream_t st, bool tma) {
   if (vc) return bwd_z<IT, NW, false, true, M>(P, grid, st, tma);
   return bwd_z<IT, NW, false, false, M>(P, grid, st, tma);
 }
+// chunk carries of the backward (time chunks 1 .. nchunk - 1)
+template <typename IT, int NW, bool VC, bool Z>
+static cudaError_t bwd_carry_go(const BwdK& P, cudaStream_t st) {
+  dim3 grid((unsigned)((int64_t)P.a.f.batch * P.nct * (P.nchunk - 1)));
+  return launch_dyn(ss_bwd_carry_kernel<IT, NW, VC, Z>, grid, 32 * NW, sizeof(BwdCarrySmem<IT, NW, VC, Z>), st, P);
+}
+template <typename IT, int NW>
+static cudaError_t bwd_carry_cz(const BwdK& P, cudaStream_t st) {
+  const bool vc = P.a.f.var_C != 0, z = P.a.f.z != nullptr;
+  if (vc) return z ? bwd_carry_go<IT, NW, true, true>(P, st) : bwd_carry_go<IT, NW, true, false>(P, st);
+  return z ? bwd_carry_go<IT, NW, false, true>(P, st) : bwd_carry_go<IT, NW, false, false>(P, st);
+}
+template <typename IT>
+static cudaError_t bwd_carries(const BwdK& P, cudaStream_t st) {
+  switch (warps_for(P.a.f.dstate)) {
+    case 1: return bwd_carry_cz<IT, 1>(P, st);
+    case 2: return bwd_carry_cz<IT, 2>(P, st);
+    default: return bwd_carry_cz<IT, 4>(P, st);
+  }
+}
+
 template <typename IT>
 cudaError_t launch_bwd(const BwdK& P, cudaStream_t st, bool tma) {
   const ss_fwd_args& f = P.a.f;
-  dim3 grid((unsigned)((int64_t)f.batch * P.nsg * P.nct));  // sizes checked on the host
+  // sizes checked on the host; nchunk > 1 only with TMA and dstate <= 16
+  dim3 grid((unsigned)((int64_t)f.batch * P.nsg * P.nct * P.nchunk));
   if (P.nsg > 1) {
     cudaError_t e =
         cudaMemsetAsync(f.work, 0, 2 * (size_t)f.batch * f.dim * (size_t)f.seqlen * sizeof(float), st);
@@ -96,6 +141,10 @@ cudaError_t launch_bwd(const BwdK& P, cudaStream_t st, bool tma) {
     const int nlc = (f.seqlen + 255) / 256;
     bwd_finish_kernel<IT><<<(unsigned)((int64_t)f.batch * f.dim * nlc), 256, 0, st>>>(P.a, nlc);
     return cudaGetLastError();
+  }
+  if (P.nchunk > 1) {
+    cudaError_t e = bwd_carries<IT>(P, st);
+    if (e != cudaSuccess) return e;
   }
   switch (warps_for(f.dstate)) {
     case 1: return bwd_bc<IT, 1, false>(P, grid, st, tma);

@@ -15,10 +15,8 @@ template <typename IT, int K, int TPC, int R, int CL>
 cudaError_t launch_mix(const MixK& P, cudaStream_t st) {
   const size_t smem = sizeof(float) * ((size_t)P.cs + 2 * (size_t)P.J);
   auto kern = mamba_step_kernel<IT, K, TPC, R, CL>;
-  if (smem > 48 * 1024) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return e;
-  }
+  cudaError_t e = ensure_smem_limit(reinterpret_cast<const void*>(kern), smem);
+  if (e != cudaSuccess) return e;
   kern<<<dim3((unsigned)((int64_t)P.a.batch * CL)), kMixThreads, smem, st>>>(P);
   return cudaGetLastError();
 }

@@ -139,6 +139,7 @@ def scan_forward(p: _Prepared, want_ckpt: bool, want_last: bool):
     args = p.fwd_args(out, ckpt, last, y, work)
     with torch.cuda.device(p.device):
         L.check(L.lib().ss_fwd(args, L.stream_of(p.device)), "ss_fwd")
+        L.maybe_check_status(p.device, "ss_fwd")
     return out, ckpt, last, y
 
 
@@ -172,6 +173,7 @@ def scan_backward(p: _Prepared, dout, ckpt, y=None):
         dA.data_ptr(), dB.data_ptr(), dC.data_ptr(), L.ptr(dD), L.ptr(dbias))
     with torch.cuda.device(dev):
         L.check(L.lib().ss_bwd(args, L.stream_of(dev)), "ss_bwd")
+        L.maybe_check_status(dev, "ss_bwd")
     return du, ddelta, dA, dB, dC, dD, dz, dbias
 
 

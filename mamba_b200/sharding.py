@@ -102,3 +102,45 @@ def reduce_param_grads(grads: dict, s: Shard, group=None) -> dict:
         if grads.get(k) is not None:
             dist.all_reduce(grads[k], op=dist.ReduceOp.SUM, group=group)
     return grads
+
+
+def verify(local: torch.Tensor, s: Shard, got_rows: torch.Tensor, want_rows, rtol: float, atol: float,
+           group=None) -> dict:
+    """Verification of a sharded result, after the computation (never inside a timed path).
+
+    * every shard is all-gathered (``gather_rows``) together with the checksum its owner took
+      of it before the exchange (float64 sum and sum of squares), and each gathered slice is
+      checked against its owner's checksum — a shard damaged between compute and exchange, or
+      in transport, is named by rank;
+    * each rank compares sampled rows of its own shard (``got_rows``) with a reference for
+      them (``want_rows``, e.g. from the CPU oracle: rows are independent, so a row's inputs
+      alone determine it) and the worst excess ``max |got - want| / (atol + rtol |want|)`` of
+      every rank is gathered — a shard computed wrongly is named by rank (excess > 1).
+
+    Returns {"gathered", "checksum_bad_ranks", "row_excess" (per rank), "bad_ranks", "ok"}.
+    Every rank takes the same collective steps in the same order."""
+    world = s.world
+    loc = local.detach().contiguous()
+    x64 = loc.double()
+    sums = torch.stack([x64.sum(), (x64 * x64).sum()]).reshape(1, 2)
+    all_sums = torch.empty(world, 2, dtype=torch.float64, device=loc.device)
+    dist.all_gather_into_tensor(all_sums, sums, group=group)
+    full = gather_rows(loc, s, group)
+    parts = full.split(loc.shape[0], dim=0) if s.axis == "batch" else full.split(loc.shape[1], dim=1)
+    bad_sum = []
+    for r, part in enumerate(parts):
+        p64 = part.double()
+        mine = torch.stack([p64.sum(), (p64 * p64).sum()])
+        ref = all_sums[r]
+        if not torch.allclose(mine, ref, rtol=1e-12, atol=1e-12 * float(ref.abs().max()) + 1e-30):
+            bad_sum.append(r)
+    g = got_rows.detach().double().cpu()
+    w = torch.as_tensor(want_rows, dtype=torch.float64)
+    exc = float(((g - w).abs() / (atol + rtol * w.abs())).max()) if w.numel() else 0.0
+    mine = torch.tensor([exc], dtype=torch.float64, device=loc.device)
+    all_exc = torch.empty(world, dtype=torch.float64, device=loc.device)
+    dist.all_gather_into_tensor(all_exc, mine, group=group)
+    row_excess = [float(v) for v in all_exc.cpu()]
+    bad = sorted(set(bad_sum) | {r for r, e in enumerate(row_excess) if not e <= 1.0})
+    return {"gathered": full, "checksum_bad_ranks": bad_sum, "row_excess": row_excess, "bad_ranks": bad,
+            "ok": not bad}

@@ -11,7 +11,8 @@ none and takes the arch from TORCH_CUDA_ARCH_LIST), and writes the module only i
 ``oracle/_ref/`` (git-ignored, but it travels to the GPU box).  It does not run the
 reference's own setup.py / pip build.
 
-Usage:  python oracle/build_ref.py [--ref /path/to/reference]
+Usage:  python oracle/build_ref.py [--ref PATH]   (default: $MAMBA_REFERENCE_ROOT, else a directory
+        named `reference` beside this repository)
 """
 from __future__ import annotations
 
@@ -23,7 +24,14 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 OUT = os.path.join(HERE, "_ref")
 
 
-def build(ref_root: str = "/root/reference", verbose: bool = False) -> str | None:
+def reference_root() -> str:
+    """$MAMBA_REFERENCE_ROOT, else a directory named `reference` beside this repository."""
+    repo = os.path.dirname(HERE)
+    return os.environ.get("MAMBA_REFERENCE_ROOT", os.path.join(os.path.dirname(repo), "reference"))
+
+
+def build(ref_root: str | None = None, verbose: bool = False) -> str | None:
+    ref_root = ref_root or reference_root()
     src = os.path.join(ref_root, "csrc", "selective_scan")
     if not os.path.isdir(src):
         print(f"[build_ref] reference sources not found at {src}; skipping", file=sys.stderr)
@@ -53,7 +61,8 @@ def build(ref_root: str = "/root/reference", verbose: bool = False) -> str | Non
 
 if __name__ == "__main__":
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--ref", default=None, help="reference tree (default: $MAMBA_REFERENCE_ROOT, else "
+                                                  "../reference beside this repository)")
     ap.add_argument("-v", action="store_true")
     a = ap.parse_args()
     # cpp_extension otherwise appends every arch in TORCH_CUDA_ARCH_LIST

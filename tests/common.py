@@ -8,9 +8,17 @@ B, C ~ N(0,1); D = 1 (mamba_simple.py:83) unless randomised; dout ~ N(0,1).
 Everything is generated on the CPU from a seed, so the oracle sees identical values.
 """
 import math
+import os
 
 import numpy as np
 import torch
+
+
+def reference_root():
+    """Where the reference's source tree lies: $MAMBA_REFERENCE_ROOT, else a directory named
+    `reference` beside this repository."""
+    here = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    return os.environ.get("MAMBA_REFERENCE_ROOT", os.path.join(os.path.dirname(here), "reference"))
 
 # tolerances stated by the task for this path: fp32 I/O, and bf16 I/O with fp32 state
 TOL = {torch.float32: (1e-4, 1e-5), torch.bfloat16: (2e-2, 5e-2), torch.float16: (2e-2, 5e-2)}

@@ -64,3 +64,35 @@ def test_reference_arm_line_and_other_ranks(capsys, monkeypatch):
     assert line["cpu_baseline"]["kind"] == "port" and line["cpu_baseline"]["cores"] == 8
     assert line["e2e"] == {"value": 1002.0, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}
     assert line["metric"] == bench.METRIC and line["config"]["global_batch"] == 16
+
+
+def test_config_workloads_0_1_2():
+    c0, c1, c2 = (bench.scan_shape(w, 1) for w in ("scan-c0", "scan-c1", "scan-c2"))
+    assert (c0["b"], c0["d"], c0["L"], c0["dtype"], c0["passes"], c0["z"], c0["last"]) == \
+        (2, 1536, 2048, "f32", "fwd", False, True)
+    assert (c1["b"], c1["dtype"], c1["passes"], c1["z"]) == (2, "bf16", "fwd+bwd", True)
+    assert (c2["b"], c2["d"], c2["L"], c2["passes"], c2["last"]) == (1, 5120, 32768, "fwd", True)
+    # per-GPU batch fixed: the job grows with the GPUs
+    assert bench.scan_shape("scan-c2", 4)["global_b"] == 4
+    # configs 0 and 1 fit in L2 and flush it between steps; the north star and config 2 do not
+    assert bench.flushes_l2(c0) and bench.flushes_l2(c1)
+    assert not bench.flushes_l2(bench.scan_shape("scan", 1)) and not bench.flushes_l2(c2)
+    assert "flushed" in bench.config_dict(1, c0)["l2"]
+
+
+def test_algorithmic_bytes_forward_only_and_fp32():
+    # config 0: fp32, no gate: read u, delta, write out (12 B / element) + B, C (128 B / token) + final state
+    fwd, _ = bench.algorithmic_bytes(2, 1536, 2048, 16, es=4, z=False, last=True)
+    assert fwd == 2 * 1536 * 2048 * 12 + 2 * 2048 * 128 + 2 * 1536 * 16 * 4
+    # config 2: bf16 with a gate: 8 B / element + 64 B / token + final state
+    fwd, _ = bench.algorithmic_bytes(1, 5120, 32768, 16, es=2, z=True, last=True)
+    assert fwd == 5120 * 32768 * 8 + 32768 * 64 + 5120 * 16 * 4
+    assert bench.launches_per_step(1536, 16, True) == 2 and bench.launches_per_step(1536, 16, False) == 1
+    assert bench.launches_per_step(1536, 64, True) == 4
+
+
+def test_cpu_baseline_sampler_forward_only():
+    s = bench.scan_shape("scan-c0", 1)
+    elems, tokens = s["b"] * s["d"] * s["L"], s["b"] * s["L"]
+    value, threads, sample, seconds = bench.cpu_sample_rate(elems, tokens, 0.3, shape=s)
+    assert value > 0 and "(fwd," in sample

@@ -33,7 +33,7 @@ def test_library_exports_every_declared_symbol():
 
 def test_abi_version_and_struct_layout():
     lib = L.lib()
-    assert lib.ss_abi_version() == 7
+    assert lib.ss_abi_version() == 8
     for i, st in enumerate(L.STRUCTS):
         assert lib.ss_struct_size(i) == ctypes.sizeof(st)
     assert lib.ss_struct_size(len(L.STRUCTS)) == 0
@@ -268,3 +268,33 @@ def test_mamba_step_validation():
     a.dt_rank, a.batch = 4, 0
     assert lib.ss_mamba_step(ctypes.byref(a), None) == L.SS_OK               # empty batch: nothing to do
     assert lib.ss_mamba_step(None, None) == L.SS_ERR_INVALID
+
+
+def test_time_chunk_workspace_sizes():
+    """dstate <= 16: the workspace holds one summary per time chunk ((dstate + 1) floats per
+    channel) when the shape's grid cannot fill the GPU, none when it can; a forced chunk count
+    sizes it for that count (capped at the number of 16-step tiles)."""
+    assert L.set_time_chunks(0) == 0
+    try:
+        for b, d, seqlen in ((2, 1536, 2048), (1, 5120, 32768)):
+            w = L.work_elems(b, d, seqlen, 16)
+            assert w > 0 and w % (b * 17 * d) == 0
+        assert L.work_elems(8, 1536, 2048, 16) == 0
+        assert L.work_elems(64, 5120, 2048, 16) == 0
+        assert L.set_time_chunks(4) == 0
+        assert L.work_elems(2, 64, 640, 16) == 2 * 4 * 17 * 64
+        assert L.work_elems(2, 64, 33, 16) == 2 * 3 * 17 * 64     # 3 tiles: at most 3 chunks
+        assert L.set_time_chunks(1) == 4
+        assert L.work_elems(2, 1536, 2048, 16) == 0               # never split
+    finally:
+        L.set_time_chunks(0)
+
+
+def test_wait_limit_setter_round_trips():
+    prev = L.set_wait_limit(12345)
+    try:
+        assert prev == 4000000000
+        assert L.set_wait_limit(-1) == 12345                      # < 0 restores the default
+        assert L.set_wait_limit(-1) == 4000000000
+    finally:
+        L.set_wait_limit(-1)

@@ -17,8 +17,11 @@ import numpy as np
 import pytest
 import torch
 
-REF_PARENT = "/root"
-REF = os.path.join(REF_PARENT, "reference")
+from common import reference_root
+
+REF = reference_root()
+REF_PARENT = os.path.dirname(REF)
+PKG = os.path.basename(REF)  # the reference tree is imported as a package of this name
 pytestmark = pytest.mark.skipif(not os.path.isdir(os.path.join(REF, "ops")), reason="reference sources absent")
 
 
@@ -45,15 +48,15 @@ def ref_pkg(monkeypatch):
     monkeypatch.setitem(sys.modules, "selective_scan", ext)
     monkeypatch.syspath_prepend(REF_PARENT)
     monkeypatch.setattr(sys, "dont_write_bytecode", True)
-    for m in [m for m in sys.modules if m == "reference" or m.startswith("reference.")]:
+    for m in [m for m in sys.modules if m == PKG or m.startswith(PKG + ".")]:
         monkeypatch.delitem(sys.modules, m)
-    return importlib.import_module("reference")
+    return importlib.import_module(os.path.basename(REF))
 
 
 def test_reference_selective_scan_fn_runs_on_dropin(ref_pkg):
     from torch_ref import scan_autograd
 
-    ssi_ref = importlib.import_module("reference.ops.selective_scan_interface")
+    ssi_ref = importlib.import_module(PKG + ".ops.selective_scan_interface")
     g = torch.Generator().manual_seed(0)
     b, d, n, L = 2, 8, 4, 24
     u = torch.randn(b, d, L, generator=g, requires_grad=True)
@@ -80,7 +83,7 @@ def test_reference_selective_scan_fn_runs_on_dropin(ref_pkg):
 
 def test_reference_mamba_simple_runs_unchanged(ref_pkg):
     """MambaSimple.forward (modules/mamba_simple.py:87-151) end to end on the drop-in."""
-    mod = importlib.import_module("reference.modules.mamba_simple")
+    mod = importlib.import_module(PKG + ".modules.mamba_simple")
     torch.manual_seed(0)
     block = mod.MambaSimple(model_dim=16, state_dim=4)
     x = torch.randn(2, 12, 16, requires_grad=True)
@@ -97,7 +100,7 @@ def test_mamba_simple_restatement_matches_reference_module(ref_pkg):
     MambaSimple: same state_dict, same outputs and parameter gradients."""
     from torch_ref import MambaSimpleRef
 
-    mod = importlib.import_module("reference.modules.mamba_simple")
+    mod = importlib.import_module(PKG + ".modules.mamba_simple")
     torch.manual_seed(1)
     ref = mod.MambaSimple(model_dim=16, state_dim=4, conv_bias=True, bias=True)
     mine = MambaSimpleRef(16, state_dim=4, conv_bias=True, bias=True)
@@ -118,7 +121,7 @@ def test_causal_lm_restatement_matches_reference_model(ref_pkg):
     CausalLM: identical state_dict keys and logits."""
     from torch_ref import CausalLMRef
 
-    lm = importlib.import_module("reference.models.causal_lm")
+    lm = importlib.import_module(PKG + ".models.causal_lm")
     torch.manual_seed(2)
     cfg = lm.CausalLMConfig(vocab_size=50, model_dim=16, state_dim=4, num_layers=2, dropout_rate=0.0)
     ref = lm.CausalLM(cfg).eval()
