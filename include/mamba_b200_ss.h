@@ -30,7 +30,8 @@
  *              21-30) fused with its Block's residual add (models/causal_lm.py:30-37), which
  *              the reference runs as a chain of PyTorch elementwise and reduction kernels.
  *
- * Tensor layouts (element strides; the innermost sequence axis must have stride 1):
+ * Tensor layouts (element strides; the innermost sequence axis must have stride 1, or, with
+ * ss_fwd_args.layout = SS_LAYOUT_BLD, the innermost dim axis):
  *   u, delta, z, out, dout, du, ddelta, dz : (batch, dim, seqlen), batch/dim strides given
  *   A, dA                                  : (dim, dstate) contiguous, fp32
  *   B, C   variable                        : (batch, ngroups, dstate, seqlen) contiguous
@@ -68,6 +69,17 @@ extern "C" {
 
 typedef enum ss_dtype { SS_F32 = 0, SS_BF16 = 1, SS_F16 = 2 } ss_dtype;
 
+/* Layout of the per-element tensors of a scan call (u, delta, z, out, out_y and, in the
+ * backward, dout, du, ddelta, dz, y):
+ *   SS_LAYOUT_BDL  (batch, dim, seqlen) with unit seqlen stride (the reference's layout);
+ *   SS_LAYOUT_BLD  (batch, seqlen, dim) with unit dim stride — the layout of the projections
+ *                  around the scan in a Mamba block (modules/mamba_simple.py:96, :104-106,
+ *                  :143-145 permute to and from it); every *_dim_stride field of the call then
+ *                  holds the stride between consecutive time steps.
+ * SS_LAYOUT_BLD needs dstate <= 16 and 16-byte aligned rows (tensor maps); otherwise the call
+ * returns SS_ERR_UNSUPPORTED. */
+typedef enum ss_layout { SS_LAYOUT_BDL = 0, SS_LAYOUT_BLD = 1 } ss_layout;
+
 typedef enum ss_status {
   SS_OK = 0,
   SS_ERR_INVALID = 1,     /* null pointer, bad size, bad stride, dim % ngroups != 0 */
@@ -100,6 +112,7 @@ typedef struct ss_fwd_args {
                                are scanned in groups of 16 whose per-element sums meet
                                here); ss_fwd and ss_bwd overwrite it; contents are not
                                needed between calls.  Nullable when dstate <= 16.          */
+  int layout;               /* ss_layout of the per-element tensors (0: batch, dim, seqlen)  */
 } ss_fwd_args;
 
 typedef struct ss_bwd_args {

@@ -16,6 +16,7 @@ _PKG = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(_PKG, "libmamba_b200_ss.so")
 
 SS_F32, SS_BF16, SS_F16 = 0, 1, 2
+SS_LAYOUT_BDL, SS_LAYOUT_BLD = 0, 1
 SS_OK, SS_ERR_INVALID, SS_ERR_UNSUPPORTED, SS_ERR_CUDA = 0, 1, 2, 3
 SS_MAX_DSTATE = 256
 TILE = 16  # time steps between checkpoints (kTile in csrc/ss_common.cuh)
@@ -39,6 +40,7 @@ class FwdArgs(ctypes.Structure):
         ("ckpt", c_vp), ("last_state", c_vp),
         ("out_y", c_vp), ("out_y_batch_stride", c_i64), ("out_y_dim_stride", c_i64),
         ("work", c_vp),
+        ("layout", c_int),
     ]
 
 

@@ -46,10 +46,16 @@ template <typename IT>
 constexpr int kStagesBwd = sizeof(IT) == 4 ? 2 : 3;
 constexpr int kS12Row = 66;    // floats per row of the packed (S1, S2) partials (64 + 2 pad)
 
-// dB/dC fold block: 16 rows of 64 floats (32 lanes x float2); 16-byte unit q of row r is
-// stored at unit q ^ (2 * (r & 3)), which keeps both the per-row float2 writes and the
-// per-lane 16-byte reads of the reduction free of bank conflicts.
-__device__ __forceinline__ int fold_off(int r, int unit) { return r * 64 + 4 * (unit ^ (2 * (r & 3))); }
+// dB/dC fold block: 16 rows of 64 floats (32 lanes x float2).  The per-row float2 writes cover
+// 256 contiguous bytes; in the reduction, lane l reads row l >> 1 with 16-byte loads.  With
+// 2-byte I/O the rows are kFoldRow = 72 floats apart, which puts the 4 rows of a quarter warp on
+// distinct bank groups (72 r mod 32 = 8 r): both sides are conflict-free with addresses of the
+// form per-lane base + constant.  With 4-byte I/O (no room for the pad) the rows are packed and
+// 16-byte unit q of row r is stored at q ^ (2 (r & 3)), conflict-free on both sides as well.
+template <typename IT> constexpr int kFoldRow = sizeof(IT) == 2 ? 72 : 64;
+template <typename IT> __device__ __forceinline__ int fold_off(int r, int unit) {
+  return sizeof(IT) == 2 ? r * 72 + 4 * unit : r * 64 + 4 * (unit ^ (2 * (r & 3)));
+}
 
 template <typename IT, int kNW, bool kVarB, bool kVarC, bool kHasZ>
 struct BwdSmem {
@@ -62,16 +68,16 @@ struct BwdSmem {
   alignas(128) IT Braw[kVarB ? kStagesBwd<IT> : 1][NS * kTile];  // TMA path: B / C have the I/O dtype
   alignas(128) IT Craw[kVarC ? kStagesBwd<IT> : 1][NS * kTile];
   alignas(128) float hck[kStagesBwd<IT>][NS][kCh];   // states at the tile start, [n][channel]
-  alignas(16) float4 dt_s[kCh][4];
-  alignas(16) float4 dtu_s[kCh][4];
-  alignas(16) float4 dy_s[kCh][4];
+  alignas(16) float4 dt_s[kCh][kElemRow<IT>];
+  alignas(16) float4 dtu_s[kCh][kElemRow<IT>];
+  alignas(16) float4 dy_s[kCh][kElemRow<IT>];
   alignas(16) float4 sig_s[kCh][4];
   alignas(16) float4 gz_s[kHasZ ? kCh : 1][4];
   alignas(16) float B_s[kVarB ? kTile : 1][NS];
   float bc_pad[16];  // puts C_s rows on the other half of the banks from B_s rows
   alignas(16) float C_s[kVarC ? kTile : 1][NS];
   alignas(16) float s12_s[kNW][kTile][kS12Row];                        // (S1, S2) per channel
-  alignas(16) float fold[(kVarB || kVarC) ? kNW : 1][16 * 64];         // 4 steps x 2 pairs x B|C
+  alignas(16) float fold[(kVarB || kVarC) ? kNW : 1][16 * kFoldRow<IT>];  // 4 steps x 2 pairs x B|C
   // per-warp channel sums of the tile: row k = (2 * pair + h) * 2 + (B|C), step t stored at
   // t ^ (4 * (k >> 1)), which makes the fold's scattered writes conflict-free while every
   // aligned group of 4 steps stays contiguous for the 16-byte reads
@@ -79,8 +85,9 @@ struct BwdSmem {
   alignas(8) uint64_t full[kStagesBwd<IT>];
 };
 
-template <typename IT, int kNW, bool kVarB, bool kVarC, bool kHasZ, bool kTMA, bool kMulti = false>
+template <typename IT, int kNW, bool kVarB, bool kVarC, bool kHasZ, bool kTMA, bool kMulti = false, bool kBLD = false>
 __global__ void __launch_bounds__(32 * kNW, 3) ss_bwd_kernel(const __grid_constant__ BwdK P) {
+  static_assert(!kBLD || (kTMA && !kMulti), "(b, L, d) tiles come from tensor maps, dstate <= 16");
   constexpr int NT = 32 * kNW;
   constexpr int NS = kSPW * kNW;
   constexpr int S = kTile / kNW;
@@ -150,7 +157,7 @@ __global__ void __launch_bounds__(32 * kNW, 3) ss_bwd_kernel(const __grid_consta
   }
 
   // ---- element role
-  const int pc = tid / kNW, pq = tid % kNW;
+  const int pc = elem_pc<kNW, kBLD>(tid), pq = elem_pq<kNW, kBLD>(tid);
   const bool pc_ok = pc < nvalid;
   const float Dv = (f.D != nullptr && pc_ok) ? f.D[c0 + pc] : 0.f;
   const float bias = (f.delta_bias != nullptr && pc_ok) ? f.delta_bias[c0 + pc] : 0.f;
@@ -161,9 +168,9 @@ __global__ void __launch_bounds__(32 * kNW, 3) ss_bwd_kernel(const __grid_consta
   const IT* gb = (const IT*)a.dout + (int64_t)b * a.dout_batch_stride + (int64_t)c0 * a.dout_dim_stride;
   const IT* zb = kHasZ ? (const IT*)f.z + (int64_t)b * f.z_batch_stride + (int64_t)c0 * f.z_dim_stride : nullptr;
   const IT* yb = kHasZ ? (const IT*)a.y + (int64_t)b * a.y_batch_stride + (int64_t)c0 * a.y_dim_stride : nullptr;
-  IT* du_row = (IT*)a.du + (int64_t)b * a.du_batch_stride + (int64_t)(c0 + pc) * a.du_dim_stride;
-  IT* dd_row = (IT*)a.ddelta + (int64_t)b * a.ddelta_batch_stride + (int64_t)(c0 + pc) * a.ddelta_dim_stride;
-  IT* dz_row = kHasZ ? (IT*)a.dz + (int64_t)b * a.dz_batch_stride + (int64_t)(c0 + pc) * a.dz_dim_stride : nullptr;
+  IT* du_row = (IT*)a.du + row_off<kBLD>(b, a.du_batch_stride, c0 + pc, a.du_dim_stride);
+  IT* dd_row = (IT*)a.ddelta + row_off<kBLD>(b, a.ddelta_batch_stride, c0 + pc, a.ddelta_dim_stride);
+  IT* dz_row = kHasZ ? (IT*)a.dz + row_off<kBLD>(b, a.dz_batch_stride, c0 + pc, a.dz_dim_stride) : nullptr;
   const int64_t bc_off = (((int64_t)b * f.ngroups + grp) * N + n0) * (int64_t)L;  // row n0 of this group
 
   const int ntiles = P.ntiles;
@@ -180,12 +187,13 @@ __global__ void __launch_bounds__(32 * kNW, 3) ss_bwd_kernel(const __grid_consta
                            ((kVarB ? 1 : 0) + (kVarC ? 1 : 0)) * bc_bytes + (k > 0 ? h_bytes : 0u);
     mbar_expect_tx(bar, bytes);
     const int t0 = k * kTile;
-    tma_load_3d(&sm.u[s][0][0], &P.tm_u, t0, c0, b, bar);
-    tma_load_3d(&sm.d[s][0][0], &P.tm_d, t0, c0, b, bar);
-    tma_load_3d(&sm.g[s][0][0], &P.tm_g, t0, c0, b, bar);
+    const int x = kBLD ? c0 : t0, y = kBLD ? t0 : c0;  // (b, L, d) maps run along the channels
+    tma_load_3d(&sm.u[s][0][0], &P.tm_u, x, y, b, bar);
+    tma_load_3d(&sm.d[s][0][0], &P.tm_d, x, y, b, bar);
+    tma_load_3d(&sm.g[s][0][0], &P.tm_g, x, y, b, bar);
     if constexpr (kHasZ) {
-      tma_load_3d(&sm.z[s][0][0], &P.tm_z, t0, c0, b, bar);
-      if constexpr (!kMulti) tma_load_3d(&sm.y[s][0][0], &P.tm_y, t0, c0, b, bar);
+      tma_load_3d(&sm.z[s][0][0], &P.tm_z, x, y, b, bar);
+      if constexpr (!kMulti) tma_load_3d(&sm.y[s][0][0], &P.tm_y, x, y, b, bar);
     }
     if constexpr (kVarB) tma_load_3d(&sm.Braw[s][0], &P.tm_B, t0, n0, b * f.ngroups + grp, bar);
     if constexpr (kVarC) tma_load_3d(&sm.Craw[s][0], &P.tm_C, t0, n0, b * f.ngroups + grp, bar);
@@ -248,10 +256,10 @@ __global__ void __launch_bounds__(32 * kNW, 3) ss_bwd_kernel(const __grid_consta
     // ---- element phase 1: delta', delta'u, dy, softplus slope, gate slope
     {
       float uv[S], dv[S], gv[S], zv[S];
-      lds_run<IT, S>(&sm.u[stg][pc][pq * S], uv);
-      lds_run<IT, S>(&sm.d[stg][pc][pq * S], dv);
-      lds_run<IT, S>(&sm.g[stg][pc][pq * S], gv);
-      if constexpr (kHasZ) lds_run<IT, S>(&sm.z[stg][pc][pq * S], zv);
+      lds_elems<IT, S, kBLD>(&sm.u[stg][0][0], pc, pq, uv);
+      lds_elems<IT, S, kBLD>(&sm.d[stg][0][0], pc, pq, dv);
+      lds_elems<IT, S, kBLD>(&sm.g[stg][0][0], pc, pq, gv);
+      if constexpr (kHasZ) lds_elems<IT, S, kBLD>(&sm.z[stg][0][0], pc, pq, zv);
       float dtv[S], dtuv[S], dyv[S], sgv[S], gzv[S];
 #pragma unroll
       for (int i = 0; i < S; ++i) {
@@ -279,10 +287,10 @@ __global__ void __launch_bounds__(32 * kNW, 3) ss_bwd_kernel(const __grid_consta
       }
 #pragma unroll
       for (int q = 0; q < S / 4; ++q) {
-        const int ch = swz(pc, pq * (S / 4) + q);
-        sm.dt_s[pc][ch] = make_float4(dtv[4 * q], dtv[4 * q + 1], dtv[4 * q + 2], dtv[4 * q + 3]);
-        sm.dtu_s[pc][ch] = make_float4(dtuv[4 * q], dtuv[4 * q + 1], dtuv[4 * q + 2], dtuv[4 * q + 3]);
-        sm.dy_s[pc][ch] = make_float4(dyv[4 * q], dyv[4 * q + 1], dyv[4 * q + 2], dyv[4 * q + 3]);
+        const int ch = pq * (S / 4) + q;
+        sm.dt_s[pc][erow<IT>(pc, ch)] = make_float4(dtv[4 * q], dtv[4 * q + 1], dtv[4 * q + 2], dtv[4 * q + 3]);
+        sm.dtu_s[pc][erow<IT>(pc, ch)] = make_float4(dtuv[4 * q], dtuv[4 * q + 1], dtuv[4 * q + 2], dtuv[4 * q + 3]);
+        sm.dy_s[pc][erow<IT>(pc, ch)] = make_float4(dyv[4 * q], dyv[4 * q + 1], dyv[4 * q + 2], dyv[4 * q + 3]);
         sm.sig_s[pc][ch] = make_float4(sgv[4 * q], sgv[4 * q + 1], sgv[4 * q + 2], sgv[4 * q + 3]);
         if constexpr (kHasZ)
           sm.gz_s[pc][ch] = make_float4(gzv[4 * q], gzv[4 * q + 1], gzv[4 * q + 2], gzv[4 * q + 3]);
@@ -302,13 +310,22 @@ __global__ void __launch_bounds__(32 * kNW, 3) ss_bwd_kernel(const __grid_consta
 
     // ---- scan phase, forward: the states of the tile in registers.  The decays are not
     //      kept (the reverse sweep recomputes them): MUFU has headroom, registers do not,
-    //      and the freed registers let the scheduler hide the shared-memory latencies.
+    //      and the freed registers let the scheduler hide the shared-memory latencies.  Each
+    //      group of 4 steps issues its 16 decays first (ordered ex2), ahead of the chain.
 #pragma unroll
     for (int i4 = 0; i4 < 4; ++i4) {
-      const float4 du4 = sm.dtu_s[lane][swz(lane, i4)];
-      const float4 dt4 = sm.dt_s[lane][swz(lane, i4)];
+      const float4 du4 = sm.dtu_s[lane][erow<IT>(lane, i4)];
+      const float4 dt4 = sm.dt_s[lane][erow<IT>(lane, i4)];
       const float dus[4] = {du4.x, du4.y, du4.z, du4.w};
       const float dts[4] = {dt4.x, dt4.y, dt4.z, dt4.w};
+      float2 dg[4][2];  // the group's decays, issued ahead of the chain that consumes them
+#pragma unroll
+      for (int st = 0; st < 4; ++st)
+#pragma unroll
+        for (int p = 0; p < 2; ++p) {
+          const float2 x = mul2(f2(dts[st]), A2[p]);
+          dg[st][p] = make_float2(ex2_ordered(x.x), ex2_ordered(x.y));
+        }
 #pragma unroll
       for (int st = 0; st < 4; ++st) {
         const int t = 4 * i4 + st;
@@ -322,10 +339,7 @@ __global__ void __launch_bounds__(32 * kNW, 3) ss_bwd_kernel(const __grid_consta
           Bv[1] = Bc[1];
         }
 #pragma unroll
-        for (int p = 0; p < 2; ++p) {
-          const float2 x = mul2(f2(dts[st]), A2[p]);
-          hp[t + 1][p] = fma2(make_float2(ex2(x.x), ex2(x.y)), hp[t][p], mul2(f2(dus[st]), Bv[p]));
-        }
+        for (int p = 0; p < 2; ++p) hp[t + 1][p] = fma2(dg[st][p], hp[t][p], mul2(f2(dus[st]), Bv[p]));
       }
     }
 
@@ -333,12 +347,20 @@ __global__ void __launch_bounds__(32 * kNW, 3) ss_bwd_kernel(const __grid_consta
     float* fold = kFold ? &sm.fold[w][0] : nullptr;
 #pragma unroll
     for (int i4 = 3; i4 >= 0; --i4) {
-      const float4 dt4 = sm.dt_s[lane][swz(lane, i4)];
-      const float4 du4 = sm.dtu_s[lane][swz(lane, i4)];
-      const float4 dy4 = sm.dy_s[lane][swz(lane, i4)];
+      const float4 dt4 = sm.dt_s[lane][erow<IT>(lane, i4)];
+      const float4 du4 = sm.dtu_s[lane][erow<IT>(lane, i4)];
+      const float4 dy4 = sm.dy_s[lane][erow<IT>(lane, i4)];
       const float dts[4] = {dt4.x, dt4.y, dt4.z, dt4.w};
       const float dus[4] = {du4.x, du4.y, du4.z, du4.w};
       const float dys[4] = {dy4.x, dy4.y, dy4.z, dy4.w};
+      float2 dg[4][2];  // the group's decays, issued ahead of the reverse steps
+#pragma unroll
+      for (int st = 3; st >= 0; --st)
+#pragma unroll
+        for (int p = 0; p < 2; ++p) {
+          const float2 x = mul2(f2(dts[st]), A2[p]);
+          dg[st][p] = make_float2(ex2_ordered(x.x), ex2_ordered(x.y));
+        }
 #pragma unroll
       for (int st = 3; st >= 0; --st) {
         const int t = 4 * i4 + st;
@@ -364,8 +386,7 @@ __global__ void __launch_bounds__(32 * kNW, 3) ss_bwd_kernel(const __grid_consta
 #pragma unroll
         for (int p = 0; p < 2; ++p) {
           const float2 dh = fma2(Cv[p], dy2, e2[p]);
-          const float2 x = mul2(dt2, A2[p]);
-          const float2 ee = mul2(make_float2(ex2(x.x), ex2(x.y)), dh);
+          const float2 ee = mul2(dg[st][p], dh);
           const float2 g = mul2(ee, hp[t][p]);
           dA2[p] = fma2(dt2, g, dA2[p]);
           s1 = fma2(Ad[p], g, s1);
@@ -373,10 +394,10 @@ __global__ void __launch_bounds__(32 * kNW, 3) ss_bwd_kernel(const __grid_consta
           const float2 vB = mul2(dh, du2);
           const float2 vC = mul2(dy2, hp[t + 1][p]);
           if constexpr (kVarB)
-            *reinterpret_cast<float2*>(fold + fold_off((st * 2 + p) * 2 + 0, lane >> 1) + 2 * (lane & 1)) = vB;
+            *reinterpret_cast<float2*>(fold + fold_off<IT>((st * 2 + p) * 2 + 0, lane >> 1) + 2 * (lane & 1)) = vB;
           else dBc[p] = add2(dBc[p], vB);
           if constexpr (kVarC)
-            *reinterpret_cast<float2*>(fold + fold_off((st * 2 + p) * 2 + 1, lane >> 1) + 2 * (lane & 1)) = vC;
+            *reinterpret_cast<float2*>(fold + fold_off<IT>((st * 2 + p) * 2 + 1, lane >> 1) + 2 * (lane & 1)) = vC;
           else dCc[p] = add2(dCc[p], vC);
           e2[p] = ee;
         }
@@ -393,7 +414,7 @@ __global__ void __launch_bounds__(32 * kNW, 3) ss_bwd_kernel(const __grid_consta
           float2 part[4];
 #pragma unroll
           for (int m = 0; m < 8; ++m) {
-            const float4 q = *reinterpret_cast<const float4*>(fold + fold_off(r, 2 * m + h));
+            const float4 q = *reinterpret_cast<const float4*>(fold + fold_off<IT>(r, 2 * m + h));
             const float2 s2q = add2(make_float2(q.x, q.y), make_float2(q.z, q.w));
             part[m & 3] = (m < 4) ? s2q : add2(part[m & 3], s2q);
           }
@@ -446,13 +467,13 @@ __global__ void __launch_bounds__(32 * kNW, 3) ss_bwd_kernel(const __grid_consta
       }
     } else {
       float uv[S], yv[S];
-      lds_run<IT, S>(&sm.u[stg][pc][pq * S], uv);
-      if constexpr (kHasZ) lds_run<IT, S>(&sm.y[stg][pc][pq * S], yv);
+      lds_elems<IT, S, kBLD>(&sm.u[stg][0][0], pc, pq, uv);
+      if constexpr (kHasZ) lds_elems<IT, S, kBLD>(&sm.y[stg][0][0], pc, pq, yv);
       float duv[S], ddv[S], dzv[S];
 #pragma unroll
       for (int q = 0; q < S / 4; ++q) {
-        const int ch = swz(pc, pq * (S / 4) + q);
-        const float4 dt4 = sm.dt_s[pc][ch], dy4 = sm.dy_s[pc][ch], sg4 = sm.sig_s[pc][ch];
+        const int ch = pq * (S / 4) + q;
+        const float4 dt4 = sm.dt_s[pc][erow<IT>(pc, ch)], dy4 = sm.dy_s[pc][erow<IT>(pc, ch)], sg4 = sm.sig_s[pc][ch];
         float4 gz4 = make_float4(0.f, 0.f, 0.f, 0.f);
         if constexpr (kHasZ) gz4 = sm.gz_s[pc][ch];
         const float dts[4] = {dt4.x, dt4.y, dt4.z, dt4.w};
@@ -474,9 +495,10 @@ __global__ void __launch_bounds__(32 * kNW, 3) ss_bwd_kernel(const __grid_consta
         }
       }
       const int nv = pc_ok ? max(0, min(S, tlen - pq * S)) : 0;
-      store_run<IT, S>(du_row + t0 + pq * S, duv, nv, P.vec_du);
-      store_run<IT, S>(dd_row + t0 + pq * S, ddv, nv, P.vec_dd);
-      if constexpr (kHasZ) store_run<IT, S>(dz_row + t0 + pq * S, dzv, nv, P.vec_dz);
+      store_elems<IT, S, kBLD>(du_row, step_stride<kBLD>(a.du_dim_stride), t0 + pq * S, duv, nv, P.vec_du);
+      store_elems<IT, S, kBLD>(dd_row, step_stride<kBLD>(a.ddelta_dim_stride), t0 + pq * S, ddv, nv, P.vec_dd);
+      if constexpr (kHasZ)
+        store_elems<IT, S, kBLD>(dz_row, step_stride<kBLD>(a.dz_dim_stride), t0 + pq * S, dzv, nv, P.vec_dz);
     }
     __syncthreads();
     if constexpr (kTMA) {
@@ -500,13 +522,16 @@ __global__ void __launch_bounds__(32 * kNW, 3) ss_bwd_kernel(const __grid_consta
     }
   }
   if constexpr (!kMulti) {  // (state groups: bwd_finish_kernel accumulates dD and ddelta_bias)
-    // the kNW element-role threads of a channel are adjacent lanes
+    if constexpr (!kBLD) {
+      // the kNW element-role threads of a channel are adjacent lanes
 #pragma unroll
-    for (int o = 1; o < kNW; o <<= 1) {
-      dD_acc += __shfl_xor_sync(0xffffffffu, dD_acc, o);
-      db_acc += __shfl_xor_sync(0xffffffffu, db_acc, o);
+      for (int o = 1; o < kNW; o <<= 1) {
+        dD_acc += __shfl_xor_sync(0xffffffffu, dD_acc, o);
+        db_acc += __shfl_xor_sync(0xffffffffu, db_acc, o);
+      }
     }
-    if (pq == 0 && pc_ok) {
+    // ((b, L, d) tiles: the kNW threads of a channel sit in different warps and each adds its own)
+    if ((kBLD || pq == 0) && pc_ok) {
       if (a.dD != nullptr) red_add(a.dD + c0 + pc, dD_acc);
       if (a.ddelta_bias != nullptr) red_add(a.ddelta_bias + c0 + pc, db_acc);
     }

@@ -94,13 +94,29 @@ bool map3(CUtensorMap* m, const void* base, int dt, uint64_t d0, uint64_t d1, ui
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-// (batch, dim, seqlen) view with element strides -> box of 16 steps x 32 channels
+// A per-element tensor -> box of 16 steps x 32 channels.  (batch, dim, seqlen) layout: extents
+// (seqlen, dim, batch), ds = dim stride; (batch, seqlen, dim) layout: extents (dim, seqlen,
+// batch), ds = seqlen stride (the box lands as [step][channel]).
 bool map_rows(CUtensorMap* m, const void* p, int dt, const ss_fwd_args& a, int64_t bs, int64_t ds) {
   const uint64_t es = dt == SS_F32 ? 4 : 2;
+  if (ds < 0 || bs < 0) return false;
+  if (a.layout == SS_LAYOUT_BLD) {
+    const uint64_t s1 = a.seqlen > 1 ? (uint64_t)ds * es : (uint64_t)a.dim * es;
+    const uint64_t s2 = a.batch > 1 ? (uint64_t)bs * es : s1 * (uint64_t)a.seqlen;
+    return map3(m, p, dt, (uint64_t)a.dim, (uint64_t)a.seqlen, (uint64_t)a.batch, s1, s2, ssb::kCh, ssb::kTile);
+  }
   const uint64_t s1 = a.dim > 1 ? (uint64_t)ds * es : (uint64_t)a.seqlen * es;
   const uint64_t s2 = a.batch > 1 ? (uint64_t)bs * es : s1 * (uint64_t)a.dim;
-  if (ds < 0 || bs < 0) return false;
   return map3(m, p, dt, (uint64_t)a.seqlen, (uint64_t)a.dim, (uint64_t)a.batch, s1, s2, ssb::kTile, ssb::kCh);
+}
+
+// (batch, seqlen, dim) calls: every tile's first channel (the tensor maps' innermost
+// coordinate) must start 16 bytes apart, i.e. the channels of a group must span whole 16-byte
+// units when there are several groups
+bool bld_channels_aligned(const ss_fwd_args& a) {
+  const int64_t dpg = a.dim / a.ngroups;
+  const int64_t es = a.io_dtype == SS_F32 ? 4 : 2;
+  return a.ngroups == 1 || (dpg * es) % 16 == 0;
 }
 
 // variable B / C (batch, ngroups, dstate, seqlen) -> box of 16 steps x (padded) dstate
@@ -142,6 +158,8 @@ int check_fwd(const ss_fwd_args* a) {
   }
   if (!dtype_ok(a->io_dtype) || !dtype_ok(a->bc_dtype)) return SS_ERR_UNSUPPORTED;
   if (a->bc_dtype != SS_F32 && a->bc_dtype != a->io_dtype) return SS_ERR_UNSUPPORTED;
+  if (a->layout != SS_LAYOUT_BDL && a->layout != SS_LAYOUT_BLD) return SS_ERR_INVALID;
+  if (a->layout == SS_LAYOUT_BLD && (nsg > 1 || !bld_channels_aligned(*a))) return SS_ERR_UNSUPPORTED;
   // empty (batch, dim, seqlen) tensors may carry null data pointers; A and constant B / C never are empty
   const bool empty = a->batch == 0 || a->seqlen == 0;
   if (!a->A || (!a->var_B && !a->B) || (!a->var_C && !a->C)) return SS_ERR_INVALID;
@@ -324,6 +342,7 @@ int ss_fwd(const ss_fwd_args* args, void* stream) {
   if (tma && a.z) tma = map_rows(&P.tm_z, a.z, a.io_dtype, a, a.z_batch_stride, a.z_dim_stride);
   if (tma && a.var_B) tma = map_bc(&P.tm_B, a.B, a);
   if (tma && a.var_C) tma = map_bc(&P.tm_C, a.C, a);
+  if (!tma && a.layout == SS_LAYOUT_BLD) return SS_ERR_UNSUPPORTED;  // (b, L, d) tiles need tensor maps
   if (tma && set_chunks(P, fwd_chunk_count(a.batch, P.nct, P.ntiles), a) > 1) {
     P.cstate = a.work;
     P.csum = a.work + (size_t)a.batch * P.nchunk * a.dstate * (size_t)a.dim;
@@ -337,18 +356,20 @@ int ss_bwd(const ss_bwd_args* args, void* stream) {
   if (rc != SS_OK) return rc;
   const ss_fwd_args& f = args->f;
   cudaStream_t st = (cudaStream_t)stream;
-  // accumulated outputs start from zero
-  const size_t nA = (size_t)f.dim * f.dstate;
-  const size_t nBv = (size_t)f.batch * f.ngroups * f.dstate * (size_t)f.seqlen;
-  const size_t nB = f.var_B ? nBv : nA, nC = f.var_C ? nBv : nA;
-  cudaError_t e = cudaMemsetAsync(args->dA, 0, nA * sizeof(float), st);
-  if (e == cudaSuccess && nB) e = cudaMemsetAsync(args->dB, 0, nB * sizeof(float), st);
-  if (e == cudaSuccess && nC) e = cudaMemsetAsync(args->dC, 0, nC * sizeof(float), st);
-  if (e == cudaSuccess && args->dD) e = cudaMemsetAsync(args->dD, 0, (size_t)f.dim * sizeof(float), st);
-  if (e == cudaSuccess && args->ddelta_bias)
-    e = cudaMemsetAsync(args->ddelta_bias, 0, (size_t)f.dim * sizeof(float), st);
-  if (e != cudaSuccess) return cuda_status(e);
-  if (f.batch == 0 || f.seqlen == 0) return SS_OK;
+  // accumulated outputs start from zero (zeroed once the call is known to run)
+  auto zero_sums = [&]() {
+    const size_t nA = (size_t)f.dim * f.dstate;
+    const size_t nBv = (size_t)f.batch * f.ngroups * f.dstate * (size_t)f.seqlen;
+    const size_t nB = f.var_B ? nBv : nA, nC = f.var_C ? nBv : nA;
+    cudaError_t e = cudaMemsetAsync(args->dA, 0, nA * sizeof(float), st);
+    if (e == cudaSuccess && nB) e = cudaMemsetAsync(args->dB, 0, nB * sizeof(float), st);
+    if (e == cudaSuccess && nC) e = cudaMemsetAsync(args->dC, 0, nC * sizeof(float), st);
+    if (e == cudaSuccess && args->dD) e = cudaMemsetAsync(args->dD, 0, (size_t)f.dim * sizeof(float), st);
+    if (e == cudaSuccess && args->ddelta_bias)
+      e = cudaMemsetAsync(args->ddelta_bias, 0, (size_t)f.dim * sizeof(float), st);
+    return e;
+  };
+  if (f.batch == 0 || f.seqlen == 0) return cuda_status(zero_sums());
   ssb::BwdK P{};
   P.a = *args;
   derive(f, P);
@@ -383,10 +404,13 @@ int ss_bwd(const ss_bwd_args* args, void* stream) {
   } else if (tma && P.ntiles > 1) {
     tma = false;
   }
+  if (!tma && f.layout == SS_LAYOUT_BLD) return SS_ERR_UNSUPPORTED;  // (b, L, d) tiles need tensor maps
   if (tma && set_chunks(P, bwd_chunk_count(f.batch, P.nct, P.ntiles), f) > 1) {
     P.ccarry = f.work;
     P.csum = f.work + (size_t)f.batch * P.nchunk * f.dstate * (size_t)f.dim;
   }
+  cudaError_t e = zero_sums();
+  if (e != cudaSuccess) return cuda_status(e);
   return dispatch(f.io_dtype, [&](auto tag) { return ssb::launch_bwd<decltype(tag)>(P, st, tma); });
 }
 

@@ -34,11 +34,33 @@ struct FwdChunkSmem {
   alignas(128) IT u[kChunkStages][kCh][kTile];
   alignas(128) IT d[kChunkStages][kCh][kTile];
   alignas(128) float Braw[kVarB ? kChunkStages : 1][NS * kTile];
-  alignas(16) float4 dt_s[kCh][4];
-  alignas(16) float4 dtu_s[kCh][4];
+  alignas(16) float4 dt_s[kCh][kElemRow<IT>];
+  alignas(16) float4 dtu_s[kCh][kElemRow<IT>];
   alignas(16) float B_s[kVarB ? kTile : 1][NS];
+  float part[kNW][kCh];  // per-warp partial sums of delta' ((b, L, d) tiles)
   alignas(8) uint64_t full[kChunkStages];
 };
+
+// Sum over the kNW element-role threads of channel pc of a per-thread partial, written by one of
+// them to dst[pc] (pc < nvalid).  [channel][step] tiles: the threads are adjacent lanes (shuffles);
+// [step][channel] tiles: they are lane pc of every warp (through shared memory).
+template <int kNW, bool kBLD>
+__device__ __forceinline__ void store_channel_sum(float v, float (*part)[kCh], float* dst, int pc, int pq, int nvalid) {
+  if constexpr (kBLD) {
+    part[pq][pc] = v;
+    __syncthreads();
+    if (pq == 0 && pc < nvalid) {
+      float sum = 0.f;
+#pragma unroll
+      for (int g = 0; g < kNW; ++g) sum += part[g][pc];
+      dst[pc] = sum;
+    }
+  } else {
+#pragma unroll
+    for (int o = 1; o < kNW; o <<= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    if (pq == 0 && pc < nvalid) dst[pc] = v;
+  }
+}
 
 // Bounded wait for ring slot `stg`; on a timeout every thread learns of it, thread 0 raises the
 // status bit and waits (with the default limit) for the copies of local tiles i .. issued - 1,
@@ -59,7 +81,7 @@ __device__ __forceinline__ bool chunk_wait_failed(uint64_t* full, int stg, int i
 
 // Forward chunk summaries: grid = batch x channel tiles x (nchunk - 1); CTA = (32 channels,
 // chunk j < nchunk - 1), lane = channel, warp w = states 4w .. 4w+3 (as ss_fwd_kernel).
-template <typename IT, int kNW, bool kVarB>
+template <typename IT, int kNW, bool kVarB, bool kBLD>
 __global__ void __launch_bounds__(32 * kNW, 4) ss_fwd_chunk_kernel(const __grid_constant__ FwdK P) {
   constexpr int NS = kSPW * kNW;
   constexpr int S = kTile / kNW;
@@ -102,7 +124,7 @@ __global__ void __launch_bounds__(32 * kNW, 4) ss_fwd_chunk_kernel(const __grid_
     Bc[p] = make_float2(bv[0], bv[1]);
     h[p] = make_float2(0.f, 0.f);
   }
-  const int pc = tid / kNW, pq = tid % kNW;
+  const int pc = elem_pc<kNW, kBLD>(tid), pq = elem_pq<kNW, kBLD>(tid);
   const bool pc_ok = pc < nvalid;
   const float bias = (a.delta_bias != nullptr && pc_ok) ? a.delta_bias[c0 + pc] : 0.f;
   float dt_sum = 0.f;
@@ -113,8 +135,9 @@ __global__ void __launch_bounds__(32 * kNW, 4) ss_fwd_chunk_kernel(const __grid_
     uint64_t* bar = &sm.full[s];
     mbar_expect_tx(bar, stage_bytes);
     const int t0 = (kb + i) * kTile;
-    tma_load_3d(&sm.u[s][0][0], &P.tm_u, t0, c0, b, bar);
-    tma_load_3d(&sm.d[s][0][0], &P.tm_d, t0, c0, b, bar);
+    const int x = kBLD ? c0 : t0, y = kBLD ? t0 : c0;  // (b, L, d) maps run along the channels
+    tma_load_3d(&sm.u[s][0][0], &P.tm_u, x, y, b, bar);
+    tma_load_3d(&sm.d[s][0][0], &P.tm_d, x, y, b, bar);
     if constexpr (kVarB) tma_load_3d(&sm.Braw[s][0], &P.tm_B, t0, 0, b * a.ngroups + grp, bar);
   };
   if (tid == 0) {
@@ -133,8 +156,8 @@ __global__ void __launch_bounds__(32 * kNW, 4) ss_fwd_chunk_kernel(const __grid_
     if (w == 0) widen_bc_warp<IT, NS, kVarB, false>(sm.B_s, sm.B_s, sm.Braw[stg], sm.Braw[stg], bc_f32, lane);
     {
       float uv[S], dv[S], dtv[S], dtuv[S];
-      lds_run<IT, S>(&sm.u[stg][pc][pq * S], uv);
-      lds_run<IT, S>(&sm.d[stg][pc][pq * S], dv);
+      lds_elems<IT, S, kBLD>(&sm.u[stg][0][0], pc, pq, uv);
+      lds_elems<IT, S, kBLD>(&sm.d[stg][0][0], pc, pq, dv);
 #pragma unroll
       for (int k = 0; k < S; ++k) {
         const bool ok = pc_ok && pq * S + k < tlen;
@@ -147,9 +170,9 @@ __global__ void __launch_bounds__(32 * kNW, 4) ss_fwd_chunk_kernel(const __grid_
       }
 #pragma unroll
       for (int q = 0; q < S / 4; ++q) {
-        const int ch = swz(pc, pq * (S / 4) + q);
-        sm.dt_s[pc][ch] = make_float4(dtv[4 * q], dtv[4 * q + 1], dtv[4 * q + 2], dtv[4 * q + 3]);
-        sm.dtu_s[pc][ch] = make_float4(dtuv[4 * q], dtuv[4 * q + 1], dtuv[4 * q + 2], dtuv[4 * q + 3]);
+        const int ch = pq * (S / 4) + q;
+        sm.dt_s[pc][erow<IT>(pc, ch)] = make_float4(dtv[4 * q], dtv[4 * q + 1], dtv[4 * q + 2], dtv[4 * q + 3]);
+        sm.dtu_s[pc][erow<IT>(pc, ch)] = make_float4(dtuv[4 * q], dtuv[4 * q + 1], dtuv[4 * q + 2], dtuv[4 * q + 3]);
       }
     }
     __syncthreads();
@@ -157,8 +180,8 @@ __global__ void __launch_bounds__(32 * kNW, 4) ss_fwd_chunk_kernel(const __grid_
     if (tid == 0 && i + kChunkStages < nt) issue(i + kChunkStages, stg);
 #pragma unroll
     for (int i4 = 0; i4 < 4; ++i4) {
-      const float4 dt4 = sm.dt_s[lane][swz(lane, i4)];
-      const float4 du4 = sm.dtu_s[lane][swz(lane, i4)];
+      const float4 dt4 = sm.dt_s[lane][erow<IT>(lane, i4)];
+      const float4 du4 = sm.dtu_s[lane][erow<IT>(lane, i4)];
       const float dts[4] = {dt4.x, dt4.y, dt4.z, dt4.w};
       const float dus[4] = {du4.x, du4.y, du4.z, du4.w};
 #pragma unroll
@@ -193,9 +216,7 @@ __global__ void __launch_bounds__(32 * kNW, 4) ss_fwd_chunk_kernel(const __grid_
       if (n < N) cs[(int64_t)n * a.dim] = hv[j];
     }
   }
-#pragma unroll
-  for (int o = 1; o < kNW; o <<= 1) dt_sum += __shfl_xor_sync(0xffffffffu, dt_sum, o);
-  if (pq == 0 && pc_ok) P.csum[bj * a.dim + c0 + pc] = dt_sum;
+  store_channel_sum<kNW, kBLD>(dt_sum, sm.part, P.csum + bj * a.dim + c0, pc, pq, nvalid);
 }
 
 template <typename IT, int kNW, bool kVarC, bool kHasZ>
@@ -205,15 +226,16 @@ struct BwdCarrySmem {
   alignas(128) IT g[kChunkStages][kCh][kTile];
   alignas(128) IT z[kHasZ ? kChunkStages : 1][kCh][kTile];
   alignas(128) IT Craw[kVarC ? kChunkStages : 1][NS * kTile];
-  alignas(16) float4 dt_s[kCh][4];
-  alignas(16) float4 dy_s[kCh][4];
+  alignas(16) float4 dt_s[kCh][kElemRow<IT>];
+  alignas(16) float4 dy_s[kCh][kElemRow<IT>];
   alignas(16) float C_s[kVarC ? kTile : 1][NS];
+  float part[kNW][kCh];
   alignas(8) uint64_t full[kChunkStages];
 };
 
 // Backward chunk summaries: grid = batch x channel tiles x (nchunk - 1); CTA = (32 channels,
 // chunk j >= 1), tiles visited last to first as in ss_bwd_kernel.
-template <typename IT, int kNW, bool kVarC, bool kHasZ>
+template <typename IT, int kNW, bool kVarC, bool kHasZ, bool kBLD>
 __global__ void __launch_bounds__(32 * kNW, 4) ss_bwd_carry_kernel(const __grid_constant__ BwdK P) {
   constexpr int NS = kSPW * kNW;
   constexpr int S = kTile / kNW;
@@ -257,7 +279,7 @@ __global__ void __launch_bounds__(32 * kNW, 4) ss_bwd_carry_kernel(const __grid_
     Cc[p] = make_float2(cv[0], cv[1]);
     e2[p] = make_float2(0.f, 0.f);
   }
-  const int pc = tid / kNW, pq = tid % kNW;
+  const int pc = elem_pc<kNW, kBLD>(tid), pq = elem_pq<kNW, kBLD>(tid);
   const bool pc_ok = pc < nvalid;
   const float bias = (f.delta_bias != nullptr && pc_ok) ? f.delta_bias[c0 + pc] : 0.f;
   float dt_sum = 0.f;
@@ -268,9 +290,10 @@ __global__ void __launch_bounds__(32 * kNW, 4) ss_bwd_carry_kernel(const __grid_
     uint64_t* bar = &sm.full[s];
     mbar_expect_tx(bar, stage_bytes);
     const int t0 = (kb + nt - 1 - i) * kTile;
-    tma_load_3d(&sm.d[s][0][0], &P.tm_d, t0, c0, b, bar);
-    tma_load_3d(&sm.g[s][0][0], &P.tm_g, t0, c0, b, bar);
-    if constexpr (kHasZ) tma_load_3d(&sm.z[s][0][0], &P.tm_z, t0, c0, b, bar);
+    const int x = kBLD ? c0 : t0, y = kBLD ? t0 : c0;
+    tma_load_3d(&sm.d[s][0][0], &P.tm_d, x, y, b, bar);
+    tma_load_3d(&sm.g[s][0][0], &P.tm_g, x, y, b, bar);
+    if constexpr (kHasZ) tma_load_3d(&sm.z[s][0][0], &P.tm_z, x, y, b, bar);
     if constexpr (kVarC) tma_load_3d(&sm.Craw[s][0], &P.tm_C, t0, 0, b * f.ngroups + grp, bar);
   };
   if (tid == 0) {
@@ -289,9 +312,9 @@ __global__ void __launch_bounds__(32 * kNW, 4) ss_bwd_carry_kernel(const __grid_
     if (w == 0) widen_bc_warp<IT, NS, false, kVarC>(sm.C_s, sm.C_s, sm.Craw[stg], sm.Craw[stg], false, lane);
     {
       float dv[S], gv[S], zv[S], dtv[S], dyv[S];
-      lds_run<IT, S>(&sm.d[stg][pc][pq * S], dv);
-      lds_run<IT, S>(&sm.g[stg][pc][pq * S], gv);
-      if constexpr (kHasZ) lds_run<IT, S>(&sm.z[stg][pc][pq * S], zv);
+      lds_elems<IT, S, kBLD>(&sm.d[stg][0][0], pc, pq, dv);
+      lds_elems<IT, S, kBLD>(&sm.g[stg][0][0], pc, pq, gv);
+      if constexpr (kHasZ) lds_elems<IT, S, kBLD>(&sm.z[stg][0][0], pc, pq, zv);
 #pragma unroll
       for (int k = 0; k < S; ++k) {
         const bool ok = pc_ok && pq * S + k < tlen;
@@ -307,17 +330,17 @@ __global__ void __launch_bounds__(32 * kNW, 4) ss_bwd_carry_kernel(const __grid_
       }
 #pragma unroll
       for (int q = 0; q < S / 4; ++q) {
-        const int ch = swz(pc, pq * (S / 4) + q);
-        sm.dt_s[pc][ch] = make_float4(dtv[4 * q], dtv[4 * q + 1], dtv[4 * q + 2], dtv[4 * q + 3]);
-        sm.dy_s[pc][ch] = make_float4(dyv[4 * q], dyv[4 * q + 1], dyv[4 * q + 2], dyv[4 * q + 3]);
+        const int ch = pq * (S / 4) + q;
+        sm.dt_s[pc][erow<IT>(pc, ch)] = make_float4(dtv[4 * q], dtv[4 * q + 1], dtv[4 * q + 2], dtv[4 * q + 3]);
+        sm.dy_s[pc][erow<IT>(pc, ch)] = make_float4(dyv[4 * q], dyv[4 * q + 1], dyv[4 * q + 2], dyv[4 * q + 3]);
       }
     }
     __syncthreads();
     if (tid == 0 && i + kChunkStages < nt) issue(i + kChunkStages, stg);
 #pragma unroll
     for (int i4 = 3; i4 >= 0; --i4) {
-      const float4 dt4 = sm.dt_s[lane][swz(lane, i4)];
-      const float4 dy4 = sm.dy_s[lane][swz(lane, i4)];
+      const float4 dt4 = sm.dt_s[lane][erow<IT>(lane, i4)];
+      const float4 dy4 = sm.dy_s[lane][erow<IT>(lane, i4)];
       const float dts[4] = {dt4.x, dt4.y, dt4.z, dt4.w};
       const float dys[4] = {dy4.x, dy4.y, dy4.z, dy4.w};
 #pragma unroll
@@ -353,9 +376,7 @@ __global__ void __launch_bounds__(32 * kNW, 4) ss_bwd_carry_kernel(const __grid_
       if (n < N) cc[(int64_t)n * f.dim] = ev[j];
     }
   }
-#pragma unroll
-  for (int o = 1; o < kNW; o <<= 1) dt_sum += __shfl_xor_sync(0xffffffffu, dt_sum, o);
-  if (pq == 0 && pc_ok) P.csum[bj * f.dim + c0 + pc] = dt_sum;
+  store_channel_sum<kNW, kBLD>(dt_sum, sm.part, P.csum + bj * f.dim + c0, pc, pq, nvalid);
 }
 
 }  // namespace ssb

@@ -254,10 +254,17 @@ __device__ __forceinline__ void load_bc_tile(float (*dst)[NS], const T* __restri
   }
 }
 
-// Swizzled [32 rows][4 float4 chunks] layout: chunk q of row r lives at q ^ ((r >> 1) & 3),
-// which makes both "lane r reads its chunk i" and "lanes write consecutive chunks"
-// conflict-free for 16-byte shared-memory accesses.
-__device__ __forceinline__ int swz(int r, int q) { return q ^ ((r >> 1) & 3); }
+// Per-element arrays of a tile ([32 channels][16 steps] as [channel][4 float4]), read by lane
+// = channel, one float4 at a time.  With 2-byte I/O their rows are padded to kElemRow = 5 float4
+// (80 bytes): "lane r reads float4 i of its row" then hits 8 distinct 16-byte bank groups per
+// quarter warp, with no swizzle, so the address is a per-lane base plus a constant.  With 4-byte
+// I/O the larger tiles leave no room for the pad (it would cost a CTA per SM), so the rows keep
+// 4 float4 and float4 q of row r is stored at q ^ ((r >> 1) & 3), which makes the same reads
+// conflict-free.
+template <typename IT> constexpr int kElemRow = sizeof(IT) == 2 ? 5 : 4;
+template <typename IT> __device__ __forceinline__ int erow(int r, int q) {
+  return sizeof(IT) == 2 ? q : (q ^ ((r >> 1) & 3));
+}
 
 // Store S consecutive values of one row of a (.., dim, seqlen) tensor (S = 4, 8 or 16),
 // vectorized when aligned and complete.
@@ -294,6 +301,48 @@ __device__ __forceinline__ void store_run(T* __restrict__ dst, const float (&v)[
 #pragma unroll
     for (int i = 0; i < S; ++i)
       if (i < nvalid) dst[i] = from_f<T>(v[i]);
+  }
+}
+
+// ---- element phases over (b, d, L) or (b, L, d) tiles ---------------------------------
+// A tile of a per-element tensor arrives from TMA as [channel][step] for the (batch, dim,
+// seqlen) layout (kBLD = false) and as [step][channel] for (batch, seqlen, dim) (kBLD = true).
+// Element-phase thread (pc, pq) handles channel pc and steps pq*S .. pq*S + S - 1:
+//   [channel][step] tiles: pc = tid / kNW, pq = tid % kNW — a channel's 16 steps are one
+//     contiguous run, read with vector loads and stored as vectors;
+//   [step][channel] tiles: pc = lane, pq = warp — a step's 32 channels are one contiguous run,
+//     read by the 32 lanes together (one wavefront) and stored coalesced along the channels.
+template <int kNW, bool kBLD> __device__ __forceinline__ int elem_pc(int tid) { return kBLD ? (tid & 31) : tid / kNW; }
+template <int kNW, bool kBLD> __device__ __forceinline__ int elem_pq(int tid) { return kBLD ? (tid >> 5) : tid % kNW; }
+
+// S consecutive steps of channel pc from a ring tile, as floats
+template <typename IT, int S, bool kBLD>
+__device__ __forceinline__ void lds_elems(const IT* tile, int pc, int pq, float (&v)[S]) {
+  if constexpr (kBLD) {
+#pragma unroll
+    for (int i = 0; i < S; ++i) v[i] = to_f<IT>(tile[(pq * S + i) * kCh + pc]);
+  } else {
+    lds_run<IT, S>(tile + pc * kTile + pq * S, v);
+  }
+}
+
+// Offset of (batch b, channel c, step 0) of a per-element tensor; consecutive steps are then
+// step_stride<kBLD>(ds) elements apart (ds: the tensor's *_dim_stride field, which holds the
+// seqlen stride for (b, L, d))
+template <bool kBLD> __device__ __forceinline__ int64_t row_off(int64_t b, int64_t bs, int64_t c, int64_t ds) {
+  return b * bs + c * (kBLD ? 1 : ds);
+}
+template <bool kBLD> __device__ __forceinline__ int64_t step_stride(int64_t ds) { return kBLD ? ds : 1; }
+
+// Store S consecutive steps (from step t) of one channel's row
+template <typename IT, int S, bool kBLD>
+__device__ __forceinline__ void store_elems(IT* row, int64_t ds, int t, const float (&v)[S], int nvalid, bool vec) {
+  if constexpr (kBLD) {
+#pragma unroll
+    for (int i = 0; i < S; ++i)
+      if (i < nvalid) row[(int64_t)(t + i) * ds] = from_f<IT>(v[i]);
+  } else {
+    store_run<IT, S>(row + t, v, nvalid, vec);
   }
 }
 

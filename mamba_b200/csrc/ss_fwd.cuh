@@ -42,8 +42,8 @@ struct FwdSmem {
   alignas(128) IT z[kHasZ ? kStages : 1][kCh][kTile];
   alignas(128) float Braw[kVarB ? kStages : 1][NS * kTile];  // TMA tile of B (its own dtype)
   alignas(128) float Craw[kVarC ? kStages : 1][NS * kTile];
-  alignas(16) float4 dt_s[kCh][4];
-  alignas(16) float4 dtu_s[kCh][4];
+  alignas(16) float4 dt_s[kCh][kElemRow<IT>];
+  alignas(16) float4 dtu_s[kCh][kElemRow<IT>];
   alignas(16) float B_s[kVarB ? kTile : 1][NS];
   float bc_pad[16];  // puts C_s rows on the other half of the banks from B_s rows
   alignas(16) float C_s[kVarC ? kTile : 1][NS];
@@ -88,9 +88,10 @@ __device__ __forceinline__ void widen_bc_warp(float (*Bd)[NS], float (*Cd)[NS], 
   for (int t = 0; t < kTile; ++t) dst[t][n] = v[t];
 }
 
-template <typename IT, int kNW, bool kVarB, bool kVarC, bool kHasZ, bool kTMA, bool kMulti = false>
+template <typename IT, int kNW, bool kVarB, bool kVarC, bool kHasZ, bool kTMA, bool kMulti = false, bool kBLD = false>
 __global__ void __launch_bounds__(32 * kNW, 4) ss_fwd_kernel(const __grid_constant__ FwdK P) {
   static_assert(!(kMulti && kHasZ), "state groups apply the gate in fwd_finish_kernel");
+  static_assert(!kBLD || (kTMA && !kMulti), "(b, L, d) tiles come from tensor maps, dstate <= 16");
   constexpr int NT = 32 * kNW;
   constexpr int NS = kSPW * kNW;   // states covered by the CTA (dstate padded up)
   constexpr int S = kTile / kNW;   // steps per thread in the element-wise phases
@@ -159,14 +160,16 @@ __global__ void __launch_bounds__(32 * kNW, 4) ss_fwd_kernel(const __grid_consta
   }
 
   // ---- element role: channel c0 + pc, steps pq*S .. pq*S + S - 1 of each tile
-  const int pc = tid / kNW, pq = tid % kNW;
+  const int pc = elem_pc<kNW, kBLD>(tid), pq = elem_pq<kNW, kBLD>(tid);
   const bool pc_ok = pc < nvalid;
   const float Dv = (a.D != nullptr && pc_ok) ? a.D[c0 + pc] : 0.f;
   const float bias = (a.delta_bias != nullptr && pc_ok) ? a.delta_bias[c0 + pc] : 0.f;
-  IT* orow = (IT*)a.out + (int64_t)b * a.out_batch_stride + (int64_t)(c0 + pc) * a.out_dim_stride;
+  IT* orow = (IT*)a.out + row_off<kBLD>(b, a.out_batch_stride, c0 + pc, a.out_dim_stride);
+  const int64_t ostep = step_stride<kBLD>(a.out_dim_stride);
   IT* yrow = (kHasZ && a.out_y != nullptr)
-                 ? (IT*)a.out_y + (int64_t)b * a.out_y_batch_stride + (int64_t)(c0 + pc) * a.out_y_dim_stride
+                 ? (IT*)a.out_y + row_off<kBLD>(b, a.out_y_batch_stride, c0 + pc, a.out_y_dim_stride)
                  : nullptr;
+  const int64_t ystep = step_stride<kBLD>(a.out_y_dim_stride);
   const int64_t bc_off = (((int64_t)b * a.ngroups + grp) * N + n0) * (int64_t)L;  // row n0 of this group
 
   // ---- producer (thread 0): TMA ring
@@ -177,9 +180,10 @@ __global__ void __launch_bounds__(32 * kNW, 4) ss_fwd_kernel(const __grid_consta
     uint64_t* bar = &sm.full[s];
     mbar_expect_tx(bar, stage_bytes);
     const int t0 = (kb + i) * kTile;
-    tma_load_3d(&sm.u[s][0][0], &P.tm_u, t0, c0, b, bar);
-    tma_load_3d(&sm.d[s][0][0], &P.tm_d, t0, c0, b, bar);
-    if constexpr (kHasZ) tma_load_3d(&sm.z[s][0][0], &P.tm_z, t0, c0, b, bar);
+    const int x = kBLD ? c0 : t0, y = kBLD ? t0 : c0;  // (b, L, d) maps run along the channels
+    tma_load_3d(&sm.u[s][0][0], &P.tm_u, x, y, b, bar);
+    tma_load_3d(&sm.d[s][0][0], &P.tm_d, x, y, b, bar);
+    if constexpr (kHasZ) tma_load_3d(&sm.z[s][0][0], &P.tm_z, x, y, b, bar);
     if constexpr (kVarB) tma_load_3d(&sm.Braw[s][0], &P.tm_B, t0, n0, b * a.ngroups + grp, bar);
     if constexpr (kVarC) tma_load_3d(&sm.Craw[s][0], &P.tm_C, t0, n0, b * a.ngroups + grp, bar);
   };
@@ -226,8 +230,8 @@ __global__ void __launch_bounds__(32 * kNW, 4) ss_fwd_kernel(const __grid_consta
     //         so the states pass through them unchanged)
     {
       float uv[S], dv[S], dtv[S], dtuv[S];
-      lds_run<IT, S>(&sm.u[stg][pc][pq * S], uv);
-      lds_run<IT, S>(&sm.d[stg][pc][pq * S], dv);
+      lds_elems<IT, S, kBLD>(&sm.u[stg][0][0], pc, pq, uv);
+      lds_elems<IT, S, kBLD>(&sm.d[stg][0][0], pc, pq, dv);
 #pragma unroll
       for (int i = 0; i < S; ++i) {
         const int t = pq * S + i;
@@ -240,9 +244,9 @@ __global__ void __launch_bounds__(32 * kNW, 4) ss_fwd_kernel(const __grid_consta
       }
 #pragma unroll
       for (int q = 0; q < S / 4; ++q) {
-        const int ch = swz(pc, pq * (S / 4) + q);
-        sm.dt_s[pc][ch] = make_float4(dtv[4 * q], dtv[4 * q + 1], dtv[4 * q + 2], dtv[4 * q + 3]);
-        sm.dtu_s[pc][ch] = make_float4(dtuv[4 * q], dtuv[4 * q + 1], dtuv[4 * q + 2], dtuv[4 * q + 3]);
+        const int ch = pq * (S / 4) + q;
+        sm.dt_s[pc][erow<IT>(pc, ch)] = make_float4(dtv[4 * q], dtv[4 * q + 1], dtv[4 * q + 2], dtv[4 * q + 3]);
+        sm.dtu_s[pc][erow<IT>(pc, ch)] = make_float4(dtuv[4 * q], dtuv[4 * q + 1], dtuv[4 * q + 2], dtuv[4 * q + 3]);
       }
     }
     if (__syncthreads_or(failed)) {  // (every thread has also finished the previous tile's epilogue)
@@ -268,7 +272,7 @@ __global__ void __launch_bounds__(32 * kNW, 4) ss_fwd_kernel(const __grid_consta
     float2 da[kTile][2];
 #pragma unroll
     for (int i4 = 0; i4 < 4; ++i4) {
-      const float4 dt4 = sm.dt_s[lane][swz(lane, i4)];
+      const float4 dt4 = sm.dt_s[lane][erow<IT>(lane, i4)];
       const float dts[4] = {dt4.x, dt4.y, dt4.z, dt4.w};
 #pragma unroll
       for (int st = 0; st < 4; ++st)
@@ -280,7 +284,7 @@ __global__ void __launch_bounds__(32 * kNW, 4) ss_fwd_kernel(const __grid_consta
     }
 #pragma unroll
     for (int i4 = 0; i4 < 4; ++i4) {
-      const float4 du4 = sm.dtu_s[lane][swz(lane, i4)];
+      const float4 du4 = sm.dtu_s[lane][erow<IT>(lane, i4)];
       const float dus[4] = {du4.x, du4.y, du4.z, du4.w};
 #pragma unroll
       for (int st = 0; st < 4; ++st) {
@@ -323,7 +327,7 @@ __global__ void __launch_bounds__(32 * kNW, 4) ss_fwd_kernel(const __grid_consta
     if constexpr (kMulti) {
       // state groups: this CTA's share of y (group 0 adds D*u) goes to the fp32 workspace
       float uo[S], ys[S];
-      lds_run<IT, S>(&sm.u[stg][pc][pq * S], uo);
+      lds_elems<IT, S, kBLD>(&sm.u[stg][0][0], pc, pq, uo);
 #pragma unroll
       for (int i = 0; i < S; ++i) {
         const int t = pq * S + i;
@@ -344,8 +348,8 @@ __global__ void __launch_bounds__(32 * kNW, 4) ss_fwd_kernel(const __grid_consta
       }
     } else {
       float yv[S], uo[S], zo[S], yu[S];
-      lds_run<IT, S>(&sm.u[stg][pc][pq * S], uo);
-      if constexpr (kHasZ) lds_run<IT, S>(&sm.z[stg][pc][pq * S], zo);
+      lds_elems<IT, S, kBLD>(&sm.u[stg][0][0], pc, pq, uo);
+      if constexpr (kHasZ) lds_elems<IT, S, kBLD>(&sm.z[stg][0][0], pc, pq, zo);
 #pragma unroll
       for (int i = 0; i < S; ++i) {
         const int t = pq * S + i;
@@ -359,8 +363,8 @@ __global__ void __launch_bounds__(32 * kNW, 4) ss_fwd_kernel(const __grid_consta
         yv[i] = y;
       }
       const int nv = pc_ok ? max(0, min(S, tlen - pq * S)) : 0;
-      store_run<IT, S>(orow + t0 + pq * S, yv, nv, P.vec_out);
-      if (kHasZ && yrow != nullptr) store_run<IT, S>(yrow + t0 + pq * S, yu, nv, P.vec_y);
+      store_elems<IT, S, kBLD>(orow, ostep, t0 + pq * S, yv, nv, P.vec_out);
+      if (kHasZ && yrow != nullptr) store_elems<IT, S, kBLD>(yrow, ystep, t0 + pq * S, yu, nv, P.vec_y);
     }
     // With TMA there is no barrier here: the next tile's recurrence writes the other y_s buffer,
     // and the slot this epilogue read is refilled only after the next tile's first barrier,

@@ -23,6 +23,10 @@ static cudaError_t launch_dyn(K kernel, dim3 grid, int threads, size_t smem, cud
 template <typename IT, int NW, bool VB, bool VC, bool Z, bool M>
 static cudaError_t fwd_go(const FwdK& P, dim3 grid, cudaStream_t st, bool tma) {
   const size_t smem = sizeof(FwdSmem<IT, NW, VB, VC, Z>);
+  if constexpr (!M) {  // (b, L, d) tensors: TMA only, dstate <= 16 (checked on the host)
+    if (P.a.layout == SS_LAYOUT_BLD)
+      return launch_dyn(ss_fwd_kernel<IT, NW, VB, VC, Z, true, false, true>, grid, 32 * NW, smem, st, P);
+  }
   if (tma) return launch_dyn(ss_fwd_kernel<IT, NW, VB, VC, Z, true, M>, grid, 32 * NW, smem, st, P);
   return launch_dyn(ss_fwd_kernel<IT, NW, VB, VC, Z, false, M>, grid, 32 * NW, smem, st, P);
 }
@@ -45,7 +49,9 @@ static cudaError_t fwd_bc(const FwdK& P, dim3 grid, cudaStream_t st, bool tma) {
 template <typename IT, int NW, bool VB>
 static cudaError_t fwd_chunk_go(const FwdK& P, cudaStream_t st) {
   dim3 grid((unsigned)((int64_t)P.a.batch * P.nct * (P.nchunk - 1)));
-  return launch_dyn(ss_fwd_chunk_kernel<IT, NW, VB>, grid, 32 * NW, sizeof(FwdChunkSmem<IT, NW, VB>), st, P);
+  const size_t smem = sizeof(FwdChunkSmem<IT, NW, VB>);
+  if (P.a.layout == SS_LAYOUT_BLD) return launch_dyn(ss_fwd_chunk_kernel<IT, NW, VB, true>, grid, 32 * NW, smem, st, P);
+  return launch_dyn(ss_fwd_chunk_kernel<IT, NW, VB, false>, grid, 32 * NW, smem, st, P);
 }
 template <typename IT, int NW>
 static cudaError_t fwd_chunk_b(const FwdK& P, cudaStream_t st) {
@@ -90,6 +96,10 @@ cudaError_t launch_fwd(const FwdK& P, cudaStream_t st, bool tma) {
 template <typename IT, int NW, bool VB, bool VC, bool Z, bool M>
 static cudaError_t bwd_go(const BwdK& P, dim3 grid, cudaStream_t st, bool tma) {
   const size_t smem = sizeof(BwdSmem<IT, NW, VB, VC, Z>);
+  if constexpr (!M) {  // (b, L, d) tensors: TMA only, dstate <= 16 (checked on the host)
+    if (P.a.f.layout == SS_LAYOUT_BLD)
+      return launch_dyn(ss_bwd_kernel<IT, NW, VB, VC, Z, true, false, true>, grid, 32 * NW, smem, st, P);
+  }
   if (tma) return launch_dyn(ss_bwd_kernel<IT, NW, VB, VC, Z, true, M>, grid, 32 * NW, smem, st, P);
   return launch_dyn(ss_bwd_kernel<IT, NW, VB, VC, Z, false, M>, grid, 32 * NW, smem, st, P);
 }
@@ -110,7 +120,10 @@ static cudaError_t bwd_bc(const BwdK& P, dim3 grid, cudaStream_t st, bool tma) {
 template <typename IT, int NW, bool VC, bool Z>
 static cudaError_t bwd_carry_go(const BwdK& P, cudaStream_t st) {
   dim3 grid((unsigned)((int64_t)P.a.f.batch * P.nct * (P.nchunk - 1)));
-  return launch_dyn(ss_bwd_carry_kernel<IT, NW, VC, Z>, grid, 32 * NW, sizeof(BwdCarrySmem<IT, NW, VC, Z>), st, P);
+  const size_t smem = sizeof(BwdCarrySmem<IT, NW, VC, Z>);
+  if (P.a.f.layout == SS_LAYOUT_BLD)
+    return launch_dyn(ss_bwd_carry_kernel<IT, NW, VC, Z, true>, grid, 32 * NW, smem, st, P);
+  return launch_dyn(ss_bwd_carry_kernel<IT, NW, VC, Z, false>, grid, 32 * NW, smem, st, P);
 }
 template <typename IT, int NW>
 static cudaError_t bwd_carry_cz(const BwdK& P, cudaStream_t st) {

@@ -47,6 +47,36 @@ def _rows(t):
     return t if t.stride(-1) == 1 or t.shape[-1] <= 1 else t.contiguous()
 
 
+# (b, d, L) views of (b, L, d) tensors — x.transpose(1, 2) of the projections around the scan in a
+# Mamba block (modules/mamba_simple.py:96, :104-106, :143-145 of the reference permute them) — run
+# in that layout (SS_LAYOUT_BLD) without a copy when the library's tensor maps can describe them.
+def _is_bld(t):
+    return t is not None and t.dim() == 3 and t.shape[1] > 1 and t.shape[2] > 1 and t.stride(1) == 1 \
+        and t.stride(2) != 1
+
+
+def _bld_aligned(t):
+    es = t.element_size()
+    return t.data_ptr() % 16 == 0 and (t.stride(0) * es) % 16 == 0 and (t.stride(2) * es) % 16 == 0
+
+
+def _in_layout(t, bld):
+    """t as a (b, d, L) view in the call's layout: (b, L, d) storage when bld, else unit seqlen
+    stride; copies only a tensor that is not already in that layout."""
+    if t is None:
+        return None
+    if bld:
+        return t if _is_bld(t) and _bld_aligned(t) else t.transpose(1, 2).contiguous().transpose(1, 2)
+    return _rows(t)
+
+
+def _empty_rows(b, d, l, dtype, device, bld):
+    """A new (b, d, L) tensor in the call's layout."""
+    if bld:
+        return torch.empty((b, l, d), dtype=dtype, device=device).transpose(1, 2)
+    return torch.empty((b, d, l), dtype=dtype, device=device)
+
+
 def _f32(t):
     return None if t is None else t.to(torch.float32).contiguous()
 
@@ -75,21 +105,34 @@ class _Prepared:
     def __init__(self, u, delta, A, B, C, D, z, delta_bias, delta_softplus):
         self.device = _cuda_device(u, delta, A, B, C, D, z, delta_bias)
         self.u_shape = u.shape
-        u = _rows(u)
+        if u.dim() != 3:
+            raise ValueError(f"expected a (batch, dim, seqlen) tensor, got shape {tuple(u.shape)}")
         io = u.dtype
         L.dtype_code(io)
-        self.delta = _rows(delta if delta.dtype == io else delta.to(io))
-        self.z = None if z is None else _rows(z if z.dtype == io else z.to(io))
+        if A.dim() != 2:
+            raise ValueError(f"A must be (dim, dstate), got {tuple(A.shape)}")
+        self.B_shape, self.C_shape = B.shape, C.shape
+        self.B, self.C, self.var_B, self.var_C, self.ngroups, self.bc_code = _bc(B, C, io)
+        # (b, L, d) layout when u comes in it and the library's tensor maps can describe the call:
+        # dstate <= 16; the groups' channels span whole 16-byte units (every 32-channel tile, and
+        # its fp32 checkpoint rows, start on one); variable B / C rows of 16-byte multiples in
+        # the I/O dtype
+        dpg = u.shape[1] // max(self.ngroups, 1)
+        bc_rows_ok = all(not v or (M.dtype == io and (M.shape[-1] * M.element_size()) % 16 == 0)
+                         for M, v in ((self.B, self.var_B), (self.C, self.var_C)))
+        self.bld = (_is_bld(u) and _bld_aligned(u) and A.shape[1] <= 16 and bc_rows_ok
+                    and (self.ngroups == 1 or ((dpg * u.element_size()) % 16 == 0 and dpg % 4 == 0)))
+        u = _in_layout(u, self.bld)
+        self.delta = _in_layout(delta if delta.dtype == io else delta.to(io), self.bld)
+        self.z = None if z is None else _in_layout(z if z.dtype == io else z.to(io), self.bld)
         self.u = u
         b, d, l = u.shape
         if self.delta.shape != u.shape or (self.z is not None and self.z.shape != u.shape):
             raise ValueError("u, delta and z must share the shape (batch, dim, seqlen)")
-        if A.dim() != 2 or A.shape[0] != d:
+        if A.shape[0] != d:
             raise ValueError(f"A must be (dim, dstate), got {tuple(A.shape)}")
         self.A = _f32(A)
         n = A.shape[1]
-        self.B_shape, self.C_shape = B.shape, C.shape
-        self.B, self.C, self.var_B, self.var_C, self.ngroups, self.bc_code = _bc(B, C, io)
         for M, name, var in ((self.B, "B", self.var_B), (self.C, "C", self.var_C)):
             want = (b, self.ngroups, n, l) if var else (d, n)
             if tuple(M.shape) != want:
@@ -107,20 +150,35 @@ class _Prepared:
         n = L.work_elems(self.b, self.d, self.l, self.n)
         return torch.empty(n, dtype=torch.float32, device=self.device) if n else None
 
+    def to_bdl(self):
+        """Fall back to the (b, d, L) layout (copies of the per-element inputs)."""
+        self.bld = False
+        self.u, self.delta, self.z = _rows(self.u), _rows(self.delta), _rows(self.z)
+
+    def rs(self, t):
+        """(batch stride, the C ABI's *_dim_stride field) of a per-element tensor of this call:
+        the dim stride, or the seqlen stride in the (b, L, d) layout."""
+        if t is None:
+            return 0, 0
+        return t.stride(0), (t.stride(2) if self.bld else t.stride(1))
+
+    def empty_rows(self, dtype=None):
+        return _empty_rows(self.b, self.d, self.l, dtype or self.io, self.device, self.bld)
+
     def fwd_args(self, out, ckpt=None, last=None, out_y=None, work=None):
         u, dl, z = self.u, self.delta, self.z
         return L.FwdArgs(
             self.b, self.d, self.l, self.n, self.ngroups, self.var_B, self.var_C, self.softplus,
             L.dtype_code(self.io), self.bc_code,
-            u.data_ptr(), u.stride(0), u.stride(1),
-            dl.data_ptr(), dl.stride(0), dl.stride(1),
+            u.data_ptr(), *self.rs(u),
+            dl.data_ptr(), *self.rs(dl),
             self.A.data_ptr(), self.B.data_ptr(), self.C.data_ptr(), L.ptr(self.D),
-            L.ptr(z), z.stride(0) if z is not None else 0, z.stride(1) if z is not None else 0,
+            L.ptr(z), *self.rs(z),
             L.ptr(self.delta_bias),
-            out.data_ptr(), out.stride(0), out.stride(1),
+            out.data_ptr(), *self.rs(out),
             L.ptr(ckpt), L.ptr(last),
-            L.ptr(out_y), out_y.stride(0) if out_y is not None else 0,
-            out_y.stride(1) if out_y is not None else 0, L.ptr(work))
+            L.ptr(out_y), *self.rs(out_y), L.ptr(work),
+            L.SS_LAYOUT_BLD if self.bld else L.SS_LAYOUT_BDL)
 
 
 def _new_ckpt(p: _Prepared):
@@ -131,14 +189,18 @@ def scan_forward(p: _Prepared, want_ckpt: bool, want_last: bool):
     """Run the native forward.  Returns (out, ckpt | None, last_state | None, y | None):
     with want_ckpt the state buffer the backward needs and, when there is a gate z, the
     ungated output y it needs as well."""
-    out = torch.empty((p.b, p.d, p.l), dtype=p.io, device=p.device)
+    out = p.empty_rows()
     ckpt = _new_ckpt(p) if want_ckpt else None
-    y = torch.empty_like(out) if (want_ckpt and p.z is not None) else None
+    y = p.empty_rows() if (want_ckpt and p.z is not None) else None
     last = torch.empty((p.b, p.d, p.n), dtype=torch.float32, device=p.device) if want_last else None
     work = p.work()
     args = p.fwd_args(out, ckpt, last, y, work)
     with torch.cuda.device(p.device):
-        L.check(L.lib().ss_fwd(args, L.stream_of(p.device)), "ss_fwd")
+        rc = L.lib().ss_fwd(args, L.stream_of(p.device))
+        if rc == L.SS_ERR_UNSUPPORTED and p.bld:  # the (b, L, d) call was refused: run it as (b, d, L)
+            p.to_bdl()
+            return scan_forward(p, want_ckpt, want_last)
+        L.check(rc, "ss_fwd")
         L.maybe_check_status(p.device, "ss_fwd")
     return out, ckpt, last, y
 
@@ -149,13 +211,13 @@ def scan_backward(p: _Prepared, dout, ckpt, y=None):
     when there is a gate) come from scan_forward; without them the forward is recomputed."""
     if ckpt is None or (p.z is not None and y is None):  # not kept: recompute
         _, ckpt, _, y = scan_forward(p, True, False)
-    dout = _rows(dout if dout.dtype == p.io else dout.to(p.io))
+    dout = _in_layout(dout if dout.dtype == p.io else dout.to(p.io), p.bld)
     if dout.shape != p.u.shape:
         raise ValueError("dout must have the shape of u")
     dev = p.device
-    du = torch.empty((p.b, p.d, p.l), dtype=p.io, device=dev)
-    ddelta = torch.empty_like(du)
-    dz = torch.empty_like(du) if p.z is not None else None
+    du = p.empty_rows()
+    ddelta = p.empty_rows()
+    dz = p.empty_rows() if p.z is not None else None
     dA = torch.empty((p.d, p.n), dtype=torch.float32, device=dev)
     dB = torch.empty(p.B.shape, dtype=torch.float32, device=dev)
     dC = torch.empty(p.C.shape, dtype=torch.float32, device=dev)
@@ -165,14 +227,18 @@ def scan_backward(p: _Prepared, dout, ckpt, y=None):
     work = p.work()  # held until the launch below is queued
     args = L.BwdArgs(
         p.fwd_args(placeholder, ckpt, None, None, work),
-        dout.data_ptr(), dout.stride(0), dout.stride(1),
-        du.data_ptr(), du.stride(0), du.stride(1),
-        ddelta.data_ptr(), ddelta.stride(0), ddelta.stride(1),
-        L.ptr(dz), dz.stride(0) if dz is not None else 0, dz.stride(1) if dz is not None else 0,
-        L.ptr(y), y.stride(0) if y is not None else 0, y.stride(1) if y is not None else 0,
+        dout.data_ptr(), *p.rs(dout),
+        du.data_ptr(), *p.rs(du),
+        ddelta.data_ptr(), *p.rs(ddelta),
+        L.ptr(dz), *p.rs(dz),
+        L.ptr(y), *p.rs(y),
         dA.data_ptr(), dB.data_ptr(), dC.data_ptr(), L.ptr(dD), L.ptr(dbias))
     with torch.cuda.device(dev):
-        L.check(L.lib().ss_bwd(args, L.stream_of(dev)), "ss_bwd")
+        rc = L.lib().ss_bwd(args, L.stream_of(dev))
+        if rc == L.SS_ERR_UNSUPPORTED and p.bld:  # the (b, L, d) call was refused: run it as (b, d, L)
+            p.to_bdl()
+            return scan_backward(p, dout, ckpt, None if y is None else _rows(y))
+        L.check(rc, "ss_bwd")
         L.maybe_check_status(dev, "ss_bwd")
     return du, ddelta, dA, dB, dC, dD, dz, dbias
 
