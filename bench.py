@@ -296,13 +296,15 @@ def cpu_sample_rate(n_full_elems, tokens_full, budget_s, seed=0, shape=None):
         zz = h.get("z")
         t = time.perf_counter()
         O.selective_scan_ref(h["u"], h["delta"], h["A"], h["B"], h["C"], h["D"], zz, h["delta_bias"], True,
-                             return_last_state=last, precision="f32")
+                             return_last_state=last, precision="f32", nthreads=threads)
         if bwd:
             O.selective_scan_ref_bwd(h["u"], h["delta"], h["A"], h["B"], h["C"], h["D"], zz, h["delta_bias"], True,
-                                     h["dout"], precision="f32")
+                                     h["dout"], precision="f32", nthreads=threads)
         return time.perf_counter() - t
 
-    threads = O.max_threads()
+    # every host thread this process may use (a launcher such as torchrun sets OMP_NUM_THREADS=1
+    # for its ranks; the baseline runs on rank 0 alone and takes them all)
+    threads = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else (os.cpu_count() or 1)
     # calibrate on a slice that keeps every thread busy, then grow the slice (channels first,
     # then whole batch rows) towards ~budget_s, never past the per-GPU workload
     cal = max(8, 8 * threads)
