@@ -169,6 +169,21 @@ def profile_traffic(workload, kernel):
     return None
 
 
+def count_own_launches(fn):
+    """Kernels of this library (C++ namespace ssb) that one call of fn launches, counted by the
+    torch profiler outside every timed region; None if the profiler is unavailable."""
+    try:
+        from torch.profiler import ProfilerActivity, profile
+
+        torch.cuda.synchronize()
+        with profile(activities=[ProfilerActivity.CUDA]) as prof:
+            fn()
+            torch.cuda.synchronize()
+        return sum(1 for e in prof.events() if e.device_type.name == "CUDA" and "ssb::" in e.name)
+    except Exception:
+        return None
+
+
 def launches_per_step(d, n, backward):
     """This library's kernels per step: the forward scan, the backward scan with it, and a
     finishing pass after each when the states run in groups (dstate > 16)."""
@@ -401,6 +416,8 @@ def _timed_calls(fn, iters, warmup=3, scrub=None):
     import torch
 
     for _ in range(warmup):
+        if scrub is not None:
+            scrub.zero_()  # its kernel loads here, not inside the timed calls
         fn()
     torch.cuda.synchronize()
     gpu_lead()
@@ -982,14 +999,16 @@ def main():
     if backward:
         for k in leaves:
             x[k].requires_grad_(True)
+    K = a.steps
+    flush = flushes_l2(shape)
+    scrub = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev) if flush else None
     for _ in range(a.warmup):
+        if flush:
+            scrub.zero_()  # its kernel loads here, not inside the timed region
         run_step(x)
         clear(x)
     torch.cuda.synchronize()
 
-    K = a.steps
-    flush = flushes_l2(shape)
-    scrub = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev) if flush else None
     ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(K)]
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier()
@@ -1101,6 +1120,10 @@ def main():
         dist.destroy_process_group()
     if rank != 0:
         return 0
+    per_step = count_own_launches(lambda: (run_step(x), clear(x)))
+    launches_src = "torch profiler, one untimed step"
+    if not per_step:
+        per_step, launches_src = launches_per_step(d, n, backward), "model (profiler unavailable)"
 
     fwd_bytes, bwd_bytes = algorithmic_bytes(b, d, L, n, ES[shape["dtype"]], with_z, last)
     if not backward:
@@ -1122,7 +1145,7 @@ def main():
         "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "pipeline": "copy-in, compute and copy-out of consecutive steps on three streams",
                 "ms_per_step": e2e_ms},
-        "gpu_launches": launches_per_step(d, n, backward) * K,
+        "gpu_launches": per_step * K, "gpu_launches_per_step": per_step, "gpu_launches_source": launches_src,
         "clocks": clk.summary(),
     }
     line["compute"] = compute_floor(b, d, L, n, ms_step, line["clocks"].get("sm_mhz"), with_z, backward)
