@@ -171,17 +171,18 @@ def profile_traffic(workload, kernel):
 
 def count_own_launches(fn):
     """Kernels of this library (C++ namespace ssb) that one call of fn launches, counted by the
-    torch profiler outside every timed region; None if the profiler is unavailable."""
+    torch profiler outside every timed region: (count, None), or (None, why) if the profiler failed."""
     try:
+        import torch
         from torch.profiler import ProfilerActivity, profile
 
         torch.cuda.synchronize()
         with profile(activities=[ProfilerActivity.CUDA]) as prof:
             fn()
             torch.cuda.synchronize()
-        return sum(1 for e in prof.events() if e.device_type.name == "CUDA" and "ssb::" in e.name)
-    except Exception:
-        return None
+        return sum(1 for e in prof.events() if e.device_type.name == "CUDA" and "ssb::" in e.name), None
+    except Exception as e:
+        return None, repr(e)[:200]
 
 
 def launches_per_step(d, n, backward):
@@ -383,6 +384,15 @@ def flushes_l2(shape):
     return step_input_bytes(shape) <= L2_BYTES
 
 
+def parallelism(world, shape):
+    if world == 1:
+        return "x1, no collective"
+    if shape["passes"] == "fwd+bwd":
+        return (f"batch-sharded x{world}; per step one NCCL all-reduce of the partial dA / dD / "
+                f"ddelta_bias (mamba_b200.sharding.reduce_param_grads) inside the step")
+    return f"batch-sharded x{world}, forward only: no exchange in the step"
+
+
 def config_dict(world, shape):
     b, d, L = shape["b"], shape["d"], shape["L"]
     mb = step_input_bytes(shape) / 1e6
@@ -391,7 +401,7 @@ def config_dict(world, shape):
           f"inputs larger than L2 ({mb:.0f} MB of per-element inputs per GPU per step)")
     return {"workload": shape["label"],
             "global_batch": shape["global_b"], "per_gpu_batch": b, "d_inner": d, "seq_len": L,
-            "d_state": shape["n"], "parallelism": f"batch-sharded x{world}, no collective in the path",
+            "d_state": shape["n"], "parallelism": parallelism(world, shape),
             "l2": l2}
 
 
@@ -432,6 +442,49 @@ def _timed_calls(fn, iters, warmup=3, scrub=None):
         evs.append((e0, e1))
     torch.cuda.synchronize()
     return statistics.mean(e0.elapsed_time(e1) for e0, e1 in evs)
+
+
+def host_link(dev, pin, dbuf, names, outs_host, s_in, s_out, e2e_ms, step_ms, reps=3):
+    """The host link alone, outside every timed region: one step's input bytes host -> device,
+    its result bytes device -> host, and both at once (the pipelined end-to-end step moves both
+    concurrently), each the best of `reps` CUDA-event timings on the end-to-end loop's streams.
+    floor_ms = max(both at once, the device step): what a perfectly overlapped end-to-end step
+    would take; frac = floor_ms / the measured end-to-end step."""
+    import torch
+
+    dres = [torch.empty(h.shape, dtype=h.dtype, device=dev) for h in outs_host]
+    h2d = sum(pin[k].numel() * pin[k].element_size() for k in names)
+    d2h = sum(h.numel() * h.element_size() for h in outs_host)
+
+    def timed(do_in, do_out):
+        best = None
+        for _ in range(reps):
+            cur = torch.cuda.current_stream(dev)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            torch.cuda.synchronize()
+            e0.record(cur)
+            for st in (s_in, s_out):
+                st.wait_stream(cur)
+            if do_in:
+                with torch.cuda.stream(s_in):
+                    for k in names:
+                        dbuf[k].copy_(pin[k], non_blocking=True)
+            if do_out:
+                with torch.cuda.stream(s_out):
+                    for hb, db in zip(outs_host, dres):
+                        hb.copy_(db, non_blocking=True)
+            for st in (s_in, s_out):
+                cur.wait_stream(st)
+            e1.record(cur)
+            torch.cuda.synchronize()
+            ms = e0.elapsed_time(e1)
+            best = ms if best is None else min(best, ms)
+        return best
+
+    ms_in, ms_out, ms_both = timed(True, False), timed(False, True), timed(True, True)
+    floor = max(ms_both, step_ms)
+    return {"h2d_gbs": h2d / ms_in / 1e6, "d2h_gbs": d2h / ms_out / 1e6, "both_ms": ms_both,
+            "floor_ms": floor, "frac": floor / e2e_ms}
 
 
 def reference_ext_compare(shape, dev, backward, iters=5):
@@ -960,7 +1013,18 @@ def main():
     dev = torch.device("cuda", local)
     if world > 1:
         from datetime import timedelta
-        dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=180))
+        # NCCL prints its version line on stdout when its communicator starts: send it to stderr,
+        # so rank 0's stdout stays one JSON line
+        sys.stdout.flush()
+        saved = os.dup(1)
+        os.dup2(2, 1)
+        try:
+            dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=180))
+            dist.barrier()
+        finally:
+            sys.stdout.flush()
+            os.dup2(saved, 1)
+            os.close(saved)
 
     shape = scan_shape(a.workload, world)
     b, d, L, n = shape["b"], shape["d"], shape["L"], shape["n"]
@@ -979,14 +1043,33 @@ def main():
                                          t["delta_bias"], True, return_last_state=last)
         return r if last else (r, None)
 
-    def run_step(t):
-        """One step; returns (out, last_state | None).  Forward-only workloads run without autograd."""
+    from mamba_b200 import sharding
+
+    shard = sharding.plan(b * world, d, world, rank)
+    exchange = world > 1 and backward
+
+    def reduce_grads(t):
+        """The sharded training step's one exchange: the batch shards' partial dA / dD /
+        ddelta_bias summed over the ranks (one NCCL all-reduce, inside the step)."""
+        sharding.reduce_param_grads({"dA": t["A"].grad, "dD": t["D"].grad if t.get("D") is not None else None,
+                                     "ddelta_bias": t["delta_bias"].grad if t.get("delta_bias") is not None else None},
+                                    shard)
+
+    def scan_step(t):
+        """One step of this rank's shard; returns (out, last_state | None).  Forward-only
+        workloads run without autograd."""
         if backward:
             out, ls = step(t)
             out.backward(t["dout"])
             return out, ls
         with torch.no_grad():
             return step(t)
+
+    def run_step(t):
+        r = scan_step(t)
+        if exchange:
+            reduce_grads(t)
+        return r
 
     def clear(t):
         for k in leaves:
@@ -1006,6 +1089,8 @@ def main():
         if flush:
             scrub.zero_()  # its kernel loads here, not inside the timed region
         run_step(x)
+        one_span = exchange and sharding._adjacent_span(
+            [x[k].grad for k in ("A", "D", "delta_bias") if x.get(k) is not None]) is not None
         clear(x)
     torch.cuda.synchronize()
 
@@ -1024,6 +1109,8 @@ def main():
                 out, _ = step(x)
                 ev[i][1].record()
                 out.backward(x["dout"])
+                if exchange:
+                    reduce_grads(x)
             else:
                 with torch.no_grad():
                     out, _ = step(x)
@@ -1120,10 +1207,11 @@ def main():
         dist.destroy_process_group()
     if rank != 0:
         return 0
-    per_step = count_own_launches(lambda: (run_step(x), clear(x)))
+    link = host_link(dev, pin, bufs[0], names, outs_host, s_in, s_out, e2e_ms, ms_step)
+    per_step, why = count_own_launches(lambda: (scan_step(x), clear(x)))  # the group is gone by now
     launches_src = "torch profiler, one untimed step"
     if not per_step:
-        per_step, launches_src = launches_per_step(d, n, backward), "model (profiler unavailable)"
+        per_step, launches_src = launches_per_step(d, n, backward), f"model (profiler: {why or 'no kernels seen'})"
 
     fwd_bytes, bwd_bytes = algorithmic_bytes(b, d, L, n, ES[shape["dtype"]], with_z, last)
     if not backward:
@@ -1144,7 +1232,10 @@ def main():
                      "traffic": profile_traffic(a.workload, dom)},
         "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "pipeline": "copy-in, compute and copy-out of consecutive steps on three streams",
-                "ms_per_step": e2e_ms},
+                "ms_per_step": e2e_ms, "host_link": link},
+        "exchange": (None if not exchange else
+                     {"collective": "NCCL all_reduce (sum) of dA / dD / ddelta_bias, once per step",
+                      "bytes_per_step": 4 * d * (n + 2), "in_place_over_one_span": one_span}),
         "gpu_launches": per_step * K, "gpu_launches_per_step": per_step, "gpu_launches_source": launches_src,
         "clocks": clk.summary(),
     }

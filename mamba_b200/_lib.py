@@ -232,8 +232,13 @@ def ptr(t):
     return None if t is None else t.data_ptr()
 
 
+# the current stream's handle without building a torch.cuda.Stream object per call
+_raw_stream = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+
+
 def stream_of(device: torch.device) -> int:
-    return torch.cuda.current_stream(device).cuda_stream
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    return _raw_stream(idx) if _raw_stream is not None else torch.cuda.current_stream(device).cuda_stream
 
 
 def device_status(device, reset: bool = True) -> int:

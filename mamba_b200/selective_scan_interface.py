@@ -77,8 +77,13 @@ def _empty_rows(b, d, l, dtype, device, bld):
     return torch.empty((b, d, l), dtype=dtype, device=device)
 
 
+def _as(t, dtype):
+    """t in dtype (None stays None; no call when it already is)."""
+    return t if t is None or t.dtype == dtype else t.to(dtype)
+
+
 def _f32(t):
-    return None if t is None else t.to(torch.float32).contiguous()
+    return None if t is None else _as(t, torch.float32).contiguous()
 
 
 def _bc(B, C, io_dtype):
@@ -144,6 +149,26 @@ class _Prepared:
         self.softplus = int(bool(delta_softplus))
         self.b, self.d, self.l, self.n = b, d, l, n
         self.io = io
+
+    # what restore() needs besides the operand tensors
+    _META = ("b", "d", "l", "n", "ngroups", "var_B", "var_C", "bc_code", "softplus", "io", "bld", "device")
+
+    def operands(self):
+        """The normalised operand tensors, in the order restore() takes them."""
+        return self.u, self.delta, self.A, self.B, self.C, self.D, self.z, self.delta_bias
+
+    def meta(self):
+        return tuple(getattr(self, k) for k in self._META)
+
+    @classmethod
+    def restore(cls, operands, meta):
+        """The call prepared before (by the forward), from its saved operands and meta(): the
+        backward runs on it without validating and normalising the inputs again."""
+        p = cls.__new__(cls)
+        p.u, p.delta, p.A, p.B, p.C, p.D, p.z, p.delta_bias = operands
+        for k, v in zip(cls._META, meta):
+            setattr(p, k, v)
+        return p
 
     def work(self):
         """fp32 scratch of the native call (dstate > 16: the state groups' partial sums), or None."""
@@ -218,11 +243,16 @@ def scan_backward(p: _Prepared, dout, ckpt, y=None):
     du = p.empty_rows()
     ddelta = p.empty_rows()
     dz = p.empty_rows() if p.z is not None else None
-    dA = torch.empty((p.d, p.n), dtype=torch.float32, device=dev)
+    # dA, dD, ddelta_bias: consecutive views of one buffer, so that a data-parallel caller sums
+    # them over its batch shards with one collective (mamba_b200.sharding.reduce_param_grads)
+    dn = p.d * p.n
+    small = torch.empty(dn + p.d * ((p.D is not None) + (p.delta_bias is not None)), dtype=torch.float32,
+                        device=dev)
+    dA = small[:dn].view(p.d, p.n)
+    dD = small[dn:dn + p.d] if p.D is not None else None
+    dbias = small[small.numel() - p.d:] if p.delta_bias is not None else None
     dB = torch.empty(p.B.shape, dtype=torch.float32, device=dev)
     dC = torch.empty(p.C.shape, dtype=torch.float32, device=dev)
-    dD = torch.empty(p.d, dtype=torch.float32, device=dev) if p.D is not None else None
-    dbias = torch.empty(p.d, dtype=torch.float32, device=dev) if p.delta_bias is not None else None
     placeholder = du  # stands in for the unused output row pointer of the embedded forward args
     work = p.work()  # held until the launch below is queued
     args = L.BwdArgs(
@@ -258,12 +288,14 @@ class SelectiveScanFn(torch.autograd.Function):
         p = _Prepared(u, delta, A, B, C, D, z, delta_bias, delta_softplus)
         need_grad = any(ctx.needs_input_grad[:8])
         out, ckpt, last, y = scan_forward(p, need_grad, return_last_state)
-        ctx.delta_softplus = delta_softplus
         ctx.shapes = (B.shape, C.shape)
         ctx.dtypes = (u.dtype, delta.dtype, A.dtype, B.dtype, C.dtype,
                       None if D is None else D.dtype, None if z is None else z.dtype,
                       None if delta_bias is None else delta_bias.dtype)
-        ctx.save_for_backward(u, delta, A, B, C, D, z, delta_bias, ckpt, y)
+        # the operands as the native forward took them (the reference's SelectiveScanFn also
+        # saves its contiguous copies): the backward reuses them as they are
+        ctx.meta = p.meta()
+        ctx.save_for_backward(*p.operands(), ckpt, y)
         if return_last_state:
             ctx.mark_non_differentiable(last)
             return out, last
@@ -271,15 +303,12 @@ class SelectiveScanFn(torch.autograd.Function):
 
     @staticmethod
     def backward(ctx, dout, *unused):
-        u, delta, A, B, C, D, z, delta_bias, ckpt, y = ctx.saved_tensors
-        p = _Prepared(u, delta, A, B, C, D, z, delta_bias, ctx.delta_softplus)
+        *operands, ckpt, y = ctx.saved_tensors
+        p = _Prepared.restore(operands, ctx.meta)
         du, ddelta, dA, dB, dC, dD, dz, dbias = scan_backward(p, dout, ckpt, y)
         tu, tdl, tA, tB, tC, tD, tz, tbias = ctx.dtypes
-        dB = dB.reshape(ctx.shapes[0]).to(tB)
-        dC = dC.reshape(ctx.shapes[1]).to(tC)
-        return (du.to(tu), ddelta.to(tdl), dA.to(tA), dB, dC,
-                None if dD is None else dD.to(tD), None if dz is None else dz.to(tz),
-                None if dbias is None else dbias.to(tbias), None, None)
+        return (_as(du, tu), _as(ddelta, tdl), _as(dA, tA), _as(dB.reshape(ctx.shapes[0]), tB),
+                _as(dC.reshape(ctx.shapes[1]), tC), _as(dD, tD), _as(dz, tz), _as(dbias, tbias), None, None)
 
 
 def selective_scan_fn(u, delta, A, B, C, D=None, z=None, delta_bias=None, delta_softplus=False,

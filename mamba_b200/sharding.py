@@ -90,6 +90,21 @@ def gather_rows(local: torch.Tensor, s: Shard, group=None) -> torch.Tensor:
     return torch.cat(parts, dim=0 if s.axis == "batch" else 1)
 
 
+def _adjacent_span(parts):
+    """One flat tensor over `parts` when they are contiguous, same-dtype views laid end to end in
+    one storage (else None), so a single collective can update them all in place."""
+    if len(parts) < 2 or not all(t.is_contiguous() and t.dtype == parts[0].dtype for t in parts):
+        return None
+    st = parts[0].untyped_storage()
+    off = parts[0].storage_offset()
+    for t in parts:
+        if t.untyped_storage().data_ptr() != st.data_ptr() or t.storage_offset() != off:
+            return None
+        off += t.numel()
+    n = off - parts[0].storage_offset()
+    return torch.empty(0, dtype=parts[0].dtype, device=parts[0].device).set_(st, parts[0].storage_offset(), (n,))
+
+
 def reduce_param_grads(grads: dict, s: Shard, group=None) -> dict:
     """Sum the gradients that are partial on each rank (see module docstring)."""
     if s.axis == "batch":
@@ -98,9 +113,21 @@ def reduce_param_grads(grads: dict, s: Shard, group=None) -> dict:
         keys = ()  # each rank owns whole groups: its dB / dC are complete
     else:
         keys = ("dB", "dC")
-    for k in keys:
-        if grads.get(k) is not None:
-            dist.all_reduce(grads[k], op=dist.ReduceOp.SUM, group=group)
+    parts = [grads[k] for k in keys if grads.get(k) is not None]
+    span = _adjacent_span(parts)
+    if span is not None:  # consecutive views of one buffer (the scan's backward allocates them so)
+        dist.all_reduce(span, op=dist.ReduceOp.SUM, group=group)
+    elif len(parts) > 1 and all(t.dtype == parts[0].dtype for t in parts):
+        # one collective for all of them: they are small (d x N + 2 d values under batch sharding)
+        flat = torch.cat([t.reshape(-1) for t in parts])
+        dist.all_reduce(flat, op=dist.ReduceOp.SUM, group=group)
+        off = 0
+        for t in parts:
+            t.copy_(flat[off:off + t.numel()].view(t.shape))
+            off += t.numel()
+    else:
+        for t in parts:
+            dist.all_reduce(t, op=dist.ReduceOp.SUM, group=group)
     return grads
 
 

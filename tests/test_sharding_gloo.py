@@ -51,6 +51,15 @@ def _worker(rank, world, port, shape, q):
         out = torch.from_numpy(O.selective_scan_ref(*args))
         g = O.selective_scan_ref_bwd(*args, t("dout", "row"))
         grads = {k: (None if v is None else torch.from_numpy(np.ascontiguousarray(v))) for k, v in g.items()}
+        if s.axis == "batch":
+            # laid out as the scan's backward returns them: consecutive views of one buffer, which
+            # reduce_param_grads sums with one collective in place
+            keys = ("dA", "dD", "ddelta_bias")
+            flat = torch.cat([grads[k].reshape(-1) for k in keys])
+            off = 0
+            for k in keys:
+                grads[k], off = flat[off:off + grads[k].numel()].view(grads[k].shape), off + grads[k].numel()
+            assert sharding._adjacent_span([grads[k] for k in keys]) is not None
         grads = sharding.reduce_param_grads(grads, s)
         full_out = sharding.gather_rows(out, s)
         full_du = sharding.gather_rows(grads["du"], s)
@@ -76,6 +85,9 @@ def _worker(rank, world, port, shape, q):
             np.testing.assert_allclose(full_out.numpy(), ref_out, rtol=1e-5, atol=1e-6)
             np.testing.assert_allclose(full_du.numpy(), ref_g["du"], rtol=1e-5, atol=1e-6)
             np.testing.assert_allclose(dA_full.numpy(), ref_g["dA"], rtol=1e-4, atol=1e-5)
+            if s.axis == "batch":
+                np.testing.assert_allclose(grads["dD"].numpy(), ref_g["dD"], rtol=1e-4, atol=1e-5)
+                np.testing.assert_allclose(grads["ddelta_bias"].numpy(), ref_g["ddelta_bias"], rtol=1e-4, atol=1e-5)
             np.testing.assert_allclose(dB_full.numpy(), ref_g["dB"], rtol=1e-4, atol=1e-5)
             q.put((s.axis, "ok"))
     except Exception as e:  # report to the parent instead of hanging it
