@@ -1135,12 +1135,13 @@ def main():
     # ---- end to end: pinned host inputs in, every result out, through the public operator.
     # Steps are independent, so the loop is pipelined over three streams: step i+1's inputs are
     # copied in while step i computes, and step i's results are copied out while step i+1
-    # computes (the host link is full duplex).  Every step still moves all of its bytes both
+    # computes (the host link is full duplex); a sharded step's gradient exchange runs on a fourth.  Every step still moves all of its bytes both
     # ways; inputs alternate between two device buffer sets.
     names = tuple(k for k in ("u", "delta", "z", "B", "C", "dout", "A", "D", "delta_bias") if k in host)
     pin = {k: v.pin_memory() for k, v in host.items()}
     bufs = [{k: torch.empty_like(v, device=dev) for k, v in host.items()} for _ in range(2)]
     s_in, s_cmp, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    s_x = torch.cuda.Stream(dev) if exchange else None
     E = max(1, a.e2e_steps)
     h2d = sum(pin[k].numel() * pin[k].element_size() for k in names)
     outs_host = []
@@ -1167,21 +1168,38 @@ def main():
             with torch.cuda.stream(s_cmp):
                 s_cmp.wait_event(in_done[i])
                 t = {k: bufs[i % 2][k].detach().requires_grad_(backward and k in leaves) for k in names}
-                out, ls = run_step(t)
+                out, ls = scan_step(t)
                 res = [out.detach()] + ([ls] if ls is not None else [])
+                names_out = ["out"] + (["last_state"] if ls is not None else [])
                 if backward:
                     res += [t[k].grad for k in leaves]
+                    names_out += ["d" + k for k in leaves]
                 cmp_done[i] = torch.cuda.Event()
                 cmp_done[i].record(s_cmp)
             if not outs_host:
                 outs_host.extend(torch.empty(r.shape, dtype=r.dtype, pin_memory=True) for r in res)
+            # a sharded step's exchange runs on a stream of its own and only the copy-out of the
+            # gradients it sums (a few hundred KB) waits for it there: the big results leave as soon
+            # as the step is computed, so the ranks' copy / compute pipelines are not put in lockstep
+            summed = [j for j, nm in enumerate(names_out) if exchange and nm in ("dA", "dD", "ddelta_bias")]
+            if summed:
+                with torch.cuda.stream(s_x):
+                    s_x.wait_event(cmp_done[i])
+                    for j in summed:
+                        res[j].record_stream(s_x)
+                    reduce_grads(t)
+                    for j in summed:
+                        outs_host[j].copy_(res[j], non_blocking=True)
             with torch.cuda.stream(s_out):
                 s_out.wait_event(cmp_done[i])
-                for hbuf, r in zip(outs_host, res):
-                    hbuf.copy_(r, non_blocking=True)
-                    r.record_stream(s_out)  # allocated on the compute stream, read here
+                for j, (hbuf, r) in enumerate(zip(outs_host, res)):
+                    if j not in summed:
+                        hbuf.copy_(r, non_blocking=True)
+                        r.record_stream(s_out)  # allocated on the compute stream, read here
             nbytes = sum(r.numel() * r.element_size() for r in res)
         if t_end is not None:
+            if s_x is not None:
+                s_out.wait_stream(s_x)  # the last exchange and its copy-out are inside the region
             t_end.record(s_out)  # s_out's last copy waited on the last compute, which waited on its inputs
         return nbytes
 
@@ -1231,7 +1249,8 @@ def main():
                      "algorithmic_bytes_per_launch": dom_bytes,
                      "traffic": profile_traffic(a.workload, dom)},
         "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                "pipeline": "copy-in, compute and copy-out of consecutive steps on three streams",
+                "pipeline": ("copy-in, compute and copy-out of consecutive steps on three streams"
+                             + (", the gradient exchange on a fourth" if exchange else "")),
                 "ms_per_step": e2e_ms, "host_link": link},
         "exchange": (None if not exchange else
                      {"collective": "NCCL all_reduce (sum) of dA / dD / ddelta_bias, once per step",
