@@ -126,7 +126,14 @@ def algorithmic_bytes(b, d, L, n, es=2, z=True, last=False):
     return fwd, bwd
 
 
-def compute_floor(b, d, L, n, ms_step, sm_mhz, z=True, backward=True):
+# warp instructions per warp-step (one lane per channel, 4 states, one time step) of the whole-row
+# scan kernels with 2-byte I/O, a gate and dstate 16, from ncu's smsp__inst_executed.sum at the
+# north-star point divided by its 3,145,728 warp-steps (profiles/ss_fwd_kernel_north_star.md,
+# profiles/ss_bwd_kernel_north_star.md)
+INST_PER_WARP_STEP = {"fwd": 124772736 / 3145728, "bwd": 263748096 / 3145728}
+
+
+def compute_floor(b, d, L, n, ms_step, sm_mhz, z=True, backward=True, io_bytes=2):
     """The step's MUFU (ex2 / lg2 / rcp) work, counted from the kernels' arithmetic, against the
     B200's 148 SMs x 16 MUFU lanes per clock at the sampled SM clock: the compute floor that
     keeps this path far from its HBM roofline.  Per element: forward 1 ex2 per state + 2
@@ -139,10 +146,19 @@ def compute_floor(b, d, L, n, ms_step, sm_mhz, z=True, backward=True):
     mhz = sm_mhz or 1965.0
     peak = 148 * 16 * mhz * 1e6
     floor_ms = mufu / peak * 1e3
-    return {"mufu_ops_per_step": mufu, "mufu_peak_ops_per_s": peak, "mufu_floor_ms": floor_ms,
-            "mufu_frac": floor_ms / ms_step,
-            "note": "MUFU floor of the step at the sampled SM clock; the scan kernels issue at ~45 % of "
-                    "peak with latency stalls on shared-memory and MUFU results (ncu summaries)"}
+    out = {"mufu_ops_per_step": mufu, "mufu_peak_ops_per_s": peak, "mufu_floor_ms": floor_ms,
+           "mufu_frac": floor_ms / ms_step,
+           "note": "MUFU floor of the step at the sampled SM clock; the scan kernels issue at ~45 % of "
+                   "peak with latency stalls on shared-memory and MUFU results (ncu summaries)"}
+    if z and n == 16 and io_bytes == 2:
+        # issue floor: the kernels' measured instruction counts at one warp instruction per
+        # scheduler per clock (148 SMs x 4 schedulers); the time-chunk summary passes are not
+        # counted, so for a time-chunked step this is a lower bound of the floor
+        warp_steps = b * L * (-(-d // 32)) * (n // 4)
+        inst = warp_steps * (INST_PER_WARP_STEP["fwd"] + (INST_PER_WARP_STEP["bwd"] if backward else 0.0))
+        issue_ms = inst / (148 * 4 * mhz * 1e6) * 1e3
+        out.update({"issue_warp_inst_per_step": inst, "issue_floor_ms": issue_ms, "issue_frac": issue_ms / ms_step})
+    return out
 
 
 def load_peaks():
@@ -1258,7 +1274,8 @@ def main():
         "gpu_launches": per_step * K, "gpu_launches_per_step": per_step, "gpu_launches_source": launches_src,
         "clocks": clk.summary(),
     }
-    line["compute"] = compute_floor(b, d, L, n, ms_step, line["clocks"].get("sm_mhz"), with_z, backward)
+    line["compute"] = compute_floor(b, d, L, n, ms_step, line["clocks"].get("sm_mhz"), with_z, backward,
+                                    ES[shape["dtype"]])
     if verification is not None:
         line["verification"] = verification
     if world == 1 and not a.no_reference_ext:
