@@ -89,7 +89,8 @@ def args_():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="mamba_b200", choices=["mamba_b200", "reference"])
-    ap.add_argument("--e2e-steps", type=int, default=20)
+    ap.add_argument("--e2e-steps", type=int, default=50,
+                    help="pipelined end-to-end steps (the loop's fill and drain are spread over them)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="CPU-baseline sample budget")
     ap.add_argument("--no-reference-ext", action="store_true",
