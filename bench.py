@@ -426,14 +426,34 @@ def config_dict(world, shape):
 REF_SO = os.path.join(HERE, "oracle", "_ref", "selective_scan.so")
 
 
-def gpu_lead(ms=5.0):
+def gpu_lead(ms=50.0):
     """Enqueue ~ms of idle GPU work (a spin kernel) so the host gets ahead of the device before a
     timed region: the CUDA events that bracket each step then measure the device's time for the
-    step, not the host's launch latency (which matters for the sub-millisecond small-batch steps).
-    The lead itself lies before the first event of the region."""
+    step, not the host's launch latency (which matters for the sub-millisecond small-batch steps)
+    nor a host-side hiccup shorter than the lead.  The lead itself lies before the first event of
+    the region."""
     import torch
 
     torch.cuda._sleep(int(ms * 1e-3 * 2.0e9))
+
+
+class quiet_host:
+    """No Python garbage collection inside a timed region (one full collection just before it),
+    as timeit does: a collector pause on the host would otherwise stall the launches."""
+
+    def __enter__(self):
+        import gc
+
+        self.was = gc.isenabled()
+        gc.collect()
+        gc.disable()
+        return self
+
+    def __exit__(self, *exc):
+        import gc
+
+        if self.was:
+            gc.enable()
 
 
 def _timed_calls(fn, iters, warmup=3, scrub=None):
@@ -447,17 +467,18 @@ def _timed_calls(fn, iters, warmup=3, scrub=None):
             scrub.zero_()  # its kernel loads here, not inside the timed calls
         fn()
     torch.cuda.synchronize()
-    gpu_lead()
     evs = []
-    for _ in range(iters):
-        if scrub is not None:
-            scrub.zero_()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record()
-        fn()
-        e1.record()
-        evs.append((e0, e1))
-    torch.cuda.synchronize()
+    with quiet_host():
+        gpu_lead()
+        for _ in range(iters):
+            if scrub is not None:
+                scrub.zero_()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            fn()
+            e1.record()
+            evs.append((e0, e1))
+        torch.cuda.synchronize()
     return statistics.mean(e0.elapsed_time(e1) for e0, e1 in evs)
 
 
@@ -1115,7 +1136,7 @@ def main():
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier()
     torch.cuda.synchronize()
-    with ClockSampler(dev.index) as clk:
+    with ClockSampler(dev.index) as clk, quiet_host():
         gpu_lead()  # outside the region: the host runs ahead of the device through it
         t0.record()
         for i in range(K):
@@ -1225,8 +1246,9 @@ def main():
     barrier()
     torch.cuda.synchronize()
     s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    d2h = e2e_run(E, s0, s1)
-    torch.cuda.synchronize()
+    with quiet_host():
+        d2h = e2e_run(E, s0, s1)
+        torch.cuda.synchronize()
     e2e_ms = s0.elapsed_time(s1) / E
     if world > 1:
         tt = torch.tensor([e2e_ms], device=dev, dtype=torch.float64)
