@@ -361,12 +361,25 @@ int ss_bwd(const ss_bwd_args* args, void* stream) {
     const size_t nA = (size_t)f.dim * f.dstate;
     const size_t nBv = (size_t)f.batch * f.ngroups * f.dstate * (size_t)f.seqlen;
     const size_t nB = f.var_B ? nBv : nA, nC = f.var_C ? nBv : nA;
-    cudaError_t e = cudaMemsetAsync(args->dA, 0, nA * sizeof(float), st);
-    if (e == cudaSuccess && nB) e = cudaMemsetAsync(args->dB, 0, nB * sizeof(float), st);
-    if (e == cudaSuccess && nC) e = cudaMemsetAsync(args->dC, 0, nC * sizeof(float), st);
-    if (e == cudaSuccess && args->dD) e = cudaMemsetAsync(args->dD, 0, (size_t)f.dim * sizeof(float), st);
-    if (e == cudaSuccess && args->ddelta_bias)
-      e = cudaMemsetAsync(args->ddelta_bias, 0, (size_t)f.dim * sizeof(float), st);
+    // the summed gradients, zeroed with one memset per run of buffers that lie end to end (the
+    // Python layer allocates dA / dD / ddelta_bias and dB / dC so): each memset is a launch
+    struct Span { char* p; size_t n; };
+    Span sp[5];
+    int k = 0;
+    auto add = [&](void* ptr, size_t elems) {
+      if (ptr == nullptr || elems == 0) return;
+      char* q = static_cast<char*>(ptr);
+      const size_t n = elems * sizeof(float);
+      if (k > 0 && sp[k - 1].p + sp[k - 1].n == q) sp[k - 1].n += n;
+      else sp[k++] = {q, n};
+    };
+    add(args->dA, nA);
+    add(args->dD, f.dim);
+    add(args->ddelta_bias, f.dim);
+    add(args->dB, nB);
+    add(args->dC, nC);
+    cudaError_t e = cudaSuccess;
+    for (int i = 0; i < k && e == cudaSuccess; ++i) e = cudaMemsetAsync(sp[i].p, 0, sp[i].n, st);
     return e;
   };
   if (f.batch == 0 || f.seqlen == 0) return cuda_status(zero_sums());

@@ -82,6 +82,17 @@ def _as(t, dtype):
     return t if t is None or t.dtype == dtype else t.to(dtype)
 
 
+def _cast_pair(dB, dC, tB, tC):
+    """dB, dC in the B / C leaves' dtypes; one cast kernel when they share their buffer (as
+    scan_backward allocates them) and go to the same dtype."""
+    base = dB._base
+    if tB == tC and dB.dtype != tB and base is not None and dC._base is base:
+        cast = base.to(tB)
+        ob, oc = dB.storage_offset() - base.storage_offset(), dC.storage_offset() - base.storage_offset()
+        return cast[ob:ob + dB.numel()].view(dB.shape), cast[oc:oc + dC.numel()].view(dC.shape)
+    return _as(dB, tB), _as(dC, tC)
+
+
 def _f32(t):
     return None if t is None else _as(t, torch.float32).contiguous()
 
@@ -251,8 +262,12 @@ def scan_backward(p: _Prepared, dout, ckpt, y=None):
     dA = small[:dn].view(p.d, p.n)
     dD = small[dn:dn + p.d] if p.D is not None else None
     dbias = small[small.numel() - p.d:] if p.delta_bias is not None else None
-    dB = torch.empty(p.B.shape, dtype=torch.float32, device=dev)
-    dC = torch.empty(p.C.shape, dtype=torch.float32, device=dev)
+    # dB, dC back to back in one buffer as well: the library zeroes each such run with one memset
+    # (dC starts on a 16-byte boundary, which the kernels' vector reductions need)
+    nb, nc = p.B.numel(), p.C.numel()
+    nb16 = -(-nb // 4) * 4
+    bc = torch.empty(nb16 + nc, dtype=torch.float32, device=dev)
+    dB, dC = bc[:nb].view(p.B.shape), bc[nb16:].view(p.C.shape)
     placeholder = du  # stands in for the unused output row pointer of the embedded forward args
     work = p.work()  # held until the launch below is queued
     args = L.BwdArgs(
@@ -307,8 +322,9 @@ class SelectiveScanFn(torch.autograd.Function):
         p = _Prepared.restore(operands, ctx.meta)
         du, ddelta, dA, dB, dC, dD, dz, dbias = scan_backward(p, dout, ckpt, y)
         tu, tdl, tA, tB, tC, tD, tz, tbias = ctx.dtypes
-        return (_as(du, tu), _as(ddelta, tdl), _as(dA, tA), _as(dB.reshape(ctx.shapes[0]), tB),
-                _as(dC.reshape(ctx.shapes[1]), tC), _as(dD, tD), _as(dz, tz), _as(dbias, tbias), None, None)
+        dB, dC = _cast_pair(dB, dC, tB, tC)
+        return (_as(du, tu), _as(ddelta, tdl), _as(dA, tA), dB.reshape(ctx.shapes[0]),
+                dC.reshape(ctx.shapes[1]), _as(dD, tD), _as(dz, tz), _as(dbias, tbias), None, None)
 
 
 def selective_scan_fn(u, delta, A, B, C, D=None, z=None, delta_bias=None, delta_softplus=False,
