@@ -137,25 +137,6 @@ __global__ void __launch_bounds__(32 * kNW, 3) ss_bwd_kernel(const __grid_consta
     Cc[p] = make_float2(cv[0], cv[1]);
     dA2[p] = e2[p] = dBc[p] = dCc[p] = make_float2(0.f, 0.f);
   }
-  // a time chunk before the last starts from the carry the later chunks send back: chunk j
-  // maps an incoming carry E to exp(A sum_j delta') E + (its local carry), folded over the
-  // chunks after this one, last first
-  if (chunk < P.nchunk - 1 && lane_ok) {
-    for (int j = P.nchunk - 1; j > chunk; --j) {
-      const int64_t bj = (int64_t)b * P.nchunk + j;
-      const float sdt = P.csum[bj * f.dim + c];
-      const float* cc = P.ccarry + (bj * N + kSPW * w) * (int64_t)f.dim + c;
-#pragma unroll
-      for (int p = 0; p < 2; ++p) {
-        const bool ok0 = kSPW * w + 2 * p < N, ok1 = kSPW * w + 2 * p + 1 < N;
-        const float e0 = ok0 ? cc[(int64_t)(2 * p) * f.dim] : 0.f;
-        const float e1 = ok1 ? cc[(int64_t)(2 * p + 1) * f.dim] : 0.f;
-        e2[p].x = fmaf(ex2(A2[p].x * sdt), e2[p].x, e0);
-        e2[p].y = fmaf(ex2(A2[p].y * sdt), e2[p].y, e1);
-      }
-    }
-  }
-
   // ---- element role
   const int pc = elem_pc<kNW, kBLD>(tid), pq = elem_pq<kNW, kBLD>(tid);
   const bool pc_ok = pc < nvalid;
@@ -207,6 +188,28 @@ __global__ void __launch_bounds__(32 * kNW, 3) ss_bwd_kernel(const __grid_consta
     __syncthreads();
     if (tid == 0)
       for (int s = 0; s < kStagesBwd<IT> && s < nt; ++s) issue(s, s);
+  }
+
+  // a time chunk before the last starts from the carry the later chunks send back: chunk j
+  // maps an incoming carry E to exp(A sum_j delta') E + (its local carry), folded over the
+  // chunks after this one, last first.  The carries come from ss_bwd_carry_kernel, which this
+  // launch may overlap (programmatic dependent launch): CTAs that read them wait for it here,
+  // with their first tiles in flight.
+  if (chunk < P.nchunk - 1) griddep_wait();
+  if (chunk < P.nchunk - 1 && lane_ok) {
+    for (int j = P.nchunk - 1; j > chunk; --j) {
+      const int64_t bj = (int64_t)b * P.nchunk + j;
+      const float sdt = P.csum[bj * f.dim + c];
+      const float* cc = P.ccarry + (bj * N + kSPW * w) * (int64_t)f.dim + c;
+#pragma unroll
+      for (int p = 0; p < 2; ++p) {
+        const bool ok0 = kSPW * w + 2 * p < N, ok1 = kSPW * w + 2 * p + 1 < N;
+        const float e0 = ok0 ? cc[(int64_t)(2 * p) * f.dim] : 0.f;
+        const float e1 = ok1 ? cc[(int64_t)(2 * p + 1) * f.dim] : 0.f;
+        e2[p].x = fmaf(ex2(A2[p].x * sdt), e2[p].x, e0);
+        e2[p].y = fmaf(ex2(A2[p].y * sdt), e2[p].y, e1);
+      }
+    }
   }
 
   for (int it = 0; it < nt; ++it) {

@@ -18,6 +18,9 @@
 // backward — so they cost a fraction of a full pass.  The main kernels then fold these
 // summaries over the chunks before (forward) or after (backward) their own into their start
 // state or carry, and run their chunk exactly as the unchunked kernel runs the whole row.
+// The main kernels are launched as programmatic dependents of these passes: they start while a
+// summary pass still runs, and only their CTAs that read summaries wait for it (the first chunk
+// of the forward and the last chunk of the backward need none).
 // This is the reference's per-chunk carry (forward_kernel.cu:274-286: the running prefix of
 // (exp(delta' A), state) pairs across 2048-step chunks inside one CTA) spread over CTAs.
 #pragma once
@@ -206,6 +209,8 @@ __global__ void __launch_bounds__(32 * kNW, 4) ss_fwd_chunk_kernel(const __grid_
     __syncthreads();  // dt_s / dtu_s / B_s are rewritten by the next tile
   }
 
+  // the main pass may start now (its CTAs that read the summaries wait for this grid to end)
+  griddep_launch_dependents();
   const int64_t bj = (int64_t)b * P.nchunk + chunk;
   if (lane_ok) {
     const float hv[kSPW] = {h[0].x, h[0].y, h[1].x, h[1].y};
@@ -366,6 +371,8 @@ __global__ void __launch_bounds__(32 * kNW, 4) ss_bwd_carry_kernel(const __grid_
     __syncthreads();
   }
 
+  // the main pass may start now (its CTAs that read the summaries wait for this grid to end)
+  griddep_launch_dependents();
   const int64_t bj = (int64_t)b * P.nchunk + chunk;
   if (lane_ok) {
     const float ev[kSPW] = {e2[0].x, e2[0].y, e2[1].x, e2[1].y};

@@ -112,6 +112,13 @@ __device__ __forceinline__ void softplus_and_slope(float v, float& sp, float& sl
   slope = lin ? 1.f : e * fast_rcp(1.f + e);
 }
 
+// Programmatic dependent launch: a kernel launched with programmatic stream serialization may
+// start before the kernel ahead of it in the stream has finished.  griddep_wait() blocks until
+// that kernel has completed and its writes are visible (it returns at once when the launch has no
+// such dependency); griddep_launch_dependents() lets the next kernel of the stream start early.
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // packed fp32x2 arithmetic (one instruction for two lanes of work on sm_100)
 __device__ __forceinline__ float2 f2(float a) { return make_float2(a, a); }
 __device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) { return __ffma2_rn(a, b, c); }

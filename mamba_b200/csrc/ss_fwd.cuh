@@ -141,24 +141,6 @@ __global__ void __launch_bounds__(32 * kNW, 4) ss_fwd_kernel(const __grid_consta
     Cc[p] = make_float2(cv[0], cv[1]);
     h[p] = make_float2(0.f, 0.f);
   }
-  // a later time chunk starts from the state the earlier chunks leave behind: chunk j maps a
-  // start state H to exp(A sum_j delta') H + (its local end state), folded over j < chunk
-  if (chunk > 0 && lane_ok) {
-    for (int j = 0; j < chunk; ++j) {
-      const int64_t bj = (int64_t)b * P.nchunk + j;
-      const float sdt = P.csum[bj * a.dim + c];
-      const float* cs = P.cstate + (bj * N + kSPW * w) * (int64_t)a.dim + c;
-#pragma unroll
-      for (int p = 0; p < 2; ++p) {
-        const bool ok0 = kSPW * w + 2 * p < N, ok1 = kSPW * w + 2 * p + 1 < N;
-        const float s0 = ok0 ? cs[(int64_t)(2 * p) * a.dim] : 0.f;
-        const float s1 = ok1 ? cs[(int64_t)(2 * p + 1) * a.dim] : 0.f;
-        h[p].x = fmaf(ex2(A2[p].x * sdt), h[p].x, s0);
-        h[p].y = fmaf(ex2(A2[p].y * sdt), h[p].y, s1);
-      }
-    }
-  }
-
   // ---- element role: channel c0 + pc, steps pq*S .. pq*S + S - 1 of each tile
   const int pc = elem_pc<kNW, kBLD>(tid), pq = elem_pq<kNW, kBLD>(tid);
   const bool pc_ok = pc < nvalid;
@@ -200,6 +182,27 @@ __global__ void __launch_bounds__(32 * kNW, 4) ss_fwd_kernel(const __grid_consta
   const IT* ub = (const IT*)a.u + (int64_t)b * a.u_batch_stride + (int64_t)c0 * a.u_dim_stride;
   const IT* db = (const IT*)a.delta + (int64_t)b * a.delta_batch_stride + (int64_t)c0 * a.delta_dim_stride;
   const IT* zb = kHasZ ? (const IT*)a.z + (int64_t)b * a.z_batch_stride + (int64_t)c0 * a.z_dim_stride : nullptr;
+
+  // a later time chunk starts from the state the earlier chunks leave behind: chunk j maps a
+  // start state H to exp(A sum_j delta') H + (its local end state), folded over j < chunk.  The
+  // summaries come from ss_fwd_chunk_kernel, which this launch may overlap (programmatic
+  // dependent launch): CTAs that read them wait for it here, with their first tiles in flight.
+  if (chunk > 0) griddep_wait();
+  if (chunk > 0 && lane_ok) {
+    for (int j = 0; j < chunk; ++j) {
+      const int64_t bj = (int64_t)b * P.nchunk + j;
+      const float sdt = P.csum[bj * a.dim + c];
+      const float* cs = P.cstate + (bj * N + kSPW * w) * (int64_t)a.dim + c;
+#pragma unroll
+      for (int p = 0; p < 2; ++p) {
+        const bool ok0 = kSPW * w + 2 * p < N, ok1 = kSPW * w + 2 * p + 1 < N;
+        const float s0 = ok0 ? cs[(int64_t)(2 * p) * a.dim] : 0.f;
+        const float s1 = ok1 ? cs[(int64_t)(2 * p + 1) * a.dim] : 0.f;
+        h[p].x = fmaf(ex2(A2[p].x * sdt), h[p].x, s0);
+        h[p].y = fmaf(ex2(A2[p].y * sdt), h[p].y, s1);
+      }
+    }
+  }
 
   for (int it = 0; it < nt; ++it) {
     const int k = kb + it;  // global tile

@@ -11,24 +11,42 @@ namespace ssb {
 
 inline int warps_for(int dstate) { return dstate <= 4 ? 1 : (dstate <= 8 ? 2 : 4); }
 
+// pdl: launch with programmatic stream serialization, so the kernel may start while the one
+// ahead of it in the stream still runs (the kernel itself waits, griddep_wait, where it reads that
+// kernel's results).
 template <typename K, typename Arg>
-static cudaError_t launch_dyn(K kernel, dim3 grid, int threads, size_t smem, cudaStream_t st, const Arg& P) {
+static cudaError_t launch_dyn(K kernel, dim3 grid, int threads, size_t smem, cudaStream_t st, const Arg& P,
+                              bool pdl = false) {
   cudaError_t e = ensure_smem_limit(reinterpret_cast<const void*>(kernel), smem);
   if (e != cudaSuccess) return e;
-  kernel<<<grid, threads, smem, st>>>(P);
-  return cudaGetLastError();
+  if (!pdl) {
+    kernel<<<grid, threads, smem, st>>>(P);
+    return cudaGetLastError();
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3((unsigned)threads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, P);
 }
 
 // ---- forward
 template <typename IT, int NW, bool VB, bool VC, bool Z, bool M>
 static cudaError_t fwd_go(const FwdK& P, dim3 grid, cudaStream_t st, bool tma) {
   const size_t smem = sizeof(FwdSmem<IT, NW, VB, VC, Z>);
+  const bool pdl = P.nchunk > 1;  // follows ss_fwd_chunk_kernel in the stream
   if constexpr (!M) {  // (b, L, d) tensors: TMA only, dstate <= 16 (checked on the host)
     if (P.a.layout == SS_LAYOUT_BLD)
-      return launch_dyn(ss_fwd_kernel<IT, NW, VB, VC, Z, true, false, true>, grid, 32 * NW, smem, st, P);
+      return launch_dyn(ss_fwd_kernel<IT, NW, VB, VC, Z, true, false, true>, grid, 32 * NW, smem, st, P, pdl);
   }
-  if (tma) return launch_dyn(ss_fwd_kernel<IT, NW, VB, VC, Z, true, M>, grid, 32 * NW, smem, st, P);
-  return launch_dyn(ss_fwd_kernel<IT, NW, VB, VC, Z, false, M>, grid, 32 * NW, smem, st, P);
+  if (tma) return launch_dyn(ss_fwd_kernel<IT, NW, VB, VC, Z, true, M>, grid, 32 * NW, smem, st, P, pdl);
+  return launch_dyn(ss_fwd_kernel<IT, NW, VB, VC, Z, false, M>, grid, 32 * NW, smem, st, P, pdl);
 }
 template <typename IT, int NW, bool VB, bool VC, bool M>
 static cudaError_t fwd_z(const FwdK& P, dim3 grid, cudaStream_t st, bool tma) {
@@ -96,12 +114,13 @@ cudaError_t launch_fwd(const FwdK& P, cudaStream_t st, bool tma) {
 template <typename IT, int NW, bool VB, bool VC, bool Z, bool M>
 static cudaError_t bwd_go(const BwdK& P, dim3 grid, cudaStream_t st, bool tma) {
   const size_t smem = sizeof(BwdSmem<IT, NW, VB, VC, Z>);
+  const bool pdl = P.nchunk > 1;  // follows ss_bwd_carry_kernel in the stream
   if constexpr (!M) {  // (b, L, d) tensors: TMA only, dstate <= 16 (checked on the host)
     if (P.a.f.layout == SS_LAYOUT_BLD)
-      return launch_dyn(ss_bwd_kernel<IT, NW, VB, VC, Z, true, false, true>, grid, 32 * NW, smem, st, P);
+      return launch_dyn(ss_bwd_kernel<IT, NW, VB, VC, Z, true, false, true>, grid, 32 * NW, smem, st, P, pdl);
   }
-  if (tma) return launch_dyn(ss_bwd_kernel<IT, NW, VB, VC, Z, true, M>, grid, 32 * NW, smem, st, P);
-  return launch_dyn(ss_bwd_kernel<IT, NW, VB, VC, Z, false, M>, grid, 32 * NW, smem, st, P);
+  if (tma) return launch_dyn(ss_bwd_kernel<IT, NW, VB, VC, Z, true, M>, grid, 32 * NW, smem, st, P, pdl);
+  return launch_dyn(ss_bwd_kernel<IT, NW, VB, VC, Z, false, M>, grid, 32 * NW, smem, st, P, pdl);
 }
 template <typename IT, int NW, bool VB, bool VC, bool M>
 static cudaError_t bwd_z(const BwdK& P, dim3 grid, cudaStream_t st, bool tma) {
