@@ -434,6 +434,7 @@ __global__ void __launch_bounds__(32 * kNW, 3) ss_bwd_kernel(const __grid_consta
 
     // ---- dB / dC of this tile: 4 consecutive steps of one (B|C, n) row per lane
     if constexpr (kFold) {
+      if (P.zero_dep && it == 0) griddep_wait();  // the sums' zeroing has completed
       const int type = lane >> 4, j = (lane >> 2) & 3, tt = 4 * (lane & 3);
       const int n = kSPW * w + j;  // within the group: dst rows start at bc_off (row n0)
       const bool want = (type == 0) ? kVarB : kVarC;
@@ -510,6 +511,7 @@ __global__ void __launch_bounds__(32 * kNW, 3) ss_bwd_kernel(const __grid_consta
   }
 
   // ---- per-channel parameter gradients (summed over batch rows by the atomics)
+  if (P.zero_dep) griddep_wait();  // the sums' zeroing has completed (at once if already waited)
 #pragma unroll
   for (int p = 0; p < 2; ++p) {
     const float dAv[2] = {dA2[p].x, dA2[p].y}, dBv[2] = {dBc[p].x, dBc[p].y}, dCv[2] = {dCc[p].x, dCc[p].y};

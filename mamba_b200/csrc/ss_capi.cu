@@ -129,6 +129,33 @@ bool map_bc(CUtensorMap* m, const void* p, const ss_fwd_args& a) {
 
 int cuda_status(cudaError_t e) { return ssb::record_cuda_status(e); }
 
+// Zeroes up to 5 fp32 spans (the backward's summed gradients) before the backward runs.  It
+// releases its programmatic dependents at once: the backward launched after it may start its
+// first tile while these stores run, and waits for this grid (griddep_wait) before it adds.
+struct ZeroSpans {
+  float* p[5];
+  long long n[5];
+  int k;
+};
+
+__global__ void __launch_bounds__(256) zero_spans_kernel(const __grid_constant__ ZeroSpans z) {
+  ssb::griddep_launch_dependents();
+  const long long stride = (long long)gridDim.x * blockDim.x;
+  for (int s = 0; s < z.k; ++s) {
+    float* p = z.p[s];
+    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < z.n[s]; i += stride) p[i] = 0.f;
+  }
+}
+
+cudaError_t launch_zero_spans(const ZeroSpans& z, cudaStream_t st) {
+  long long total = 0;
+  for (int s = 0; s < z.k; ++s) total += z.n[s];
+  if (total == 0) return cudaSuccess;
+  const long long blocks = std::min<long long>((total + 255) / 256, 2 * 148);
+  zero_spans_kernel<<<(unsigned)blocks, 256, 0, st>>>(z);
+  return cudaGetLastError();
+}
+
 size_t esize(int dt) { return dt == SS_F32 ? 4 : 2; }
 bool dtype_ok(int dt) { return dt == SS_F32 || dt == SS_BF16 || dt == SS_F16; }
 
@@ -357,29 +384,27 @@ int ss_bwd(const ss_bwd_args* args, void* stream) {
   const ss_fwd_args& f = args->f;
   cudaStream_t st = (cudaStream_t)stream;
   // accumulated outputs start from zero (zeroed once the call is known to run)
-  auto zero_sums = [&]() {
+  // the summed gradients, as runs of buffers that lie end to end (the Python layer allocates
+  // dA / dD / ddelta_bias and dB / dC so): one memset, or one span of the zeroing kernel, per run
+  ZeroSpans zs{};
+  {
     const size_t nA = (size_t)f.dim * f.dstate;
     const size_t nBv = (size_t)f.batch * f.ngroups * f.dstate * (size_t)f.seqlen;
     const size_t nB = f.var_B ? nBv : nA, nC = f.var_C ? nBv : nA;
-    // the summed gradients, zeroed with one memset per run of buffers that lie end to end (the
-    // Python layer allocates dA / dD / ddelta_bias and dB / dC so): each memset is a launch
-    struct Span { char* p; size_t n; };
-    Span sp[5];
-    int k = 0;
-    auto add = [&](void* ptr, size_t elems) {
+    auto add = [&](float* ptr, size_t elems) {
       if (ptr == nullptr || elems == 0) return;
-      char* q = static_cast<char*>(ptr);
-      const size_t n = elems * sizeof(float);
-      if (k > 0 && sp[k - 1].p + sp[k - 1].n == q) sp[k - 1].n += n;
-      else sp[k++] = {q, n};
+      if (zs.k > 0 && zs.p[zs.k - 1] + zs.n[zs.k - 1] == ptr) zs.n[zs.k - 1] += (long long)elems;
+      else { zs.p[zs.k] = ptr; zs.n[zs.k] = (long long)elems; ++zs.k; }
     };
     add(args->dA, nA);
     add(args->dD, f.dim);
     add(args->ddelta_bias, f.dim);
     add(args->dB, nB);
     add(args->dC, nC);
+  }
+  auto zero_sums = [&]() {
     cudaError_t e = cudaSuccess;
-    for (int i = 0; i < k && e == cudaSuccess; ++i) e = cudaMemsetAsync(sp[i].p, 0, sp[i].n, st);
+    for (int i = 0; i < zs.k && e == cudaSuccess; ++i) e = cudaMemsetAsync(zs.p[i], 0, zs.n[i] * sizeof(float), st);
     return e;
   };
   if (f.batch == 0 || f.seqlen == 0) return cuda_status(zero_sums());
@@ -422,7 +447,16 @@ int ss_bwd(const ss_bwd_args* args, void* stream) {
     P.ccarry = f.work;
     P.csum = f.work + (size_t)f.batch * P.nchunk * f.dstate * (size_t)f.dim;
   }
-  cudaError_t e = zero_sums();
+  cudaError_t e;
+  if (P.nsg > 1) {
+    e = zero_sums();
+  } else {
+    // our zeroing kernel lets the backward start before it ends (programmatic dependent launch);
+    // whole-row launches wait for it before their first atomic add, time-chunked ones need not
+    // (the carry pass between them starts only after it has completed)
+    e = launch_zero_spans(zs, st);
+    P.zero_dep = (P.nchunk == 1 && zs.k > 0) ? 1 : 0;  // (dA is never empty: the kernel ran)
+  }
   if (e != cudaSuccess) return cuda_status(e);
   return dispatch(f.io_dtype, [&](auto tag) { return ssb::launch_bwd<decltype(tag)>(P, st, tma); });
 }

@@ -390,6 +390,11 @@ struct BwdK {
   int nchunk, chunk_tiles;
   float* ccarry;
   float* csum;
+  // 1: launched as a programmatic dependent of the kernel that zeroes dA / dB / dC / dD /
+  // ddelta_bias (whole rows, no state groups), so the kernel waits for it before its first
+  // atomic add; the time-chunked launch follows the carry pass, which starts only after that
+  // zeroing has completed
+  int zero_dep;
 };
 
 constexpr int kGroupStates = 16;  // states per CTA when dstate > 16 (4 warps x 4)

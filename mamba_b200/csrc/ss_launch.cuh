@@ -114,7 +114,8 @@ cudaError_t launch_fwd(const FwdK& P, cudaStream_t st, bool tma) {
 template <typename IT, int NW, bool VB, bool VC, bool Z, bool M>
 static cudaError_t bwd_go(const BwdK& P, dim3 grid, cudaStream_t st, bool tma) {
   const size_t smem = sizeof(BwdSmem<IT, NW, VB, VC, Z>);
-  const bool pdl = P.nchunk > 1;  // follows ss_bwd_carry_kernel in the stream
+  // follows ss_bwd_carry_kernel, or the zeroing kernel (zero_dep), in the stream
+  const bool pdl = P.nchunk > 1 || P.zero_dep != 0;
   if constexpr (!M) {  // (b, L, d) tensors: TMA only, dstate <= 16 (checked on the host)
     if (P.a.f.layout == SS_LAYOUT_BLD)
       return launch_dyn(ss_bwd_kernel<IT, NW, VB, VC, Z, true, false, true>, grid, 32 * NW, smem, st, P, pdl);
