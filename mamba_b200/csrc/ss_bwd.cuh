@@ -194,8 +194,9 @@ __global__ void __launch_bounds__(32 * kNW, 3) ss_bwd_kernel(const __grid_consta
   // maps an incoming carry E to exp(A sum_j delta') E + (its local carry), folded over the
   // chunks after this one, last first.  The carries come from ss_bwd_carry_kernel, which this
   // launch may overlap (programmatic dependent launch): CTAs that read them wait for it here,
-  // with their first tiles in flight.
-  if (chunk < P.nchunk - 1) griddep_wait();
+  // with their first tiles in flight.  A whole-row launch (zero_dep) waits here for the kernel
+  // that zeroes the summed gradients before any of its atomic adds.
+  if (chunk < P.nchunk - 1 || P.zero_dep) griddep_wait();
   if (chunk < P.nchunk - 1 && lane_ok) {
     for (int j = P.nchunk - 1; j > chunk; --j) {
       const int64_t bj = (int64_t)b * P.nchunk + j;
@@ -434,7 +435,6 @@ __global__ void __launch_bounds__(32 * kNW, 3) ss_bwd_kernel(const __grid_consta
 
     // ---- dB / dC of this tile: 4 consecutive steps of one (B|C, n) row per lane
     if constexpr (kFold) {
-      if (P.zero_dep && it == 0) griddep_wait();  // the sums' zeroing has completed
       const int type = lane >> 4, j = (lane >> 2) & 3, tt = 4 * (lane & 3);
       const int n = kSPW * w + j;  // within the group: dst rows start at bc_off (row n0)
       const bool want = (type == 0) ? kVarB : kVarC;
@@ -511,7 +511,6 @@ __global__ void __launch_bounds__(32 * kNW, 3) ss_bwd_kernel(const __grid_consta
   }
 
   // ---- per-channel parameter gradients (summed over batch rows by the atomics)
-  if (P.zero_dep) griddep_wait();  // the sums' zeroing has completed (at once if already waited)
 #pragma unroll
   for (int p = 0; p < 2; ++p) {
     const float dAv[2] = {dA2[p].x, dA2[p].y}, dBv[2] = {dBc[p].x, dBc[p].y}, dCv[2] = {dCc[p].x, dCc[p].y};

@@ -130,8 +130,9 @@ bool map_bc(CUtensorMap* m, const void* p, const ss_fwd_args& a) {
 int cuda_status(cudaError_t e) { return ssb::record_cuda_status(e); }
 
 // Zeroes up to 5 fp32 spans (the backward's summed gradients) before the backward runs.  It
-// releases its programmatic dependents at once: the backward launched after it may start its
-// first tile while these stores run, and waits for this grid (griddep_wait) before it adds.
+// releases its programmatic dependents at once: the backward launched after it starts (setup,
+// first tile copies) while these stores run, and waits for this grid (griddep_wait) before its
+// tile loop.
 struct ZeroSpans {
   float* p[5];
   long long n[5];
@@ -452,8 +453,8 @@ int ss_bwd(const ss_bwd_args* args, void* stream) {
     e = zero_sums();
   } else {
     // our zeroing kernel lets the backward start before it ends (programmatic dependent launch);
-    // whole-row launches wait for it before their first atomic add, time-chunked ones need not
-    // (the carry pass between them starts only after it has completed)
+    // whole-row launches wait for it before their tile loop, time-chunked ones need not (the
+    // carry pass between them starts only after it has completed)
     e = launch_zero_spans(zs, st);
     P.zero_dep = (P.nchunk == 1 && zs.k > 0) ? 1 : 0;  // (dA is never empty: the kernel ran)
   }

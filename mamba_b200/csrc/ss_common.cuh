@@ -391,9 +391,9 @@ struct BwdK {
   float* ccarry;
   float* csum;
   // 1: launched as a programmatic dependent of the kernel that zeroes dA / dB / dC / dD /
-  // ddelta_bias (whole rows, no state groups), so the kernel waits for it before its first
-  // atomic add; the time-chunked launch follows the carry pass, which starts only after that
-  // zeroing has completed
+  // ddelta_bias (whole rows, no state groups), so the kernel waits for it before its tile loop
+  // (its setup and first copies overlap that kernel); the time-chunked launch follows the carry
+  // pass, which starts only after that zeroing has completed
   int zero_dep;
 };
 
