@@ -131,7 +131,7 @@ def algorithmic_bytes(b, d, L, n, es=2, z=True, last=False):
 # scan kernels with 2-byte I/O, a gate and dstate 16, from ncu's smsp__inst_executed.sum at the
 # north-star point divided by its 3,145,728 warp-steps (profiles/ss_fwd_kernel_north_star.md,
 # profiles/ss_bwd_kernel_north_star.md)
-INST_PER_WARP_STEP = {"fwd": 124772736 / 3145728, "bwd": 263748096 / 3145728}
+INST_PER_WARP_STEP = {"fwd": 124773888 / 3145728, "bwd": 267692544 / 3145728}
 
 
 def compute_floor(b, d, L, n, ms_step, sm_mhz, z=True, backward=True, io_bytes=2):

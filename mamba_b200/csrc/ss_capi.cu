@@ -24,6 +24,36 @@ template <typename IT> cudaError_t launch_bwd(const BwdK&, cudaStream_t, bool);
 template <typename IT> cudaError_t launch_step(const ss_step_args&, cudaStream_t);
 }  // namespace ssb
 
+namespace ssb {
+// Zeroes up to 5 fp32 spans (the backward's summed gradients) before the backward runs.  It
+// releases its programmatic dependents at once: the backward launched after it starts (setup,
+// first tile copies) while these stores run, and waits for this grid (griddep_wait) before its
+// tile loop.
+struct ZeroSpans {
+  float* p[5];
+  long long n[5];
+  int k;
+};
+
+__global__ void __launch_bounds__(256) zero_spans_kernel(const __grid_constant__ ZeroSpans z) {
+  griddep_launch_dependents();
+  const long long stride = (long long)gridDim.x * blockDim.x;
+  for (int s = 0; s < z.k; ++s) {
+    float* p = z.p[s];
+    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < z.n[s]; i += stride) p[i] = 0.f;
+  }
+}
+
+cudaError_t launch_zero_spans(const ZeroSpans& z, cudaStream_t st) {
+  long long total = 0;
+  for (int s = 0; s < z.k; ++s) total += z.n[s];
+  if (total == 0) return cudaSuccess;
+  const long long blocks = std::min<long long>((total + 255) / 256, 2 * 148);
+  zero_spans_kernel<<<(unsigned)blocks, 256, 0, st>>>(z);
+  return cudaGetLastError();
+}
+}  // namespace ssb
+
 // One status word per device that loads the library: kernels OR kStatus* bits into it when
 // a bounded wait gives up (see ss_device_status).
 __device__ int g_ss_status;
@@ -129,33 +159,6 @@ bool map_bc(CUtensorMap* m, const void* p, const ss_fwd_args& a) {
 
 int cuda_status(cudaError_t e) { return ssb::record_cuda_status(e); }
 
-// Zeroes up to 5 fp32 spans (the backward's summed gradients) before the backward runs.  It
-// releases its programmatic dependents at once: the backward launched after it starts (setup,
-// first tile copies) while these stores run, and waits for this grid (griddep_wait) before its
-// tile loop.
-struct ZeroSpans {
-  float* p[5];
-  long long n[5];
-  int k;
-};
-
-__global__ void __launch_bounds__(256) zero_spans_kernel(const __grid_constant__ ZeroSpans z) {
-  ssb::griddep_launch_dependents();
-  const long long stride = (long long)gridDim.x * blockDim.x;
-  for (int s = 0; s < z.k; ++s) {
-    float* p = z.p[s];
-    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < z.n[s]; i += stride) p[i] = 0.f;
-  }
-}
-
-cudaError_t launch_zero_spans(const ZeroSpans& z, cudaStream_t st) {
-  long long total = 0;
-  for (int s = 0; s < z.k; ++s) total += z.n[s];
-  if (total == 0) return cudaSuccess;
-  const long long blocks = std::min<long long>((total + 255) / 256, 2 * 148);
-  zero_spans_kernel<<<(unsigned)blocks, 256, 0, st>>>(z);
-  return cudaGetLastError();
-}
 
 size_t esize(int dt) { return dt == SS_F32 ? 4 : 2; }
 bool dtype_ok(int dt) { return dt == SS_F32 || dt == SS_BF16 || dt == SS_F16; }
@@ -387,7 +390,7 @@ int ss_bwd(const ss_bwd_args* args, void* stream) {
   // accumulated outputs start from zero (zeroed once the call is known to run)
   // the summed gradients, as runs of buffers that lie end to end (the Python layer allocates
   // dA / dD / ddelta_bias and dB / dC so): one memset, or one span of the zeroing kernel, per run
-  ZeroSpans zs{};
+  ssb::ZeroSpans zs{};
   {
     const size_t nA = (size_t)f.dim * f.dstate;
     const size_t nBv = (size_t)f.batch * f.ngroups * f.dstate * (size_t)f.seqlen;
@@ -455,7 +458,7 @@ int ss_bwd(const ss_bwd_args* args, void* stream) {
     // our zeroing kernel lets the backward start before it ends (programmatic dependent launch);
     // whole-row launches wait for it before their tile loop, time-chunked ones need not (the
     // carry pass between them starts only after it has completed)
-    e = launch_zero_spans(zs, st);
+    e = ssb::launch_zero_spans(zs, st);
     P.zero_dep = (P.nchunk == 1 && zs.k > 0) ? 1 : 0;  // (dA is never empty: the kernel ran)
   }
   if (e != cudaSuccess) return cuda_status(e);

@@ -43,8 +43,8 @@ def test_cpu_baseline_sampler_reports_a_rate():
 def test_compute_floor_is_a_fraction_of_the_step():
     f = bench.compute_floor(8, 1536, 2048, 16, ms_step=0.87, sm_mhz=1965.0)
     assert 0.2 < f["mufu_frac"] < 0.6 and f["mufu_floor_ms"] > 0
-    # the issue floor from the ncu instruction counts: 388.5M warp instructions per north-star step
-    assert abs(f["issue_warp_inst_per_step"] - (124772736 + 263748096)) < 1
+    # the issue floor from the ncu instruction counts: 392.5M warp instructions per north-star step
+    assert abs(f["issue_warp_inst_per_step"] - (124773888 + 267692544)) < 1
     assert 0.0 < f["issue_frac"] < 1.0
     assert "issue_floor_ms" not in bench.compute_floor(2, 1536, 2048, 16, 0.1, 1965.0, False, False, 4)
 
