@@ -212,10 +212,11 @@ def launches_per_step(d, n, backward):
 # ----------------------------------------------------------------------------- clocks
 class ClockSampler:
     """SM clock and clock-event reasons of this process's GPU, polled through NVML from a
-    thread every ~2 ms while the timed region runs, with one sample at each end, so even a
-    short region is covered.  The GPU is found by UUID (then PCI bus id), never by index,
-    because CUDA_VISIBLE_DEVICES may renumber devices."""
-    PERIOD_S = 0.002
+    thread every ~10 ms while the timed region runs, with one sample at each end, so even a
+    short region is covered (every rank polls its own GPU: a faster poll adds driver queries
+    that contend with the ranks' launches on a shared host).  The GPU is found by UUID (then PCI
+    bus id), never by index, because CUDA_VISIBLE_DEVICES may renumber devices."""
+    PERIOD_S = 0.010
 
     def __init__(self, device_index):
         self.dev = device_index
@@ -284,7 +285,7 @@ class ClockSampler:
                 "sw_power_cap": N.nvmlClocksEventReasonSwPowerCap}
         reasons = sorted({k for _, r in self.rows for k, bit in bits.items() if r & bit})
         return {"sm_mhz": statistics.median(r[0] for r in self.rows), "sm_max_mhz": self.max_mhz,
-                "reasons": reasons, "samples": len(self.rows), "source": "NVML, 2 ms poll"}
+                "reasons": reasons, "samples": len(self.rows), "source": "NVML, 10 ms poll"}
 
 
 # ----------------------------------------------------------------------------- inputs
@@ -1245,11 +1246,17 @@ def main():
     torch.cuda.synchronize()
     barrier()
     torch.cuda.synchronize()
-    s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with quiet_host():
-        d2h = e2e_run(E, s0, s1)
-        torch.cuda.synchronize()
-    e2e_ms = s0.elapsed_time(s1) / E
+    # three timed runs of E steps each; the median run per rank (the host side of a shared
+    # machine adds stalls now and then), then the max over ranks
+    runs = []
+    for _ in range(3):
+        s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        barrier()
+        with quiet_host():
+            d2h = e2e_run(E, s0, s1)
+            torch.cuda.synchronize()
+        runs.append(s0.elapsed_time(s1) / E)
+    e2e_ms = statistics.median(runs)
     if world > 1:
         tt = torch.tensor([e2e_ms], device=dev, dtype=torch.float64)
         dist.all_reduce(tt, op=dist.ReduceOp.MAX)
@@ -1290,7 +1297,7 @@ def main():
         "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "pipeline": ("copy-in, compute and copy-out of consecutive steps on three streams"
                              + (", the gradient exchange on a fourth" if exchange else "")),
-                "ms_per_step": e2e_ms, "host_link": link},
+                "ms_per_step": e2e_ms, "runs_ms_per_step": runs, "steps_per_run": E, "host_link": link},
         "exchange": (None if not exchange else
                      {"collective": "NCCL all_reduce (sum) of dA / dD / ddelta_bias, once per step",
                       "bytes_per_step": 4 * d * (n + 2), "in_place_over_one_span": one_span}),
