@@ -265,10 +265,16 @@ SS_API size_t ss_ckpt_elems(int batch, int dim, int seqlen, int dstate);
  * scans each row in one piece.  Size it after any ss_set_time_chunks call. */
 SS_API size_t ss_work_elems(int batch, int dim, int seqlen, int dstate);
 
-/* Forward scan: out = (D*u + sum_n C*h) [* silu(z)], h_t = exp(delta'*A) h_{t-1} + delta'*u*B. */
+/* Forward scan: out = (D*u + sum_n C*h) [* silu(z)], h_t = exp(delta'*A) h_{t-1} + delta'*u*B.
+ * With time chunks (see ss_work_elems) it runs a summary pass over the chunks, then the main pass
+ * as a programmatic dependent of it; the backward does the same with its carry pass. */
 SS_API int ss_fwd(const ss_fwd_args* args, void* stream);
 
-/* Backward scan: all input gradients from dout, using the forward's ckpt. */
+/* Backward scan: all input gradients from dout, using the forward's ckpt.  On `stream` it runs a
+ * kernel that zeroes dA / dB / dC / dD / ddelta_bias (one span per run of buffers that lie end to
+ * end, so callers may allocate them adjacently to save launches), then the backward, launched as
+ * a programmatic dependent that may start before the zeroing ends and waits for it before
+ * accumulating (dstate > 16: memsets and an ordinary launch). */
 SS_API int ss_bwd(const ss_bwd_args* args, void* stream);
 
 /* Backward scan for callers that cannot allocate device memory (an FFI host without a
