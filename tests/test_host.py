@@ -6,7 +6,7 @@ import pytest
 import torch
 
 from mamba_b200 import selective_scan_ext, selective_scan_fn, selective_state_update, sharding
-from mamba_b200.selective_scan_interface import _bc
+from mamba_b200.selective_scan_interface import _bc, _cast_pair, _Prepared
 
 
 def test_cpu_tensors_fail_loudly():
@@ -74,3 +74,33 @@ def test_plan_rejects_bad_ranks():
         sharding.plan(8, 64, 4, 4)
     with pytest.raises(ValueError):
         sharding.plan(3, 96, 2, 0, ngroups=3)
+
+
+def test_cast_pair_casts_a_shared_buffer_once():
+    """dB / dC as the backward allocates them (two views of one fp32 buffer, dC 16-byte aligned)
+    come back in the leaves' dtype with their values and shapes; one cast of the shared buffer
+    when the dtypes agree, separate casts otherwise, none when they are already right."""
+    buf = torch.randn(8 + 12)
+    dB, dC = buf[:6].view(2, 3), buf[8:].view(3, 4)
+    b, c = _cast_pair(dB, dC, torch.bfloat16, torch.bfloat16)
+    assert b.dtype == c.dtype == torch.bfloat16 and b.shape == dB.shape and c.shape == dC.shape
+    assert torch.equal(b, dB.to(torch.bfloat16)) and torch.equal(c, dC.to(torch.bfloat16))
+    assert b.untyped_storage().data_ptr() == c.untyped_storage().data_ptr()  # one cast
+    b, c = _cast_pair(dB, dC, torch.bfloat16, torch.float16)
+    assert (b.dtype, c.dtype) == (torch.bfloat16, torch.float16)
+    assert torch.equal(b, dB.to(torch.bfloat16)) and torch.equal(c, dC.to(torch.float16))
+    b, c = _cast_pair(dB, dC, torch.float32, torch.float32)
+    assert b is dB and c is dC
+
+
+def test_prepared_restore_round_trip():
+    """The backward rebuilds the forward's prepared call from its saved operands and meta()
+    without validating them again: every field the native calls read comes back."""
+    p = _Prepared.__new__(_Prepared)
+    ops = tuple(torch.zeros(1) for _ in range(8))
+    for k, v in zip(_Prepared._META, (2, 64, 100, 16, 1, 1, 1, 3, 1, torch.bfloat16, True, torch.device("cpu"))):
+        setattr(p, k, v)
+    p.u, p.delta, p.A, p.B, p.C, p.D, p.z, p.delta_bias = ops
+    q = _Prepared.restore(p.operands(), p.meta())
+    assert all(a is b for a, b in zip(q.operands(), ops))
+    assert q.meta() == p.meta()
