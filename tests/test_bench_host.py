@@ -100,3 +100,22 @@ def test_cpu_baseline_sampler_forward_only():
     elems, tokens = s["b"] * s["d"] * s["L"], s["b"] * s["L"]
     value, threads, sample, seconds = bench.cpu_sample_rate(elems, tokens, 0.3, shape=s)
     assert value > 0 and "(fwd," in sample
+
+
+def test_parallelism_names_the_exchange():
+    """N > 1 fwd+bwd steps carry one all-reduce of the partial parameter gradients; forward-only
+    steps and single GPUs have no exchange."""
+    ns, c2 = bench.scan_shape("scan", 2), bench.scan_shape("scan-c2", 2)
+    assert "all-reduce" in bench.parallelism(2, ns) and "inside the step" in bench.parallelism(2, ns)
+    assert "no exchange" in bench.parallelism(2, c2)
+    assert bench.parallelism(1, ns) == "x1, no collective"
+
+
+def test_launch_counter_reports_why_it_could_not_count():
+    """Without a GPU the torch profiler cannot count kernels: the counter says so instead of
+    claiming a number (the bench then falls back to its launch model and names the reason)."""
+    n, why = bench.count_own_launches(lambda: None)
+    if n is None:
+        assert isinstance(why, str) and why
+    else:  # a machine with a GPU: nothing of this library launched
+        assert n == 0 and why is None
